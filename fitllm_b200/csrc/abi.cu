@@ -1,0 +1,491 @@
+// extern "C" entry points of libfitq (declared in include/fitq.h): argument
+// checks, workspace carving and kernel sequencing.  No entry point allocates
+// device memory; scratch comes from the caller's workspace.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+// Device status word shared by all kernels of the library (first error wins).
+__device__ int g_fitq_status = 0;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+constexpr int kMaxDevices = 64;
+
+// Number of SMs of the current device; 0 with an error if it is not sm_100.
+int current_sms(int* code) {
+  static int cache[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    *code = fail(FITQ_ERR_NO_DEVICE, "no CUDA device available");
+    return 0;
+  }
+  if (cache[dev] == 0) {
+    int major = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (major != 10) {
+      *code = fail(FITQ_ERR_NO_DEVICE, "device %d is sm_%d0, libfitq is built for sm_100a", dev,
+                   major);
+      return 0;
+    }
+    cache[dev] = sms;
+  }
+  *code = FITQ_OK;
+  return cache[dev];
+}
+
+// Device address of g_fitq_status on the current device (looked up once per device).
+int* status_ptr() {
+  static int* cache[kMaxDevices] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fitq_status) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_weight(const fitq_nf4_weight* w, fitq::Nf4Args* a) {
+  if (!w) return fail(FITQ_ERR_ARG, "weight descriptor is NULL");
+  if (!w->packed || !w->quant_map)
+    return fail(FITQ_ERR_ARG, "weight: packed and quant_map are required");
+  const bool nested = w->absmax_code && w->nested_absmax && w->nested_quant_map;
+  if (!nested && !w->absmax_f32)
+    return fail(FITQ_ERR_ARG,
+                "weight: need absmax_code+nested_absmax+nested_quant_map or absmax_f32");
+  if (w->n_out <= 0 || w->k_in <= 0) return fail(FITQ_ERR_SHAPE, "weight: empty shape");
+  if (w->k_in % 64 != 0)
+    return fail(FITQ_ERR_SHAPE, "weight: K=%lld is not a multiple of the NF4 block (64)",
+                (long long)w->k_in);
+  if (w->n_out >= (1ll << 31) || w->k_in >= (1ll << 31))
+    return fail(FITQ_ERR_SHAPE, "weight: dimension too large");
+  if (!al16(w->packed)) return fail(FITQ_ERR_ALIGN, "weight: packed not 16-byte aligned");
+  a->packed = w->packed;
+  a->absmax_code = nested ? w->absmax_code : nullptr;
+  a->nested_absmax = nested ? w->nested_absmax : nullptr;
+  a->nested_quant_map = nested ? w->nested_quant_map : nullptr;
+  a->absmax_f32 = nested ? nullptr : w->absmax_f32;
+  a->quant_map = w->quant_map;
+  a->offset = w->offset;
+  a->n_out = w->n_out;
+  a->k_in = w->k_in;
+  return FITQ_OK;
+}
+
+// Bump allocator over the caller's workspace (256-byte aligned pieces).
+struct Carve {
+  uint8_t* base;
+  size_t cap;
+  size_t used = 0;
+  void* take(size_t bytes) {
+    size_t off = (used + 255) & ~static_cast<size_t>(255);
+    used = off + bytes;
+    return base ? base + off : nullptr;
+  }
+  bool ok() const { return used <= cap; }
+};
+
+inline size_t bf16_bytes(int64_t n) { return static_cast<size_t>(n) * 2; }
+
+bool valid_rank(int r) { return r == 0 || r == 16 || r == 32 || r == 48 || r == 64; }
+
+int launch_status(int rc, const char* what) {
+  if (rc == FITQ_OK) return FITQ_OK;
+  cudaError_t e = cudaGetLastError();
+  return fail(rc, "%s: launch failed (%s)", what, cudaGetErrorString(e));
+}
+
+// Workspace layout of the forward (shared by the size query and the call).
+struct FwdPlan {
+  bool gemv;
+  void* wdeq;      // bf16 [N,K]               (GEMM path)
+  void* a_bf16;    // bf16 [r,K]               (rank > 0)
+  void* t_pad;     // bf16 [M,64]              (rank > 0)
+  void* b_pad;     // bf16 [N,64] = s.B        (GEMM path, rank > 0)
+  float* partial;  // fp32 [splits,M,N]        (GEMV path)
+};
+
+size_t plan_fwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, int sms, FwdPlan* p) {
+  p->gemv = (m <= 64) && (n % 64 == 0);
+  p->wdeq = p->a_bf16 = p->t_pad = p->b_pad = nullptr;
+  p->partial = nullptr;
+  if (rank > 0) {
+    p->a_bf16 = c.take(bf16_bytes(static_cast<int64_t>(rank) * k));
+    p->t_pad = c.take(bf16_bytes(m * 64));
+  }
+  if (p->gemv) {
+    p->partial = static_cast<float*>(c.take(fitq::gemv_partial_bytes(m, n, k, sms, nullptr)));
+  } else {
+    p->wdeq = c.take(bf16_bytes(n * k));
+    if (rank > 0) p->b_pad = c.take(bf16_bytes(n * 64));
+  }
+  return c.used;
+}
+
+struct BwdPlan {
+  void* wt;       // bf16 [K,N]  transposed dequant
+  void* a_bf16;   // bf16 [r,K]  (T recompute)
+  void* t_pad;    // bf16 [M,64] (T recompute)
+  void* bt_bf16;  // bf16 [r,N]  B^T for U = dy.B
+  void* u_pad;    // bf16 [M,64]
+  void* at_pad;   // bf16 [K,64] = s.A^T
+  float* partial; // colproj scratch
+};
+
+size_t plan_bwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, bool need_dx, bool need_t,
+                int sms, BwdPlan* p) {
+  *p = BwdPlan{};
+  if (need_dx) p->wt = c.take(bf16_bytes(n * k));
+  if (rank > 0) {
+    if (need_t) {
+      p->a_bf16 = c.take(bf16_bytes(static_cast<int64_t>(rank) * k));
+      p->t_pad = c.take(bf16_bytes(m * 64));
+    }
+    p->bt_bf16 = c.take(bf16_bytes(static_cast<int64_t>(rank) * n));
+    p->u_pad = c.take(bf16_bytes(m * 64));
+    if (need_dx) p->at_pad = c.take(bf16_bytes(k * 64));
+    size_t pa = fitq::lora_colproj_workspace(m, k, rank, sms);
+    size_t pb = fitq::lora_colproj_workspace(m, n, rank, sms);
+    p->partial = static_cast<float*>(c.take(pa > pb ? pa : pb));
+  }
+  return c.used;
+}
+
+int sms_for_sizing() {
+  int code;
+  int s = current_sms(&code);
+  return s > 0 ? s : 148;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fitq_version(void) { return "fitq 0.1.0 (sm_100a: tcgen05/TMEM/TMA GEMM, NF4 GEMV)"; }
+
+const char* fitq_last_error(void) { return g_last_error.c_str(); }
+
+int fitq_get_device_status(int reset, fitq_stream_t stream) {
+  int code;
+  if (current_sms(&code) == 0) return code;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(FITQ_ERR_CUDA, "stream sync: %s", cudaGetErrorString(cudaGetLastError()));
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fitq_status, sizeof(int)) != cudaSuccess)
+    return fail(FITQ_ERR_CUDA, "status read: %s", cudaGetErrorString(cudaGetLastError()));
+  if (reset) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_fitq_status, &zero, sizeof(int));
+  }
+  return v;
+}
+
+int fitq_nf4_dequant(const fitq_nf4_weight* w, void* out, int out_dtype, int transpose,
+                     fitq_stream_t stream) {
+  fitq::Nf4Args a;
+  int rc = check_weight(w, &a);
+  if (rc) return rc;
+  if (!out) return fail(FITQ_ERR_ARG, "dequant: out is NULL");
+  if (!al16(out)) return fail(FITQ_ERR_ALIGN, "dequant: out not 16-byte aligned");
+  if (out_dtype != FITQ_DTYPE_BF16 && out_dtype != FITQ_DTYPE_F16)
+    return fail(FITQ_ERR_ARG, "dequant: unknown out_dtype %d", out_dtype);
+  if (transpose && a.n_out % 64 != 0)
+    return fail(FITQ_ERR_SHAPE, "dequant: transpose needs N %% 64 == 0 (N=%lld)",
+                (long long)a.n_out);
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  return launch_status(fitq::launch_nf4_dequant(a, out, out_dtype, transpose,
+                                                static_cast<cudaStream_t>(stream), sms),
+                       "nf4_dequant");
+}
+
+size_t fitq_nf4_quantize_workspace(int64_t n_out, int64_t k_in) {
+  Carve c{nullptr, 0};
+  const int64_t nb = n_out * k_in / 64;
+  c.take(static_cast<size_t>(nb) * sizeof(float));
+  c.take(static_cast<size_t>((nb + fitq::kOffsetChunk - 1) / fitq::kOffsetChunk) * sizeof(double));
+  return c.used;
+}
+
+int fitq_nf4_quantize(const float* w, int64_t n_out, int64_t k_in, const float* quant_map,
+                      const float* nested_quant_map, uint8_t* packed, uint8_t* absmax_code,
+                      float* nested_absmax, float* offset_out, void* workspace,
+                      size_t workspace_bytes, fitq_stream_t stream) {
+  if (!w || !quant_map || !nested_quant_map || !packed || !absmax_code || !nested_absmax ||
+      !offset_out)
+    return fail(FITQ_ERR_ARG, "quantize: NULL argument");
+  if (n_out <= 0 || k_in <= 0 || k_in % 64 != 0)
+    return fail(FITQ_ERR_SHAPE, "quantize: need K %% 64 == 0 (N=%lld K=%lld)", (long long)n_out,
+                (long long)k_in);
+  if ((reinterpret_cast<uintptr_t>(w) & 7u) != 0)
+    return fail(FITQ_ERR_ALIGN, "quantize: w not 8-byte aligned");
+  const size_t need = fitq_nf4_quantize_workspace(n_out, k_in);
+  if (!workspace || workspace_bytes < need)
+    return fail(FITQ_ERR_WORKSPACE, "quantize: workspace %zu < %zu bytes", workspace_bytes, need);
+  int rc;
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  const int64_t nb = n_out * k_in / 64;
+  float* absmax = static_cast<float*>(c.take(static_cast<size_t>(nb) * sizeof(float)));
+  double* partial = static_cast<double*>(
+      c.take(static_cast<size_t>((nb + fitq::kOffsetChunk - 1) / fitq::kOffsetChunk) *
+             sizeof(double)));
+  return launch_status(fitq::launch_nf4_quantize(w, n_out * k_in, quant_map, nested_quant_map,
+                                                 packed, absmax_code, nested_absmax, offset_out,
+                                                 absmax, partial,
+                                                 static_cast<cudaStream_t>(stream), sms),
+                       "nf4_quantize");
+}
+
+size_t fitq_qlora_fwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank) {
+  Carve c{nullptr, 0};
+  FwdPlan p;
+  return plan_fwd(c, m, n_out, k_in, rank, sms_for_sizing(), &p);
+}
+
+static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                          const float* lora_b, int rank, float scale, const void* bias, void* y,
+                          const void* y_add,
+                          void* t_out, void* workspace, size_t workspace_bytes,
+                          fitq_stream_t stream, int force_gemv) {
+  fitq::Nf4Args a;
+  int rc = check_weight(w, &a);
+  if (rc) return rc;
+  if (!x || !y) return fail(FITQ_ERR_ARG, "qlora_fwd: x and y are required");
+  if (m <= 0 || m >= (1ll << 31)) return fail(FITQ_ERR_SHAPE, "qlora_fwd: bad M=%lld", (long long)m);
+  if (!valid_rank(rank)) return fail(FITQ_ERR_UNSUPPORTED, "qlora_fwd: rank %d not in {0,16,32,48,64}", rank);
+  if (rank > 0 && (!lora_a || !lora_b)) return fail(FITQ_ERR_ARG, "qlora_fwd: lora_a/lora_b required for rank > 0");
+  if (a.n_out % 16 != 0) return fail(FITQ_ERR_SHAPE, "qlora_fwd: N=%lld not a multiple of 16", (long long)a.n_out);
+  if (!al16(x) || !al16(y) || (y_add && !al16(y_add)) || (t_out && !al16(t_out)) ||
+      (bias && !al16(bias)))
+    return fail(FITQ_ERR_ALIGN, "qlora_fwd: x/y/bias/y_add/t_out must be 16-byte aligned");
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  const int64_t N = a.n_out, K = a.k_in;
+  Carve probe{nullptr, 0};
+  FwdPlan p;
+  const size_t need = plan_fwd(probe, m, N, K, rank, sms, &p);
+  if (force_gemv && !p.gemv)
+    return fail(FITQ_ERR_SHAPE, "nf4_gemv: needs M <= 64 and N %% 64 == 0 (M=%lld N=%lld)",
+                (long long)m, (long long)N);
+  if (workspace_bytes < need || (need > 0 && !workspace))
+    return fail(FITQ_ERR_WORKSPACE, "qlora_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  plan_fwd(c, m, N, K, rank, sms, &p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (rank > 0) {
+    rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
+    if (rc) return launch_status(rc, "lora_a cast");
+    rc = fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
+    if (rc) return launch_status(rc, "lora T = x.A^T");
+  }
+  if (p.gemv) {
+    int splits = 1;
+    rc = fitq::launch_nf4_gemv_core(a, x, m, p.partial, st, sms, &splits);
+    if (rc) return launch_status(rc, "nf4_gemv");
+    rc = fitq::launch_gemv_finish(p.partial, splits, m, N, p.t_pad, lora_b, rank, scale, bias,
+                                  y_add, y, st, sms);
+    return launch_status(rc, "nf4_gemv finish");
+  }
+  rc = fitq::launch_nf4_dequant(a, p.wdeq, FITQ_DTYPE_BF16, 0, st, sms);
+  if (rc) return launch_status(rc, "nf4_dequant");
+  if (rank > 0) {
+    rc = fitq::launch_pad_lora_weight(lora_b, N, rank, scale, 0, p.b_pad, st);
+    if (rc) return launch_status(rc, "lora B pad");
+  }
+  fitq::GemmArgs g{};
+  g.a = x; g.lda = K;
+  g.b = p.wdeq; g.ldb = K;
+  g.pa = p.t_pad; g.pb = p.b_pad;
+  g.c = y; g.ldc = N;
+  g.c_add = y_add; g.ldc_add = N;
+  g.bias = bias;
+  g.m = m; g.n = N; g.k = K;
+  g.lora_k = rank;
+  g.status = status_ptr();
+  return launch_status(fitq::launch_gemm_bf16_tn(g, st, sms), "tcgen05 gemm");
+}
+
+int fitq_qlora_fwd(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                   const float* lora_b, int rank, float scale, const void* bias, void* y,
+                   const void* y_add, void* t_out, void* workspace, size_t workspace_bytes,
+                   fitq_stream_t stream) {
+  return qlora_fwd_impl(w, x, m, lora_a, lora_b, rank, scale, bias, y, y_add, t_out, workspace,
+                        workspace_bytes, stream, 0);
+}
+
+size_t fitq_nf4_gemv_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank) {
+  return fitq_qlora_fwd_workspace(m, n_out, k_in, rank);
+}
+
+int fitq_nf4_gemv(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                  const float* lora_b, int rank, float scale, const void* bias, void* y,
+                  const void* y_add, void* workspace, size_t workspace_bytes,
+                  fitq_stream_t stream) {
+  return qlora_fwd_impl(w, x, m, lora_a, lora_b, rank, scale, bias, y, y_add, nullptr, workspace,
+                        workspace_bytes, stream, 1);
+}
+
+size_t fitq_qlora_bwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank) {
+  Carve c{nullptr, 0};
+  BwdPlan p;
+  return plan_bwd(c, m, n_out, k_in, rank, true, true, sms_for_sizing(), &p);
+}
+
+int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int64_t m,
+                   const float* lora_a, const float* lora_b, int rank, float scale,
+                   const void* t_saved, void* dx, int dx_accumulate, float* grad_a,
+                   float* grad_b, int grad_accumulate, void* workspace, size_t workspace_bytes,
+                   fitq_stream_t stream) {
+  fitq::Nf4Args a;
+  int rc = check_weight(w, &a);
+  if (rc) return rc;
+  if (!dy) return fail(FITQ_ERR_ARG, "qlora_bwd: dy is required");
+  if (m <= 0 || m >= (1ll << 31)) return fail(FITQ_ERR_SHAPE, "qlora_bwd: bad M=%lld", (long long)m);
+  if (!valid_rank(rank)) return fail(FITQ_ERR_UNSUPPORTED, "qlora_bwd: rank %d not in {0,16,32,48,64}", rank);
+  if (rank > 0 && (!lora_a || !lora_b || !grad_a || !grad_b || !x))
+    return fail(FITQ_ERR_ARG, "qlora_bwd: x, lora_a/b and grad_a/b are required for rank > 0");
+  const int64_t N = a.n_out, K = a.k_in;
+  if (N % 64 != 0) return fail(FITQ_ERR_SHAPE, "qlora_bwd: N=%lld not a multiple of 64", (long long)N);
+  if (!al16(dy) || (x && !al16(x)) || (dx && !al16(dx)) || (t_saved && !al16(t_saved)))
+    return fail(FITQ_ERR_ALIGN, "qlora_bwd: x/dy/dx/t_saved must be 16-byte aligned");
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  const bool need_dx = dx != nullptr;
+  const bool need_t = rank > 0 && t_saved == nullptr;
+  Carve probe{nullptr, 0};
+  BwdPlan p;
+  const size_t need = plan_bwd(probe, m, N, K, rank, need_dx, need_t, sms, &p);
+  if (workspace_bytes < need || (need > 0 && !workspace))
+    return fail(FITQ_ERR_WORKSPACE, "qlora_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  plan_bwd(c, m, N, K, rank, need_dx, need_t, sms, &p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const void* t_ptr = t_saved;
+  int64_t t_ld = rank;
+  if (rank > 0) {
+    if (need_t) {
+      rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
+      if (rc) return launch_status(rc, "lora_a cast");
+      rc = fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, nullptr, st, sms);
+      if (rc) return launch_status(rc, "lora T recompute");
+      t_ptr = p.t_pad;
+      t_ld = 64;
+    }
+    // U = dy.B, with B^T cast to bf16 [r, N]
+    rc = fitq::launch_f32_to_bf16_t(lora_b, N, rank, p.bt_bf16, st);
+    if (rc) return launch_status(rc, "lora_b cast");
+    rc = fitq::launch_lora_rowproj(dy, N, m, N, p.bt_bf16, rank, p.u_pad, nullptr, st, sms);
+    if (rc) return launch_status(rc, "lora U = dy.B");
+    // dB[N, r] = s.dy^T.T ; dA[r, K] = s.U^T.x
+    rc = fitq::launch_lora_colproj(t_ptr, t_ld, dy, N, m, N, rank, scale, grad_b, 1,
+                                   grad_accumulate, p.partial, st, sms);
+    if (rc) return launch_status(rc, "lora dB");
+    rc = fitq::launch_lora_colproj(p.u_pad, 64, x, K, m, K, rank, scale, grad_a, 0,
+                                   grad_accumulate, p.partial, st, sms);
+    if (rc) return launch_status(rc, "lora dA");
+  }
+  if (!need_dx) return FITQ_OK;
+  // dx[M, K] = dy[M, N].W[N, K] + U.(s.A): W^T materialised [K, N] bf16 (bit-exact dequant).
+  rc = fitq::launch_nf4_dequant(a, p.wt, FITQ_DTYPE_BF16, 1, st, sms);
+  if (rc) return launch_status(rc, "nf4_dequant (transposed)");
+  if (rank > 0) {
+    rc = fitq::launch_pad_lora_weight(lora_a, K, rank, scale, 1, p.at_pad, st);
+    if (rc) return launch_status(rc, "lora A^T pad");
+  }
+  fitq::GemmArgs g{};
+  g.a = dy; g.lda = N;
+  g.b = p.wt; g.ldb = N;
+  g.pa = p.u_pad; g.pb = p.at_pad;
+  g.c = dx; g.ldc = K;
+  g.c_add = dx_accumulate ? dx : nullptr; g.ldc_add = K;
+  g.m = m; g.n = K; g.k = N;
+  g.lora_k = rank;
+  g.status = status_ptr();
+  return launch_status(fitq::launch_gemm_bf16_tn(g, st, sms), "tcgen05 gemm (dx)");
+}
+
+int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, int64_t m,
+                      int64_t n, int64_t k, fitq_stream_t stream) {
+  if (!a || !b || !c) return fail(FITQ_ERR_ARG, "gemm: NULL operand");
+  if (m <= 0 || n <= 0 || k <= 0 || k % 64 != 0 || n % 16 != 0 || m >= (1ll << 31) ||
+      n >= (1ll << 31) || k >= (1ll << 31))
+    return fail(FITQ_ERR_SHAPE, "gemm: need K %% 64 == 0 and N %% 16 == 0 (M=%lld N=%lld K=%lld)",
+                (long long)m, (long long)n, (long long)k);
+  if (!al16(a) || !al16(b) || !al16(c) || (c_add && !al16(c_add)))
+    return fail(FITQ_ERR_ALIGN, "gemm: operands must be 16-byte aligned");
+  int rc;
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  fitq::GemmArgs g{};
+  g.a = a; g.lda = k;
+  g.b = b; g.ldb = k;
+  g.c = c; g.ldc = n;
+  g.c_add = c_add; g.ldc_add = n;
+  g.m = m; g.n = n; g.k = k;
+  g.lora_k = 0;
+  g.status = status_ptr();
+  return launch_status(fitq::launch_gemm_bf16_tn(g, static_cast<cudaStream_t>(stream), sms),
+                       "tcgen05 gemm");
+}
+
+int fitq_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq,
+                    int64_t n, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, int step, const float* clip, fitq_stream_t stream) {
+  if (!param || !grad || !exp_avg || !exp_avg_sq) return fail(FITQ_ERR_ARG, "adamw: NULL buffer");
+  if (n < 0 || step < 1) return fail(FITQ_ERR_ARG, "adamw: need n >= 0 and step >= 1");
+  int rc;
+  if (!current_sms(&rc)) return rc;
+  if (n == 0) return FITQ_OK;
+  return launch_status(fitq::launch_adamw(param, grad, exp_avg, exp_avg_sq, n, lr, beta1, beta2,
+                                          eps, weight_decay, step, clip,
+                                          static_cast<cudaStream_t>(stream)),
+                       "adamw");
+}
+
+size_t fitq_grad_norm_workspace(int64_t n) { return fitq::grad_norm_workspace(n); }
+
+int fitq_grad_clip_coef(const float* grads, int64_t n, float max_norm, float* norm_out,
+                        void* workspace, size_t workspace_bytes, fitq_stream_t stream) {
+  if (!grads || !norm_out) return fail(FITQ_ERR_ARG, "grad_clip: NULL buffer");
+  if (n < 0) return fail(FITQ_ERR_ARG, "grad_clip: n < 0");
+  const size_t need = fitq::grad_norm_workspace(n);
+  if (!workspace || workspace_bytes < need)
+    return fail(FITQ_ERR_WORKSPACE, "grad_clip: workspace %zu < %zu bytes", workspace_bytes, need);
+  int rc;
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_grad_clip(grads, n, max_norm, norm_out, workspace,
+                                              static_cast<cudaStream_t>(stream)),
+                       "grad_clip");
+}
+
+}  // extern "C"

@@ -1,0 +1,85 @@
+// Internal launcher declarations shared by the .cu files of libfitq.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace fitq {
+
+constexpr int64_t kOffsetChunk = 4096;  // absmax mean: double sum per chunk, then chunks in order
+
+// Device-side copy of fitq_nf4_weight.
+struct Nf4Args {
+  const uint8_t* packed;
+  const uint8_t* absmax_code;
+  const float* nested_absmax;
+  const float* nested_quant_map;
+  const float* absmax_f32;
+  const float* quant_map;
+  float offset;
+  int64_t n_out;
+  int64_t k_in;
+};
+
+int launch_nf4_dequant(const Nf4Args& w, void* out, int out_dtype, int transpose, cudaStream_t st,
+                       int num_sms);
+int launch_nf4_quantize(const float* wt, int64_t n, const float* qmap, const float* nqmap,
+                        uint8_t* packed, uint8_t* codes, float* nested_absmax, float* offset_out,
+                        float* absmax_ws, double* partial_ws, cudaStream_t st, int num_sms);
+
+// tcgen05 GEMM: C[M,N] = A[M,K].B[N,K]^T (+ Pa[M,r].Pb[N,r]^T) (+ C_add).
+// A/B/Pa/Pb bf16 row-major; Pa/Pb have a row pitch of 64 elements, columns
+// r..63 ignored.  lora_k in {0,16,32,48,64}.
+struct GemmArgs {
+  const void* a; int64_t lda;
+  const void* b; int64_t ldb;
+  const void* pa;  // may be null when lora_k == 0
+  const void* pb;
+  void* c; int64_t ldc;
+  const void* c_add; int64_t ldc_add;
+  const void* bias;  // bf16 [N] or null
+  int64_t m, n, k;
+  int lora_k;
+  int* status;  // device status word (bounded-wait timeouts)
+};
+int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms);
+
+// LoRA building blocks (lora.cu).
+// out[M, r] = in[M, D] . wt[r, D]^T  (bf16 in, fp32 accumulate); written as
+// bf16 into out_pad (row pitch 64; columns r..63 are left untouched and never
+// read, since r % 16 == 0) and, when non-null, into out_dense [M, r].
+int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, const void* wt_bf16,
+                        int r, void* out_pad, void* out_dense, cudaStream_t st, int num_sms);
+// Reduction over rows:  res[r, D] = scale . p[M, r]^T . in[M, D]
+// (p bf16 with row pitch ld_p, a multiple of 8).  layout 0 writes res[r][D],
+// layout 1 res[D][r].  accumulate != 0 adds into res.  partial_ws: fp32
+// [chunks, r, D] scratch of lora_colproj_workspace() bytes.
+size_t lora_colproj_workspace(int64_t M, int64_t D, int r, int num_sms);
+int launch_lora_colproj(const void* p, int64_t ld_p, const void* in, int64_t ld_in, int64_t M, int64_t D,
+                        int r, float scale, float* res, int layout, int accumulate,
+                        float* partial_ws, cudaStream_t st, int num_sms);
+// fp32 [rows, r] (row-major) -> bf16 scaled, pitch 64, zero padded: out[i][j] = bf16(s*in[i][j]).
+int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, int transpose_in,
+                           void* out_pad, cudaStream_t st);
+// fp32 -> bf16 copy of a [r, D] matrix.
+int launch_f32_to_bf16(const float* in, int64_t n, void* out, cudaStream_t st);
+// fp32 [rows, cols] -> bf16 [cols, rows] (transposed).
+int launch_f32_to_bf16_t(const float* in, int64_t rows, int cols, void* out, cudaStream_t st);
+
+// NF4 GEMV / skinny GEMM for M <= 64 (gemv.cu): split-K partial products
+// [splits, M, N] fp32, then a finishing pass adding LoRA / y_add -> bf16.
+size_t gemv_partial_bytes(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* splits_out);
+int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* partial,
+                         cudaStream_t st, int num_sms, int* splits_out);
+int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, const void* t_pad,
+                       const float* lora_b, int rank, float scale, const void* bias,
+                       const void* y_add, void* y, cudaStream_t st, int num_sms);
+
+// Optimizer kernels (optim.cu).
+int launch_adamw(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
+                 float b2, float eps, float wd, int step, const float* clip, cudaStream_t st);
+size_t grad_norm_workspace(int64_t n);
+int launch_grad_clip(const float* g, int64_t n, float max_norm, float* norm_out, void* ws,
+                     cudaStream_t st);
+
+}  // namespace fitq

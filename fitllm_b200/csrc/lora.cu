@@ -1,0 +1,278 @@
+// LoRA adapter kernels for the QLoRA linear (PEFT lora.Linear4bit semantics,
+// fitllm/qlora.py:74-83): the rank-r projections T = x.A^T and U = dy.B, the
+// row reductions dA = s.U^T.x and dB = s.dy^T.T, and the small casts that turn
+// the fp32 adapter parameters into the bf16 operands of the tcgen05 GEMM.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fitq {
+namespace {
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// out[M, R] = in[M, D] . wt[R, D]^T with warp-level bf16 MMA (m16n8k16).
+// A CTA owns 16 rows; its 4 warps take interleaved 32-column chunks of D and
+// are reduced through shared memory in a fixed order.  Inside a chunk every
+// thread loads 16 contiguous bytes of a row and feeds them to two MMAs: the
+// reduction index is permuted identically in both operands, which leaves the
+// sum unchanged and keeps every load coalesced.
+template <int R>
+__global__ void __launch_bounds__(128) lora_rowproj_kernel(const __nv_bfloat16* __restrict__ in,
+                                                           int64_t ld, int64_t M, int64_t D,
+                                                           const __nv_bfloat16* __restrict__ wt,
+                                                           __nv_bfloat16* __restrict__ out_pad,
+                                                           __nv_bfloat16* __restrict__ out_dense) {
+  constexpr int NT = R / 8;
+  __shared__ float red[4][16][R];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 16;
+  const int64_t ra = m0 + g, rb = m0 + g + 8;
+  float acc[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
+  const int64_t nchunks = D / 32;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int64_t c = warp; c < nchunks; c += 4) {
+    const int64_t col = c * 32 + 8 * q;
+    const uint4 xa = ra < M ? __ldg(reinterpret_cast<const uint4*>(in + ra * ld + col)) : zero;
+    const uint4 xb = rb < M ? __ldg(reinterpret_cast<const uint4*>(in + rb * ld + col)) : zero;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint4 wb = __ldg(reinterpret_cast<const uint4*>(wt + (int64_t)(8 * t + g) * D + col));
+      mma_bf16_16816(acc[t], xa.x, xb.x, xa.y, xb.y, wb.x, wb.y);
+      mma_bf16_16816(acc[t], xa.z, xb.z, xa.w, xb.w, wb.z, wb.w);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    red[warp][g][8 * t + 2 * q] = acc[t][0];
+    red[warp][g][8 * t + 2 * q + 1] = acc[t][1];
+    red[warp][g + 8][8 * t + 2 * q] = acc[t][2];
+    red[warp][g + 8][8 * t + 2 * q + 1] = acc[t][3];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 16 * R / 2; e += 128) {
+    const int row = (2 * e) / R, col = (2 * e) % R;
+    const int64_t m = m0 + row;
+    if (m >= M) continue;
+    float v0 = red[0][row][col], v1 = red[0][row][col + 1];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) {
+      v0 += red[w][row][col];
+      v1 += red[w][row][col + 1];
+    }
+    const uint32_t pk = pack_bf16x2(v0, v1);
+    *reinterpret_cast<uint32_t*>(out_pad + m * 64 + col) = pk;
+    if (out_dense) *reinterpret_cast<uint32_t*>(out_dense + m * R + col) = pk;
+  }
+}
+
+// Partial row reduction:  partial[chunk][j][d] = sum_{m in chunk} p[m][j0+j] * in[m][d]
+// for a 16-wide group of adapter columns j0 = 16*blockIdx.z.  CTA = 8 warps
+// over one 256-column tile of D (8 columns per lane); warps take rows
+// m = first + warp + 8i and are combined in shared memory in warp order.
+__global__ void __launch_bounds__(256) lora_colproj_kernel(
+    const __nv_bfloat16* __restrict__ p_pad, int64_t ld_p, const __nv_bfloat16* __restrict__ in,
+    int64_t ld, int64_t M, int64_t D, int64_t rows_per_chunk, int R, float* __restrict__ partial) {
+  __shared__ float red[16][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t d0 = static_cast<int64_t>(blockIdx.x) * 256 + lane * 8;
+  const int64_t chunk = blockIdx.y;
+  const int j0 = blockIdx.z * 16;
+  const int64_t mb = chunk * rows_per_chunk;
+  const int64_t me = mb + rows_per_chunk < M ? mb + rows_per_chunk : M;
+  float acc[16][8];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[j][c] = 0.f;
+  const bool col_ok = d0 < D;
+  for (int64_t m = mb + warp; m < me; m += 8) {
+    float xv[8];
+    if (col_ok) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(in + m * ld + d0));
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(w4[i]);
+        xv[2 * i] = f.x;
+        xv[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[i] = 0.f;
+    }
+    const uint4 pa = __ldg(reinterpret_cast<const uint4*>(p_pad + m * ld_p + j0));
+    const uint4 pb = __ldg(reinterpret_cast<const uint4*>(p_pad + m * ld_p + j0 + 8));
+    const uint32_t pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 f = unpack_bf16x2(pw[i]);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        acc[2 * i][c] = fmaf(f.x, xv[c], acc[2 * i][c]);
+        acc[2 * i + 1][c] = fmaf(f.y, xv[c], acc[2 * i + 1][c]);
+      }
+    }
+  }
+  // Fixed-order combination of the 8 warps.
+  for (int w = 0; w < 8; ++w) {
+    if (warp == w) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float& r = red[j][lane * 8 + c];
+          r = (w == 0) ? acc[j][c] : r + acc[j][c];
+        }
+    }
+    __syncthreads();
+  }
+  // write partial[chunk][j0 + j][d]
+  for (int e = threadIdx.x; e < 16 * 256; e += 256) {
+    const int j = e / 256, c = e % 256;
+    const int64_t d = static_cast<int64_t>(blockIdx.x) * 256 + c;
+    if (d < D) partial[(chunk * R + j0 + j) * D + d] = red[j][c];
+  }
+}
+
+// res = (accumulate ? res : 0) + scale * sum_chunks partial, chunks in order.
+__global__ void lora_colproj_finish_kernel(const float* __restrict__ partial, int64_t nchunks,
+                                           int R, int64_t D, float scale, float* __restrict__ res,
+                                           int layout, int accumulate) {
+  const int64_t total = static_cast<int64_t>(R) * D;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int64_t c = 0; c < nchunks; ++c) s += partial[c * total + e];
+    const int64_t j = e / D, d = e % D;
+    const int64_t o = layout == 0 ? e : d * R + j;
+    const float v = scale * s;
+    res[o] = accumulate ? res[o] + v : v;
+  }
+}
+
+// out[i][j] = bf16(scale * in(i, j)), pitch 64; in(i,j) = in[i*r + j] or, when
+// transpose_in, in[j*rows + i].  Columns r..63 are zeroed.
+__global__ void pad_lora_weight_kernel(const float* __restrict__ in, int64_t rows, int r,
+                                       float scale, int transpose_in,
+                                       __nv_bfloat16* __restrict__ out) {
+  const int64_t total = rows * 64;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e >> 6;
+    const int j = static_cast<int>(e & 63);
+    float v = 0.f;
+    if (j < r) v = scale * (transpose_in ? in[j * rows + i] : in[i * r + j]);
+    out[e] = __float2bfloat16_rn(v);
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ in, int64_t n,
+                                   __nv_bfloat16* __restrict__ out) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x)
+    out[e] = __float2bfloat16_rn(in[e]);
+}
+
+// out[j][i] = bf16(in[i][j]) for in fp32 [rows, cols].
+__global__ void f32_to_bf16_t_kernel(const float* __restrict__ in, int64_t rows, int cols,
+                                     __nv_bfloat16* __restrict__ out) {
+  const int64_t total = rows * cols;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = e / rows, i = e % rows;  // output index e = j*rows + i
+    out[e] = __float2bfloat16_rn(in[i * cols + j]);
+  }
+}
+
+int grid_for(int64_t n, int threads, int num_sms) {
+  int64_t b = (n + threads - 1) / threads;
+  int64_t cap = static_cast<int64_t>(num_sms) * 16;
+  return static_cast<int>(b < cap ? (b > 0 ? b : 1) : cap);
+}
+
+void colproj_geometry(int64_t M, int64_t D, int num_sms, int64_t* rows_per_chunk,
+                      int64_t* nchunks) {
+  const int64_t dtiles = (D + 255) / 256;
+  int64_t want = (2 * static_cast<int64_t>(num_sms) + dtiles - 1) / dtiles;
+  if (want < 1) want = 1;
+  int64_t rpc = (M + want - 1) / want;
+  rpc = ((rpc + 7) / 8) * 8;
+  if (rpc < 8) rpc = 8;
+  *rows_per_chunk = rpc;
+  *nchunks = (M + rpc - 1) / rpc;
+}
+
+}  // namespace
+
+int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, const void* wt_bf16,
+                        int r, void* out_pad, void* out_dense, cudaStream_t st, int num_sms) {
+  (void)num_sms;
+  const int grid = static_cast<int>((M + 15) / 16);
+  auto i = static_cast<const __nv_bfloat16*>(in);
+  auto w = static_cast<const __nv_bfloat16*>(wt_bf16);
+  auto op = static_cast<__nv_bfloat16*>(out_pad);
+  auto od = static_cast<__nv_bfloat16*>(out_dense);
+  switch (r) {
+    case 16: lora_rowproj_kernel<16><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
+    case 32: lora_rowproj_kernel<32><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
+    case 48: lora_rowproj_kernel<48><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
+    case 64: lora_rowproj_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
+    default: return FITQ_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+size_t lora_colproj_workspace(int64_t M, int64_t D, int r, int num_sms) {
+  int64_t rpc, nch;
+  colproj_geometry(M, D, num_sms, &rpc, &nch);
+  return static_cast<size_t>(nch) * r * D * sizeof(float);
+}
+
+int launch_lora_colproj(const void* p_pad, int64_t ld_p, const void* in, int64_t ld_in, int64_t M,
+                        int64_t D, int r, float scale, float* res, int layout, int accumulate,
+                        float* partial_ws, cudaStream_t st, int num_sms) {
+  int64_t rpc, nch;
+  colproj_geometry(M, D, num_sms, &rpc, &nch);
+  dim3 grid(static_cast<unsigned>((D + 255) / 256), static_cast<unsigned>(nch),
+            static_cast<unsigned>(r / 16));
+  lora_colproj_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p_pad), ld_p,
+                                            static_cast<const __nv_bfloat16*>(in), ld_in, M, D,
+                                            rpc, r, partial_ws);
+  lora_colproj_finish_kernel<<<grid_for(static_cast<int64_t>(r) * D, 256, num_sms), 256, 0, st>>>(
+      partial_ws, nch, r, D, scale, res, layout, accumulate);
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, int transpose_in,
+                           void* out_pad, cudaStream_t st) {
+  pad_lora_weight_kernel<<<grid_for(rows * 64, 256, 148), 256, 0, st>>>(
+      in, rows, r, scale, transpose_in, static_cast<__nv_bfloat16*>(out_pad));
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_f32_to_bf16_t(const float* in, int64_t rows, int cols, void* out, cudaStream_t st) {
+  f32_to_bf16_t_kernel<<<grid_for(rows * cols, 256, 148), 256, 0, st>>>(
+      in, rows, cols, static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_f32_to_bf16(const float* in, int64_t n, void* out, cudaStream_t st) {
+  f32_to_bf16_kernel<<<grid_for(n, 256, 148), 256, 0, st>>>(in, n,
+                                                             static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+}  // namespace fitq

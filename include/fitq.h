@@ -1,0 +1,180 @@
+/*
+ * fitq -- C ABI of the B200 (sm_100a) NF4 QLoRA linear.
+ *
+ * Every pointer is a device pointer owned by the caller unless stated
+ * otherwise; every call is asynchronous on the given stream and returns a
+ * status code (FITQ_OK = 0).  No entry point allocates device memory except
+ * where a caller-provided workspace is named; no entry point synchronises the
+ * stream except fitq_get_device_status.  Shapes that a kernel does not
+ * support return an error: there is no fallback path.
+ *
+ * Reference interfaces these calls replace (paths inside FitLLM; the NF4 and
+ * LoRA arithmetic itself lives in bitsandbytes and PEFT, which FitLLM calls):
+ *   fitq_nf4_dequant   bitsandbytes dequantize_4bit, run inside every
+ *                      bnb.nn.Linear4bit forward (fitllm/forward.py:511 ->
+ *                      _run_layer, fitllm/forward.py:680-686) and again in
+ *                      MatMul4Bit.backward (fitllm/backward.py:234).
+ *   fitq_nf4_quantize  bitsandbytes quantize_4bit(nf4, compress_statistics)
+ *                      run at load time by BitsAndBytesConfig
+ *                      (fitllm/model.py:211-219).
+ *   fitq_qlora_fwd     PEFT lora.Linear4bit.forward = Linear4bit.forward +
+ *                      lora_B(lora_A(x)) * scaling (fitllm/qlora.py:74-83),
+ *                      entered from fitllm/forward.py:511 and the recompute
+ *                      in fitllm/backward.py:222-231.
+ *   fitq_qlora_bwd     autograd of the above: MatMul4Bit.backward (dX through
+ *                      the dequantised weight) + the LoRA graph (dA, dB),
+ *                      entered by h_out.backward (fitllm/backward.py:234);
+ *                      grad_accumulate mirrors _accumulate_grads_to_ram
+ *                      (fitllm/backward.py:287-299).
+ *   fitq_nf4_gemv      bitsandbytes gemv_4bit, the single-token decode path of
+ *                      matmul_4bit (fitllm/forward.py:623-625), widened to the
+ *                      speculative-verify row counts (M <= 64,
+ *                      fitllm/inference.py:380-397).
+ *   fitq_adamw_step    ShardOptimizer.step_from_memory AdamW update
+ *                      (fitllm/optimizer.py:161-231) with the global-norm clip
+ *                      of _clip_lora_accum_grads (fitllm/trainer.py:70-88).
+ *   fitq_gemm_bf16_tn  (building block, no direct reference counterpart) the
+ *                      tcgen05 GEMM that the fused paths are built on.
+ */
+#ifndef FITQ_H
+#define FITQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FITQ_API __attribute__((visibility("default")))
+#else
+#define FITQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FITQ_OK = 0,
+  FITQ_ERR_ARG = 1,         /* null pointer or invalid scalar argument       */
+  FITQ_ERR_SHAPE = 2,       /* a dimension the kernels do not support        */
+  FITQ_ERR_ALIGN = 3,       /* a pointer or row pitch not 16-byte aligned    */
+  FITQ_ERR_UNSUPPORTED = 4, /* valid request outside the implemented range   */
+  FITQ_ERR_WORKSPACE = 5,   /* workspace missing or smaller than required    */
+  FITQ_ERR_CUDA = 6,        /* CUDA runtime / driver call failed             */
+  FITQ_ERR_TIMEOUT = 7,     /* a bounded device-side wait ran out            */
+  FITQ_ERR_NO_DEVICE = 8    /* no usable sm_100 device                       */
+};
+
+/* A cudaStream_t (CUstream) handle; NULL is the legacy default stream. */
+typedef void* fitq_stream_t;
+
+/* One NF4 weight W[N,K] in the bitsandbytes Params4bit layout (flat keys
+ * <param>, .absmax, .nested_absmax, .quant_map, .nested_quant_map and the
+ * nested_offset of .quant_state.bitsandbytes__nf4, fitllm/forward.py:95-109).
+ * packed: N*K/2 bytes, flat row-major, element 2i in the high nibble.
+ * Double-quantised statistics: absmax_code (one uint8 per 64 elements),
+ * nested_absmax (one fp32 per 256 codes), nested_quant_map (256 fp32), offset.
+ * A state without double quantisation sets absmax_f32 (one fp32 per 64
+ * elements) instead and leaves the three nested fields NULL. */
+typedef struct fitq_nf4_weight {
+  const uint8_t* packed;
+  const uint8_t* absmax_code;
+  const float* nested_absmax;
+  const float* nested_quant_map;
+  const float* absmax_f32;
+  const float* quant_map;
+  float offset;
+  int64_t n_out;
+  int64_t k_in;
+} fitq_nf4_weight;
+
+/* Output dtypes of fitq_nf4_dequant. */
+enum { FITQ_DTYPE_BF16 = 0, FITQ_DTYPE_F16 = 1 };
+
+FITQ_API const char* fitq_version(void);
+
+/* Text of the last host-side error seen by this thread (never NULL). */
+FITQ_API const char* fitq_last_error(void);
+
+/* Synchronise `stream`, then return the device status word (FITQ_OK or the
+ * first FITQ_ERR_* a kernel recorded, e.g. FITQ_ERR_TIMEOUT).  reset != 0
+ * clears it afterwards. */
+FITQ_API int fitq_get_device_status(int reset, fitq_stream_t stream);
+
+/* W -> out, bit-exact: absmax_b = fl(fl(nqm[code_b]*nabs[b/256]) + offset),
+ * w = fl(qm[nibble]*absmax_b) rounded to nearest even into bf16 or fp16.
+ * transpose = 0 writes out[N,K]; transpose = 1 writes out[K,N].
+ * Requires K % 64 == 0 and, for transpose, N % 64 == 0. */
+FITQ_API int fitq_nf4_dequant(const fitq_nf4_weight* w, void* out, int out_dtype, int transpose,
+                     fitq_stream_t stream);
+
+/* fp32 W[N,K] -> NF4 with double-quantised absmax.  quant_map (16) and
+ * nested_quant_map (256) are the sorted level tables to use; offset_out
+ * receives the fp32 mean of the first-level absmax (device, 1 float).
+ * workspace >= fitq_nf4_quantize_workspace(N, K) bytes. */
+FITQ_API size_t fitq_nf4_quantize_workspace(int64_t n_out, int64_t k_in);
+FITQ_API int fitq_nf4_quantize(const float* w, int64_t n_out, int64_t k_in, const float* quant_map,
+                      const float* nested_quant_map, uint8_t* packed, uint8_t* absmax_code,
+                      float* nested_absmax, float* offset_out, void* workspace,
+                      size_t workspace_bytes, fitq_stream_t stream);
+
+/* y[M,N] (bf16) = x[M,K].W^T + scale.(x.A^T).B^T (+ bias[N]) (+ y_add[M,N]).
+ * x bf16 row-major; lora_a fp32 [rank,K] and lora_b fp32 [N,rank] (PEFT
+ * layout), both NULL (rank 0) for a bare Linear4bit; bias bf16 [N] or NULL
+ * (Linear4bit's frozen bias); y_add bf16 [M,N] or NULL (fused residual).  t_out, if non-NULL,
+ * receives T = x.A^T as bf16 [M,rank] for the backward.  rank in {0,16,32,48,64}.
+ * M <= 64 runs the NF4 GEMV kernel, larger M the tcgen05 GEMM. */
+FITQ_API size_t fitq_qlora_fwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank);
+FITQ_API int fitq_qlora_fwd(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                   const float* lora_b, int rank, float scale, const void* bias, void* y,
+                   const void* y_add, void* t_out, void* workspace, size_t workspace_bytes,
+                   fitq_stream_t stream);
+
+/* Backward of fitq_qlora_fwd for upstream grad dy[M,N] (bf16):
+ *   dx[M,K]       = dy.W + scale.(dy.B).A            (bf16; += if dx_accumulate)
+ *   grad_a[rank,K] = scale.(dy.B)^T.x                 (fp32; += if grad_accumulate)
+ *   grad_b[N,rank] = scale.dy^T.(x.A^T)               (fp32; += if grad_accumulate)
+ * t_saved: T from the forward (bf16 [M,rank]) or NULL to recompute it.
+ * dx may be NULL (no input grad); grad_a/grad_b NULL when rank == 0. */
+FITQ_API size_t fitq_qlora_bwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank);
+FITQ_API int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int64_t m,
+                   const float* lora_a, const float* lora_b, int rank, float scale,
+                   const void* t_saved, void* dx, int dx_accumulate, float* grad_a,
+                   float* grad_b, int grad_accumulate, void* workspace, size_t workspace_bytes,
+                   fitq_stream_t stream);
+
+/* Decode / speculative-verify projection for M <= 64 rows: the NF4 weight is
+ * streamed once from HBM and dequantised in registers.  Same arithmetic
+ * contract as fitq_qlora_fwd. */
+FITQ_API size_t fitq_nf4_gemv_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank);
+FITQ_API int fitq_nf4_gemv(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                  const float* lora_b, int rank, float scale, const void* bias, void* y,
+                  const void* y_add, void* workspace, size_t workspace_bytes,
+                  fitq_stream_t stream);
+
+/* c[M,N] (bf16) = a[M,K].b[N,K]^T (+ c_add) on the tcgen05 tensor cores,
+ * fp32 accumulation.  K % 64 == 0, N % 16 == 0, rows 16-byte aligned. */
+FITQ_API int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, int64_t m,
+                      int64_t n, int64_t k, fitq_stream_t stream);
+
+/* AdamW over n fp32 values, in place on param/exp_avg/exp_avg_sq:
+ *   g = grad * clip;  m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2
+ *   param -= lr * (m/(1-b1^t) / (sqrt(v/(1-b2^t)) + eps) + wd * param)
+ * clip: device fp32 scalar from fitq_grad_clip_coef, or NULL for 1. */
+FITQ_API int fitq_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq,
+                    int64_t n, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, int step, const float* clip, fitq_stream_t stream);
+
+/* Global L2 norm of n fp32 values (all LoRA grads of a step, one flat
+ * buffer) -> norm_out[0], and the clip coefficient -> norm_out[1]:
+ * max_norm/(norm+1e-6) when max_norm > 0 and norm > max_norm, else 1
+ * (_clip_lora_accum_grads, fitllm/trainer.py:70-88).  Deterministic (fixed
+ * fp64 summation order).  workspace >= fitq_grad_norm_workspace(n) bytes. */
+FITQ_API size_t fitq_grad_norm_workspace(int64_t n);
+FITQ_API int fitq_grad_clip_coef(const float* grads, int64_t n, float max_norm, float* norm_out,
+                        void* workspace, size_t workspace_bytes, fitq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FITQ_H */

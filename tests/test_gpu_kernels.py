@@ -1,0 +1,156 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the CPU oracle.
+
+Bit-exact: NF4 dequant (bf16 and fp16, plain and transposed), NF4 quantise.
+Within the 1e-2 relative contract (||out - ref|| / ||ref||, bf16 in, fp32
+accumulate): the tcgen05 GEMM, the QLoRA forward (GEMM and GEMV paths) and the
+backward (dX, dA, dB).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nf4 as onf4
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2  # north-star output/gradient tolerance (relative Frobenius norm)
+
+
+def _state_to_device(st, dev):
+    from fitllm_b200.nf4 import QuantState
+    packed = torch.from_numpy(st.packed.copy()).to(dev).view(-1, 1)
+    qs = QuantState(
+        absmax=torch.from_numpy(st.absmax_code.copy()).to(dev),
+        shape=st.shape,
+        quant_map=torch.from_numpy(st.quant_map.copy()).to(dev),
+        nested_absmax=torch.from_numpy(st.nested_absmax.copy()).to(dev),
+        nested_quant_map=torch.from_numpy(st.nested_quant_map.copy()).to(dev),
+        offset=float(st.offset))
+    return packed, qs
+
+
+def _weights(n, k, seed, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(n, k, generator=g) * std).numpy().astype(np.float32)
+
+
+def _bf16(t):
+    return t.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("n,k", [(64, 64), (128, 320), (1024, 512), (192, 4096)])
+def test_dequant_bit_exact(cuda_dev, n, k):
+    from fitllm_b200.nf4 import dequantize_nf4
+    st = onf4.quantize(_weights(n, k, 10 + n))
+    packed, qs = _state_to_device(st, cuda_dev)
+    ref = onf4.dequant(st, "bf16")
+    out = dequantize_nf4(packed, qs, torch.bfloat16)
+    got = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.array_equal(got, ref)
+    ref16 = onf4.dequant(st, "f16")
+    out16 = dequantize_nf4(packed, qs, torch.float16)
+    assert np.array_equal(out16.view(torch.int16).cpu().numpy().view(np.uint16), ref16)
+    outt = dequantize_nf4(packed, qs, torch.bfloat16, transpose=True)
+    assert np.array_equal(outt.view(torch.int16).cpu().numpy().view(np.uint16), ref.T)
+
+
+def test_dequant_plain_absmax(cuda_dev):
+    """State without double quantisation (fp32 absmax)."""
+    from fitllm_b200.nf4 import QuantState, dequantize_nf4
+    n, k = 96, 256
+    w = _weights(n, k, 3)
+    st = onf4.quantize(w)
+    absmax = onf4.absmax_decode(st)
+    packed = torch.from_numpy(st.packed.copy()).to(cuda_dev)
+    qs = QuantState(absmax=torch.from_numpy(absmax).to(cuda_dev), shape=(n, k),
+                    quant_map=torch.from_numpy(st.quant_map.copy()).to(cuda_dev))
+    out = dequantize_nf4(packed, qs).view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.array_equal(out, onf4.dequant(st, "bf16"))
+
+
+@pytest.mark.parametrize("n,k", [(64, 64), (256, 1024), (333 * 64 // 64, 64 * 70)])
+def test_quantize_bit_exact(cuda_dev, n, k):
+    from fitllm_b200.nf4 import quantize_nf4
+    w = _weights(n, k, 100 + k)
+    w[0, :64] = 0.0  # an all-zero block
+    st = onf4.quantize(w)
+    packed, qs = quantize_nf4(torch.from_numpy(w).to(cuda_dev))
+    assert np.array_equal(packed.view(-1).cpu().numpy(), st.packed)
+    assert np.array_equal(qs.absmax.cpu().numpy(), st.absmax_code)
+    assert np.array_equal(qs.nested_absmax.cpu().numpy(), st.nested_absmax)
+    assert np.float32(qs.offset) == st.offset
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (1, 16, 64), (300, 272, 192),
+                                   (512, 1024, 512), (1000, 768, 1024)])
+def test_gemm_bf16_tn(cuda_dev, m, n, k):
+    from fitllm_b200.ops import gemm_bf16_tn
+    g = torch.Generator(device="cpu").manual_seed(m * 7 + n)
+    a = _bf16(torch.randn(m, k, generator=g)).to(cuda_dev)
+    b = _bf16(torch.randn(n, k, generator=g)).to(cuda_dev)
+    c = gemm_bf16_tn(a, b)
+    ref = a.float() @ b.float().T
+    assert onf4.rel_err(c.float().cpu().numpy(), ref.cpu().numpy()) < 4e-3
+    add = _bf16(torch.randn(m, n, generator=g)).to(cuda_dev)
+    c2 = gemm_bf16_tn(a, b, add)
+    assert onf4.rel_err(c2.float().cpu().numpy(), (ref + add.float()).cpu().numpy()) < 4e-3
+
+
+def _qlora_case(m, n, k, r, seed, dev):
+    from fitllm_b200.nf4 import Nf4WeightCRef
+    st = onf4.quantize(_weights(n, k, seed))
+    packed, qs = _state_to_device(st, dev)
+    w_deq = onf4.bf16_bits_to_f32(onf4.dequant(st, "bf16"))
+    g = torch.Generator().manual_seed(seed + 1)
+    bound = 1.0 / np.sqrt(k)  # kaiming_uniform(a=sqrt(5)) bound for a [r, k] weight
+    A = (torch.rand(r, k, generator=g) * 2 - 1) * bound if r else None
+    B = torch.randn(n, r, generator=g) * 0.01 if r else None
+    x = _bf16(torch.randn(m, k, generator=g))
+    dy = _bf16(torch.randn(m, n, generator=g))
+    return st, Nf4WeightCRef(packed, qs), w_deq, A, B, x, dy
+
+
+@pytest.mark.parametrize("m,n,k,r", [(512, 256, 512, 16), (200, 512, 256, 16), (130, 128, 128, 32),
+                                     (384, 1024, 640, 64), (256, 320, 256, 0)])
+def test_qlora_forward_backward(cuda_dev, m, n, k, r):
+    from fitllm_b200 import ops
+    s = 2.0
+    st, wref, w_deq, A, B, x, dy = _qlora_case(m, n, k, r, 7 + m, cuda_dev)
+    xd, dyd = x.to(cuda_dev), dy.to(cuda_dev)
+    Ad = A.to(cuda_dev) if r else None
+    Bd = B.to(cuda_dev) if r else None
+    y, t = ops.qlora_forward(xd, wref, Ad, Bd, s, want_t=True)
+    Anp = A.numpy() if r else np.zeros((0, k), np.float32)
+    Bnp = B.numpy() if r else np.zeros((n, 0), np.float32)
+    ref = onf4.qlora_forward(x.float().numpy(), w_deq, Anp, Bnp, s)
+    assert onf4.rel_err(y.float().cpu().numpy(), ref) < REL_TOL
+    dx, ga, gb = ops.qlora_backward(xd, dyd, wref, Ad, Bd, s, t_saved=t)
+    rdx, rda, rdb = onf4.qlora_backward(x.float().numpy(), w_deq, Anp, Bnp, s, dy.float().numpy())
+    assert onf4.rel_err(dx.float().cpu().numpy(), rdx) < REL_TOL
+    if r:
+        assert onf4.rel_err(ga.cpu().numpy(), rda) < REL_TOL
+        assert onf4.rel_err(gb.cpu().numpy(), rdb) < REL_TOL
+        # recompute of T inside the backward gives the same grads
+        dx2, ga2, gb2 = ops.qlora_backward(xd, dyd, wref, Ad, Bd, s, t_saved=None)
+        assert onf4.rel_err(ga2.cpu().numpy(), rda) < REL_TOL
+        assert onf4.rel_err(gb2.cpu().numpy(), rdb) < REL_TOL
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("m", [1, 4, 16, 40, 64])
+@pytest.mark.parametrize("n,k,r", [(256, 512, 16), (128, 1024, 0)])
+def test_gemv_paths(cuda_dev, m, n, k, r):
+    from fitllm_b200 import ops
+    s = 2.0
+    st, wref, w_deq, A, B, x, dy = _qlora_case(m, n, k, r, 31 + m, cuda_dev)
+    Ad = A.to(cuda_dev) if r else None
+    Bd = B.to(cuda_dev) if r else None
+    bias = _bf16(torch.randn(n) * 0.1)
+    y, _ = ops.qlora_forward(x.to(cuda_dev), wref, Ad, Bd, s, gemv=True, bias=bias.to(cuda_dev))
+    Anp = A.numpy() if r else np.zeros((0, k), np.float32)
+    Bnp = B.numpy() if r else np.zeros((n, 0), np.float32)
+    ref = onf4.qlora_forward(x.float().numpy(), w_deq, Anp, Bnp, s) + bias.float().numpy()[None, :]
+    assert onf4.rel_err(y.float().cpu().numpy(), ref) < REL_TOL
+    # the GEMM path on the same inputs agrees too
+    y2, _ = ops.qlora_forward(x.to(cuda_dev), wref, Ad, Bd, s, bias=bias.to(cuda_dev))
+    assert onf4.rel_err(y2.float().cpu().numpy(), ref) < REL_TOL
