@@ -1,0 +1,312 @@
+#!/usr/bin/env python
+"""QLoRA layer fwd+bwd tokens/s on a Qwen2.5-32B-shaped layer (B200).
+
+Workload (default, the headline configuration): one Qwen2.5-32B-shaped
+decoder layer (hidden 5120, 40/8 heads x 128, MLP 27648, RMSNorm, RoPE 1e6),
+all seven projections NF4 (blocksize 64, double-quantised absmax) from seeded
+N(0, 0.02) weights, LoRA r=16 / alpha=32 on q_proj and v_proj; one
+shard-stationary layer step = forward over the micro-batches (no autograd) +
+recompute-with-autograd + backward (dX, dA, dB) + the per-layer LoRA gradient
+all-reduce + global-norm clip + AdamW, over grad_accum = 16 micro-batches of
+1 x 2048 tokens (token ids uniform over vocab 152064, seeded; embeddings
+N(0, 0.02); upstream gradient N(0, 1) at the layer output).  The 16
+micro-batches are split across the N GPUs (fixed total work: strong scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fitq|reference]
+
+One JSON line on rank 0 (see the keys at the end of main()).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "QLoRA layer fwd+bwd tokens/s @Qwen2.5-32B shape"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="fitq", choices=["fitq", "reference"])
+    ap.add_argument("--microbatches", type=int, default=16)
+    ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seq", type=int, default=2048)
+    return ap.parse_args()
+
+
+def workload(a):
+    return {"workload": "qwen2.5-32b-layer-shard-stationary-fwd-bwd", "layers": 1,
+            "grad_accum_microbatches": a.microbatches, "seq_len": a.seq, "hidden": 5120,
+            "heads": 40, "kv_heads": 8, "intermediate": 27648, "lora_rank": 16, "lora_alpha": 32,
+            "lora_targets": ["q_proj", "v_proj"], "nf4_blocksize": 64, "double_quant": True,
+            "parallelism": f"microbatch-dp{a.gpus}",
+            "l2": "inputs larger than L2 (activations 335 MB per 16x2048 batch, weights 251.5 MB)"}
+
+
+# Algorithmic FLOPs per token (no recompute counted): projections 4*P_layer
+# (fwd 2P + dX 2P), LoRA 6r(N+K) for q and v, causal attention 3.5*2*S*d_model.
+def flops_per_token(seq: int) -> float:
+    p_layer = 487_587_840
+    lora = 6 * 16 * (5120 + 5120) + 6 * 16 * (1024 + 5120)
+    attn = 3.5 * 2 * seq * 5120
+    return 4 * p_layer + lora + attn
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        load = [s for s, p in zip(sm, pw) if p > 200] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def cpu_baseline(a, seq):
+    from oracle import layer_ref
+    r = layer_ref.time_cpu_step(seq=seq, microbatches=1)
+    return {"value": round(r["tokens_per_s"], 3), "unit": UNIT, "cores": r["threads"],
+            "kind": "port",
+            "sample": f"1 micro-batch x {seq} tokens through one layer step (fwd + recompute + bwd), "
+                      f"fp32 torch CPU restatement with oracle-dequantised NF4 weights; "
+                      f"{r['step_s']:.1f} s step (quantisation {r['quantize_s']:.1f} s untimed)"}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = cpu_baseline(a, a.cpu_seq)
+    vals = []
+    from oracle import layer_ref
+    import torch
+    w = layer_ref.build_layer(seed=0)
+    g = torch.Generator().manual_seed(5)
+    h = torch.randn(1, a.cpu_seq, 5120, generator=g).bfloat16().float()
+    go = torch.randn(1, a.cpu_seq, 5120, generator=g).bfloat16().float()
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        layer_ref.layer_step(w, h, go)
+        dt = time.perf_counter() - t0
+        if i >= a.warmup:
+            vals.append(a.cpu_seq / dt)
+    v = statistics.median(vals)
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT,
+           "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+           "ms_per_step": round(1000 * a.cpu_seq / v, 1), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": dict(workload(a), sample_microbatches=1, sample_seq=a.cpu_seq),
+           "cpu_baseline": {"kind": "port", "cores": base["cores"], "value": round(v, 3),
+                            "unit": UNIT, "sample": base["sample"]},
+           "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+
+    import torch
+    from fitllm_b200 import _lib
+    from fitllm_b200.distributed import (LoRAGradComm, barrier, init_from_env, max_over_ranks,
+                                         microbatch_range)
+    from fitllm_b200.engine import ShardStationaryEngine, build_synthetic_model
+    from fitllm_b200.layer import LayerConfig
+    from fitllm_b200.optimizer import ShardOptimizer
+
+    rank, world = init_from_env()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L = _lib.load()
+
+    cfg = LayerConfig.qwen25_32b()
+    sched, store = build_synthetic_model(cfg, 1, dev, seed=0)
+    comm = LoRAGradComm(store)
+    eng = ShardStationaryEngine(cfg, sched, store, dev, comm=comm)
+    opt = ShardOptimizer(store)
+
+    mb0, mb1 = microbatch_range(a.microbatches, rank, world)
+    nmb = mb1 - mb0
+    # Inputs: token ids -> embeddings (seeded, identical across N), upstream grad N(0,1).
+    g = torch.Generator(device=dev).manual_seed(5)
+    ids = torch.randint(0, cfg.vocab, (a.microbatches, a.seq), generator=g, device=dev)
+    g.manual_seed(6)
+    emb = torch.randn(cfg.vocab, cfg.hidden, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
+    h0 = emb[ids[mb0:mb1]].contiguous()
+    del emb, ids
+    g.manual_seed(7)
+    gout_all = torch.randn(a.microbatches, a.seq, cfg.hidden, generator=g, device=dev,
+                           dtype=torch.bfloat16)
+    gout = gout_all[mb0:mb1].contiguous()
+    del gout_all
+    torch.cuda.empty_cache()
+
+    def step():
+        store.zero_grad()
+        eng.step(h0, gout)
+        opt.step()
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if _lib.load().fitq_get_device_status(1, None) != 0:
+        raise RuntimeError("device status error after warm-up")
+
+    clocks = ClockSampler(local)
+    L.fitq_timing_enable(4096)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = L.fitq_launch_count()
+    s_ev = torch.cuda.Event(enable_timing=True)
+    e_ev = torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(a.steps):
+        step()
+    e_ev.record()
+    launches = L.fitq_launch_count() - launches0
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms_local = s_ev.elapsed_time(e_ev) / a.steps
+    import ctypes
+    nmax = 4096
+    ms_arr = (ctypes.c_float * nmax)()
+    fl_arr = (ctypes.c_double * nmax)()
+    n_t = L.fitq_timing_read(ms_arr, fl_arr, nmax)
+    L.fitq_timing_enable(0)
+    gemm_ms = sum(ms_arr[i] for i in range(n_t))
+    gemm_flops = sum(fl_arr[i] for i in range(n_t))
+    ms = max_over_ranks(ms_local, dev)
+    tokens = a.microbatches * a.seq
+    value = tokens / (ms / 1000.0)
+
+    # ---------------------------------------------------------------- e2e
+    e2e = None
+    if not a.no_e2e:
+        h_host = h0.cpu().pin_memory()
+        g_host = gout.cpu().pin_memory()
+        gin_host = torch.empty_like(h_host).pin_memory()
+        lora_host = torch.empty(store.per_layer, dtype=torch.float32).pin_memory()
+        shard_bytes = sched.layer_bytes(0)
+
+        def e2e_step():
+            sched.invalidate()  # the layer shard is uploaded from pinned host memory every step
+            hd = h_host.to(dev, non_blocking=True)
+            gd = g_host.to(dev, non_blocking=True)
+            store.zero_grad()
+            gin = eng.step(hd, gd)
+            opt.step()
+            gin_host.copy_(gin, non_blocking=True)
+            lora_host.copy_(store.layer_slice(store.grad, 0), non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        s2 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(a.steps):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(s2.elapsed_time(e2) / a.steps, dev)
+        e2e = {"value": round(tokens / (ms_e2e / 1000.0), 1), "unit": UNIT,
+               "h2d_bytes_per_step": int(shard_bytes + h_host.numel() * 2 + g_host.numel() * 2),
+               "d2h_bytes_per_step": int(gin_host.numel() * 2 + lora_host.numel() * 4),
+               "ms_per_step": round(ms_e2e, 3),
+               "note": "public API with pinned host buffers: layer shard H2D through the staging "
+                       "ring, hidden states and upstream grad H2D, input grad and LoRA grads D2H"}
+
+    if rank != 0:
+        return
+    peaks = {}
+    pk_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk_path):
+        peaks = json.load(open(pk_path))
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "of measured (bf16_tflops_sustained, kernel timed inside a long step)"
+    if peak is None:
+        peak, peak_src = 1400.0, "of fallback (sustained 1.4 PFLOP/s)"
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded NF4 weights, token ids, upstream grad)",
+        "config": workload(a),
+        "model_tflops": round(tokens * flops_per_token(a.seq) / (ms / 1000.0) / 1e12, 1),
+        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn_kernel (tcgen05)",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if achieved else None,
+                     "peak_source": peak_src, "traffic": None,
+                     "launches": n_t, "gemm_ms_per_step": round(gemm_ms / a.steps, 3),
+                     "gemm_share_of_step": round(gemm_ms / a.steps / ms, 3)},
+        "clocks": clk,
+        "gpu_launches": int(launches),
+        "e2e": e2e,
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(a, a.cpu_seq)
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

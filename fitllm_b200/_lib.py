@@ -51,6 +51,9 @@ SIGNATURES = {
     "fitq_adamw_step": (I32, [P, P, P, P, I64, F32, F32, F32, F32, F32, I32, P, P]),
     "fitq_grad_norm_workspace": (SZ, [I64]),
     "fitq_grad_clip_coef": (I32, [P, I64, F32, P, P, SZ, P]),
+    "fitq_timing_enable": (I32, [I32]),
+    "fitq_timing_read": (I32, [P, P, I32]),
+    "fitq_launch_count": (ctypes.c_longlong, []),
 }
 
 

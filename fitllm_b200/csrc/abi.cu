@@ -4,7 +4,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -489,3 +492,79 @@ int fitq_grad_clip_coef(const float* grads, int64_t n, float max_norm, float* no
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- launch timing
+// One process-wide table of CUDA event pairs (events are host handles; no
+// device memory is allocated).  Recording is off unless fitq_timing_enable()
+// was called with a positive capacity.
+namespace {
+struct TimingTable {
+  std::vector<cudaEvent_t> start, stop;
+  std::vector<double> flops;
+  int used = 0;
+  int capacity = 0;
+};
+TimingTable g_timing;
+std::mutex g_timing_mu;
+}  // namespace
+
+namespace fitq {
+int timing_begin(cudaStream_t st, double flops) {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  if (g_timing.used >= g_timing.capacity) return -1;
+  const int slot = g_timing.used++;
+  g_timing.flops[slot] = flops;
+  cudaEventRecord(g_timing.start[slot], st);
+  return slot;
+}
+void timing_end(int slot, cudaStream_t st) {
+  if (slot < 0) return;
+  cudaEventRecord(g_timing.stop[slot], st);
+}
+}  // namespace fitq
+
+extern "C" {
+
+int fitq_timing_enable(int capacity) {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  if (capacity < 0) return fail(FITQ_ERR_ARG, "timing: negative capacity");
+  if (static_cast<size_t>(capacity) > g_timing.start.size()) {
+    int code;
+    if (!current_sms(&code)) return code;
+    while (g_timing.start.size() < static_cast<size_t>(capacity)) {
+      cudaEvent_t a, b;
+      if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess)
+        return fail(FITQ_ERR_CUDA, "timing: cudaEventCreate failed");
+      g_timing.start.push_back(a);
+      g_timing.stop.push_back(b);
+      g_timing.flops.push_back(0.0);
+    }
+  }
+  g_timing.capacity = capacity;
+  g_timing.used = 0;
+  return FITQ_OK;
+}
+
+int fitq_timing_read(float* ms, double* flops, int max) {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  const int n = g_timing.used < max ? g_timing.used : max;
+  for (int i = 0; i < n; ++i) {
+    if (cudaEventSynchronize(g_timing.stop[i]) != cudaSuccess)
+      return -fail(FITQ_ERR_CUDA, "timing: event sync failed");
+    float t = 0.f;
+    cudaEventElapsedTime(&t, g_timing.start[i], g_timing.stop[i]);
+    if (ms) ms[i] = t;
+    if (flops) flops[i] = g_timing.flops[i];
+  }
+  return n;
+}
+
+}  // extern "C"
+
+namespace {
+std::atomic<long long> g_launches{0};
+}
+namespace fitq {
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace fitq
+extern "C" long long fitq_launch_count(void) { return g_launches.load(); }

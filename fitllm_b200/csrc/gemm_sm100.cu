@@ -313,7 +313,12 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   }
   const int tiles = p.num_m * p.num_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
+  const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *
+                       static_cast<double>(g.k + g.lora_k);
+  const int slot = timing_begin(st, flops);
   gemm_bf16_tn_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, p);
+  note_launch();
+  timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 

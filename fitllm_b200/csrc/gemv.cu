@@ -233,6 +233,7 @@ int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* part
       attr[T] = (e == cudaSuccess);                                                              \
     }                                                                                            \
     nf4_gemv_kernel<T><<<grid, kGemvWarps * 32, smem, st>>>(w, xb, M, per, partial);             \
+    note_launch();                                                                               \
     break;
   switch (mt) {
     FITQ_GEMV_CASE(1)
@@ -258,6 +259,7 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
       partial, splits, static_cast<int>(m), n, static_cast<const __nv_bfloat16*>(t_pad), lora_b,
       rank, scale, static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(y_add),
       static_cast<__nv_bfloat16*>(y));
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 

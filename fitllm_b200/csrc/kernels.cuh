@@ -75,6 +75,14 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
                        const float* lora_b, int rank, float scale, const void* bias,
                        const void* y_add, void* y, cudaStream_t st, int num_sms);
 
+// Launch timing of the tcgen05 GEMM (abi.cu): when enabled, CUDA events are
+// recorded on the launching stream around each launch.  timing_begin returns
+// a slot (or -1 when disabled / full); timing_end records the stop event.
+int timing_begin(cudaStream_t st, double flops);
+// Counts kernel launches made by the library (read by fitq_launch_count).
+void note_launch();
+void timing_end(int slot, cudaStream_t st);
+
 // Optimizer kernels (optim.cu).
 int launch_adamw(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
                  float b2, float eps, float wd, int step, const float* clip, cudaStream_t st);

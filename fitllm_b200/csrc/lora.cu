@@ -226,10 +226,10 @@ int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, con
   auto op = static_cast<__nv_bfloat16*>(out_pad);
   auto od = static_cast<__nv_bfloat16*>(out_dense);
   switch (r) {
-    case 16: lora_rowproj_kernel<16><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
-    case 32: lora_rowproj_kernel<32><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
-    case 48: lora_rowproj_kernel<48><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
-    case 64: lora_rowproj_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); break;
+    case 16: lora_rowproj_kernel<16><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 32: lora_rowproj_kernel<32><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 48: lora_rowproj_kernel<48><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 64: lora_rowproj_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
     default: return FITQ_ERR_UNSUPPORTED;
   }
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
@@ -251,8 +251,10 @@ int launch_lora_colproj(const void* p_pad, int64_t ld_p, const void* in, int64_t
   lora_colproj_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p_pad), ld_p,
                                             static_cast<const __nv_bfloat16*>(in), ld_in, M, D,
                                             rpc, r, partial_ws);
+  note_launch();
   lora_colproj_finish_kernel<<<grid_for(static_cast<int64_t>(r) * D, 256, num_sms), 256, 0, st>>>(
       partial_ws, nch, r, D, scale, res, layout, accumulate);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
@@ -260,18 +262,21 @@ int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, in
                            void* out_pad, cudaStream_t st) {
   pad_lora_weight_kernel<<<grid_for(rows * 64, 256, 148), 256, 0, st>>>(
       in, rows, r, scale, transpose_in, static_cast<__nv_bfloat16*>(out_pad));
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 int launch_f32_to_bf16_t(const float* in, int64_t rows, int cols, void* out, cudaStream_t st) {
   f32_to_bf16_t_kernel<<<grid_for(rows * cols, 256, 148), 256, 0, st>>>(
       in, rows, cols, static_cast<__nv_bfloat16*>(out));
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 int launch_f32_to_bf16(const float* in, int64_t n, void* out, cudaStream_t st) {
   f32_to_bf16_kernel<<<grid_for(n, 256, 148), 256, 0, st>>>(in, n,
                                                              static_cast<__nv_bfloat16*>(out));
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 

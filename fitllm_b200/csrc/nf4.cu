@@ -205,6 +205,7 @@ int launch_nf4_dequant(const Nf4Args& w, void* out, int out_dtype, int transpose
       nf4_dequant_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(w, (__nv_bfloat16*)out, items);
     else
       nf4_dequant_kernel<__half><<<grid, 256, 0, st>>>(w, (__half*)out, items);
+    note_launch();
   } else {
     const int64_t tiles = (w.n_out / 64) * (w.k_in / 64);
     const int grid = (int)(tiles < (int64_t)num_sms * 8 ? tiles : (int64_t)num_sms * 8);
@@ -212,6 +213,7 @@ int launch_nf4_dequant(const Nf4Args& w, void* out, int out_dtype, int transpose
       nf4_dequant_t_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(w, (__nv_bfloat16*)out);
     else
       nf4_dequant_t_kernel<__half><<<grid, 256, 0, st>>>(w, (__half*)out);
+    note_launch();
   }
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
@@ -224,12 +226,16 @@ int launch_nf4_quantize(const float* wt, int64_t n, const float* qmap, const flo
     const int64_t want = (nb + 7) / 8;
     const int grid = (int)(want < (int64_t)num_sms * 16 ? want : (int64_t)num_sms * 16);
     nf4_quant_blocks_kernel<<<grid, 256, 0, st>>>(wt, nb, qmap, packed, absmax_ws);
+    note_launch();
   }
   const int64_t nchunks = (nb + kOffsetChunk - 1) / kOffsetChunk;
   absmax_chunk_sum_kernel<<<(int)((nchunks + 127) / 128), 128, 0, st>>>(absmax_ws, nb, partial_ws);
+  note_launch();
   absmax_offset_kernel<<<1, 32, 0, st>>>(partial_ws, nchunks, nb, offset_out);
+  note_launch();
   const int64_t nn = (nb + 255) / 256;
   dq_quant_kernel<<<(int)nn, 256, 0, st>>>(absmax_ws, nb, nqmap, offset_out, codes, nested_absmax);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 

@@ -80,6 +80,7 @@ int launch_adamw(float* p, const float* g, float* m, float* v, int64_t n, float 
   adamw_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(p, g, m, v, n, lr, b1, omb1, b2, omb2,
                                                          eps, wd, static_cast<float>(bc1),
                                                          static_cast<float>(bc2), clip);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
@@ -92,8 +93,12 @@ int launch_grad_clip(const float* g, int64_t n, float max_norm, float* norm_out,
                      cudaStream_t st) {
   const int64_t parts = (n + kNormChunk - 1) / kNormChunk;
   double* partial = static_cast<double*>(ws);
-  if (parts > 0) sumsq_partial_kernel<<<static_cast<int>(parts), kNormThreads, 0, st>>>(g, n, partial);
+  if (parts > 0) {
+    sumsq_partial_kernel<<<static_cast<int>(parts), kNormThreads, 0, st>>>(g, n, partial);
+    note_launch();
+  }
   clip_finish_kernel<<<1, 32, 0, st>>>(partial, parts, max_norm, norm_out);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 

@@ -1,0 +1,192 @@
+"""Shard-stationary forward / backward over layers (FitLLM's training loop core).
+
+Follows ForwardEngine.shard_stationary_forward (fitllm/forward.py:408-541) and
+BackwardEngine.shard_stationary_backward (fitllm/backward.py:149-251):
+
+* forward: for each layer, load its shard ONCE and run every micro-batch
+  through it without autograd, keeping the boundary activation h_l;
+* backward, layers in reverse: reload the shard, recompute the layer forward
+  with autograd from h_l, back-propagate the upstream gradient, hand the
+  gradient w.r.t. h_l to the next layer down, and accumulate the LoRA
+  gradients of all micro-batches into that layer's gradient slice
+  (_accumulate_grads_to_ram, fitllm/backward.py:287-299).
+
+B200 differences (same mathematics):
+* the micro-batches of a rank are stacked along the batch dimension, so each
+  projection is ONE GEMM over all of them (optionally in chunks);
+* shards stream through the scheduler's pinned-host -> device ring, with the
+  next layer's upload overlapping the current layer's compute;
+* activations and gradients stay in HBM (180 GB) instead of round-tripping
+  through host memory per micro-batch;
+* LoRA gradients accumulate in place in a flat fp32 device buffer, and each
+  layer's slice is all-reduced across ranks as soon as its backward is queued;
+* the recompute uses the same dtype and attention mask as the forward
+  (the reference's recompute drops autocast and the mask,
+  fitllm/backward.py:222-231, which its own notes call a bug).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from .distributed import LoRAGradComm
+from .layer import DecoderLayer, LayerConfig, add_lora_, rotary_cos_sin
+from .nf4 import QuantState
+from .optimizer import LoRAStore
+from .qlora import Linear4bit, Params4bit, QLoRALinear4bit
+from .scheduler import ShardScheduler
+
+
+def layer_shard(layer: DecoderLayer) -> Dict[str, torch.Tensor]:
+    """The flat shard key set of one layer (fitllm/forward.py:95-109 layout),
+    adapter keys excluded."""
+    sd = {}
+    for k, v in layer.state_dict().items():
+        if "lora_A" in k or "lora_B" in k:
+            continue
+        sd[k.replace(".base_layer.", ".")] = v
+    return sd
+
+
+def bind_layer(layer: DecoderLayer, tensors: Dict[str, torch.Tensor], meta: Dict[str, dict]) -> None:
+    """Point the template layer's weights at one shard's device tensors (no copies).
+
+    The device-side counterpart of _reconstruct_layer_module +
+    _restore_bnb_quant_state (fitllm/forward.py:723-762, :76-109)."""
+    for name, mod in layer.projections():
+        base: Linear4bit = mod.base_layer if isinstance(mod, QLoRALinear4bit) else mod
+        key = name + ".weight"
+        m = meta[key]
+        qs = QuantState(
+            absmax=tensors[key + ".absmax"], shape=(int(m["shape"][0]), int(m["shape"][1])),
+            quant_map=tensors[key + ".quant_map"],
+            nested_absmax=tensors.get(key + ".nested_absmax"),
+            nested_quant_map=tensors.get(key + ".nested_quant_map"),
+            offset=float(m.get("nested_offset", 0.0)))
+        base.weight = Params4bit(tensors[key], qs)
+        base._wref = None
+        if base.bias is not None:
+            base.bias.data = tensors[name + ".bias"]
+    layer.input_layernorm.weight.data = tensors["input_layernorm.weight"]
+    layer.post_attention_layernorm.weight.data = tensors["post_attention_layernorm.weight"]
+
+
+def lora_entries(layer: DecoderLayer):
+    return [(n, tuple(p.shape)) for n, p in layer.named_parameters() if "lora_" in n]
+
+
+class ShardStationaryEngine:
+    def __init__(self, cfg: LayerConfig, scheduler: ShardScheduler, store: LoRAStore, device,
+                 comm: Optional[LoRAGradComm] = None, mb_chunk: Optional[int] = None):
+        self.cfg = cfg
+        self.scheduler = scheduler
+        self.store = store
+        self.device = torch.device(device)
+        self.comm = comm
+        self.mb_chunk = mb_chunk
+        self.layer = DecoderLayer(cfg, device=self.device)
+        add_lora_(self.layer, cfg.lora_rank, cfg.lora_alpha, cfg.lora_targets, seed=0)
+        self.layer.eval()
+        self._pe = None
+
+    @property
+    def num_layers(self) -> int:
+        return self.scheduler.num_layers
+
+    def position_embeddings(self, seq_len: int, dtype=torch.bfloat16):
+        if self._pe is None or self._pe[0].shape[0] != seq_len:
+            self._pe = rotary_cos_sin(seq_len, self.cfg.head_dim, self.cfg.rope_theta, self.device, dtype)
+        return self._pe
+
+    def _load(self, l: int) -> None:
+        t = self.scheduler.get_layer_tensors(l)
+        bind_layer(self.layer, t, self.scheduler.quant_meta(l))
+        self.store.bind(l, self.layer)
+
+    def _chunks(self, b: int):
+        c = self.mb_chunk or b
+        return [(i, min(b, i + c)) for i in range(0, b, c)]
+
+    @torch.no_grad()
+    def forward(self, h: torch.Tensor) -> List[torch.Tensor]:
+        """h: [B, S, hidden] bf16 (B stacked micro-batches).  Returns the L+1
+        boundary activations (activations[i] = hidden state before layer i)."""
+        pe = self.position_embeddings(h.shape[1], h.dtype)
+        acts = [h]
+        self.scheduler.prefetch(0)
+        for l in range(self.num_layers):
+            self.scheduler.prefetch(l + 1)
+            self._load(l)
+            out = torch.empty_like(h)
+            for a, b in self._chunks(h.shape[0]):
+                out[a:b] = self.layer(h[a:b], position_embeddings=pe)
+            self.scheduler.release(l)
+            h = out
+            acts.append(h)
+        return acts
+
+    def backward(self, acts: Sequence[torch.Tensor], grad_out: torch.Tensor) -> torch.Tensor:
+        """Reverse layer loop with recompute; accumulates LoRA grads into
+        store.grad (caller zeroes it per optimizer step) and returns the
+        gradient w.r.t. activations[0]."""
+        pe = self.position_embeddings(grad_out.shape[1], grad_out.dtype)
+        g = grad_out
+        L = self.num_layers
+        self.scheduler.prefetch(L - 1)
+        for l in reversed(range(L)):
+            self.scheduler.prefetch(l - 1)
+            self._load(l)
+            h_prev = acts[l]
+            g_in = torch.empty_like(h_prev)
+            for a, b in self._chunks(h_prev.shape[0]):
+                x = h_prev[a:b].detach().requires_grad_(True)
+                with torch.enable_grad():
+                    y = self.layer(x, position_embeddings=pe)
+                y.backward(g[a:b])
+                g_in[a:b] = x.grad
+                del x, y
+            self.scheduler.release(l)
+            if self.comm is not None:
+                self.comm.allreduce_layer(l)
+            g = g_in
+        if self.comm is not None:
+            self.comm.wait()
+        return g
+
+    def step(self, h: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
+        acts = self.forward(h)
+        return self.backward(acts, grad_out)
+
+
+def build_synthetic_model(cfg: LayerConfig, num_layers: int, device, seed: int = 0,
+                          ring_slots: int = 2, pin_memory: bool = True, lora_b_std: float = 0.01):
+    """Random-init NF4 layers (quantised on the device, per-layer seeds) loaded
+    into a pinned host store, plus a LoRAStore with PEFT-initialised adapters
+    (B ~ N(0, lora_b_std) so that dA is non-zero).  Returns (scheduler, store)."""
+    dev = torch.device(device)
+    sched = ShardScheduler(num_layers, dev, ring_slots=ring_slots, pin_memory=pin_memory)
+    proto = DecoderLayer(cfg, device=dev)
+    add_lora_(proto, cfg.lora_rank, cfg.lora_alpha, cfg.lora_targets, seed=0)
+    entries = lora_entries(proto)
+    store = LoRAStore(num_layers, entries, dev)
+    from .layer import quantize_layer_
+    for l in range(num_layers):
+        quantize_layer_(proto, seed=seed * 1000 + l)
+        sched.add_layer(l, layer_shard(proto))
+        # PEFT init per layer: A ~ U(-1/sqrt(K), 1/sqrt(K)) (Kaiming-uniform,
+        # a=sqrt(5)); B zeros, or N(0, lora_b_std) when lora_b_std > 0.
+        g = torch.Generator(device=dev).manual_seed(seed * 7919 + l)
+        vals = {}
+        for name, shape in entries:
+            if "lora_A" in name:
+                bound = 1.0 / (shape[1] ** 0.5)
+                vals[name] = (torch.rand(shape, generator=g, device=dev) * 2 - 1) * bound
+            elif lora_b_std > 0:
+                vals[name] = torch.randn(shape, generator=g, device=dev) * lora_b_std
+            else:
+                vals[name] = torch.zeros(shape, device=dev)
+        store.init_layer_(l, vals)
+    del proto
+    torch.cuda.empty_cache()
+    return sched, store

@@ -1,0 +1,189 @@
+"""Qwen2.5-32B-shaped decoder layer whose seven projections are NF4.
+
+The layer FitLLM drives through its shard-stationary loop is a HuggingFace
+``Qwen2DecoderLayer`` after QLoRA preparation (fitllm/model.py:209-267,
+fitllm/forward.py:657-701): RMSNorm, q/k/v (with bias) / o projections,
+RoPE (theta 1e6), causal GQA attention (40 query / 8 KV heads of 128),
+RMSNorm, SwiGLU MLP (27648).  This module keeps HF's attribute names
+(``self_attn.q_proj``, ``mlp.gate_proj``, ``input_layernorm`` ...) so the
+shard keys of fitllm/forward.py:95-109 load unchanged, and runs:
+
+* every projection as an NF4 ``Linear4bit`` / ``QLoRALinear4bit`` on the
+  sm_100a kernels (the residual adds of o_proj and down_proj ride in the GEMM
+  epilogue);
+* attention with torch SDPA (library kernel), norms / RoPE / SiLU as torch ops.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional, Sequence, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .qlora import Linear4bit, QLoRALinear4bit
+
+
+@dataclass
+class LayerConfig:
+    hidden: int = 5120
+    heads: int = 40
+    kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 27648
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    vocab: int = 152064
+    lora_rank: int = 16
+    lora_alpha: float = 32.0
+    lora_targets: Tuple[str, ...] = ("q_proj", "v_proj")
+
+    @classmethod
+    def qwen25_32b(cls, **kw) -> "LayerConfig":
+        return cls(**kw)
+
+    def proj_shapes(self):
+        """(name, N_out, K_in, has_bias) of the seven projections."""
+        h, q, kv, i = self.hidden, self.heads * self.head_dim, self.kv_heads * self.head_dim, self.intermediate
+        return [("self_attn.q_proj", q, h, True), ("self_attn.k_proj", kv, h, True),
+                ("self_attn.v_proj", kv, h, True), ("self_attn.o_proj", h, q, False),
+                ("mlp.gate_proj", i, h, False), ("mlp.up_proj", i, h, False),
+                ("mlp.down_proj", h, i, False)]
+
+    def nf4_weights_per_layer(self) -> int:
+        return sum(n * k for _, n, k, _ in self.proj_shapes())
+
+
+class RMSNorm(nn.Module):
+    """Qwen2RMSNorm: fp32 variance, weight applied after casting back."""
+
+    def __init__(self, hidden: int, eps: float, device=None, dtype=torch.bfloat16):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(hidden, device=device, dtype=dtype), requires_grad=False)
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return self.weight * xf.to(x.dtype)
+
+
+def rotary_cos_sin(seq_len: int, head_dim: int, theta: float, device, dtype=torch.bfloat16,
+                   position_ids: Optional[torch.Tensor] = None):
+    """(cos, sin) [S, head_dim] of the HF rotary embedding (rotate_half layout)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device, dtype=torch.float32) / head_dim))
+    pos = torch.arange(seq_len, device=device, dtype=torch.float32) if position_ids is None \
+        else position_ids.to(device, torch.float32)
+    freqs = torch.outer(pos, inv)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def apply_rotary(q, k, cos, sin):
+    # q: [B, H, S, D]; cos/sin: [S, D]
+    return q * cos + _rotate_half(q) * sin, k * cos + _rotate_half(k) * sin
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: LayerConfig, device=None):
+        super().__init__()
+        self.cfg = cfg
+        h, qd, kvd = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        self.q_proj = Linear4bit(h, qd, bias=True, device=device)
+        self.k_proj = Linear4bit(h, kvd, bias=True, device=device)
+        self.v_proj = Linear4bit(h, kvd, bias=True, device=device)
+        self.o_proj = Linear4bit(qd, h, bias=False, device=device)
+
+    def forward(self, x, residual, cos, sin, attn_mask: Optional[torch.Tensor] = None):
+        cfg = self.cfg
+        b, s, _ = x.shape
+        q = self.q_proj(x).view(b, s, cfg.heads, cfg.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        q, k = apply_rotary(q, k, cos, sin)
+        if attn_mask is None:
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        else:
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask, enable_gqa=True)
+        o = o.transpose(1, 2).reshape(b, s, cfg.heads * cfg.head_dim)
+        return self.o_proj(o, residual=residual)
+
+
+class MLP(nn.Module):
+    def __init__(self, cfg: LayerConfig, device=None):
+        super().__init__()
+        self.gate_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
+        self.up_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
+        self.down_proj = Linear4bit(cfg.intermediate, cfg.hidden, device=device)
+
+    def forward(self, x, residual):
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x), residual=residual)
+
+
+class DecoderLayer(nn.Module):
+    """h_out = h + o_proj(attn(norm(h)));  out = h_out + down(silu(gate) * up)(norm(h_out))."""
+
+    def __init__(self, cfg: LayerConfig, device=None):
+        super().__init__()
+        self.cfg = cfg
+        self.input_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps, device=device)
+        self.self_attn = Attention(cfg, device=device)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps, device=device)
+        self.mlp = MLP(cfg, device=device)
+
+    def forward(self, h: torch.Tensor, position_embeddings=None, attention_mask=None, **_):
+        if position_embeddings is None:
+            position_embeddings = rotary_cos_sin(h.shape[1], self.cfg.head_dim, self.cfg.rope_theta,
+                                                 h.device, h.dtype)
+        cos, sin = position_embeddings
+        h1 = self.self_attn(self.input_layernorm(h), h, cos, sin, attention_mask)
+        return self.mlp(self.post_attention_layernorm(h1), h1)
+
+    def projections(self):
+        for name, _, _, _ in self.cfg.proj_shapes():
+            yield name, self.get_submodule(name)
+
+    def lora_modules(self):
+        for name, mod in self.projections():
+            if isinstance(mod, QLoRALinear4bit):
+                yield name, mod
+
+
+def quantize_layer_(layer: DecoderLayer, seed: int, std: float = 0.02,
+                    bias_std: float = 0.02) -> None:
+    """Fill every projection with NF4 weights quantised on the device from
+    seeded N(0, std) fp32 values (biases N(0, bias_std) in bf16)."""
+    dev = layer.input_layernorm.weight.device
+    g = torch.Generator(device=dev)
+    for i, (name, n, k, has_bias) in enumerate(layer.cfg.proj_shapes()):
+        mod = layer.get_submodule(name)
+        base = mod.base_layer if isinstance(mod, QLoRALinear4bit) else mod
+        g.manual_seed(seed * 100 + i)
+        w = torch.randn(n, k, generator=g, device=dev, dtype=torch.float32) * std
+        fresh = Linear4bit.from_float(w, None)
+        del w
+        base.set_quantized(fresh.weight.data, fresh.quant_state)
+        if has_bias:
+            base.bias.data.copy_((torch.randn(n, generator=g, device=dev) * bias_std).to(base.bias.dtype))
+
+
+def add_lora_(layer: DecoderLayer, rank: int, alpha: float, targets: Sequence[str], seed: int,
+              b_std: float = 0.0) -> None:
+    """Wrap the target projections with rank-r adapters (PEFT init: A
+    Kaiming-uniform, B zeros, or N(0, b_std) when b_std > 0 so that dA != 0)."""
+    for i, (name, mod) in enumerate(list(layer.projections())):
+        short = name.rsplit(".", 1)[-1]
+        if short in targets and isinstance(mod, Linear4bit):
+            parent = layer.get_submodule(name.rsplit(".", 1)[0])
+            torch.manual_seed(seed * 1000 + i)
+            q = QLoRALinear4bit(mod, r=rank, lora_alpha=alpha)
+            if b_std > 0:
+                with torch.no_grad():
+                    q.lora_B["default"].weight.normal_(0.0, b_std)
+            setattr(parent, short, q)

@@ -1,0 +1,176 @@
+"""Shard upload path: pinned host store -> copy stream -> K-slot device ring.
+
+Replaces the per-tensor ``.to(device, non_blocking)`` upload of
+``ShardScheduler._transfer_to_gpu`` / ``get_layer_tensors``
+(fitllm/scheduler.py:162-178, :259-290) and its per-eviction
+``empty_cache``/``gc`` (fitllm/scheduler.py:317-324, :440-456), following the
+resident-pinned-weights design the reference documents for itself
+(EFFICIENT_TRAINING.md:81-193):
+
+* every layer's shard (the flat key set of fitllm/forward.py:95-109) lives in
+  ONE pinned host arena, each tensor at a 256-byte aligned offset;
+* ``prefetch(l)`` issues one ``cudaMemcpyAsync`` of the whole arena on a
+  dedicated copy stream into ring slot ``l % K`` once the compute stream has
+  released that slot (event), so layer l+1 uploads while layer l computes;
+* ``get_layer_tensors(l)`` makes the compute stream wait on the slot's ready
+  event and returns device views with the same keys -- no allocation, no
+  cache eviction, no synchronisation in the loop.
+
+LoRA keys found in a shard are dropped, as fitllm/forward.py:733-734 does.
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+_ALIGN = 256
+
+
+@dataclass
+class _Entry:
+    key: str
+    offset: int
+    nbytes: int
+    dtype: torch.dtype
+    shape: Tuple[int, ...]
+
+
+def _layout(tensors: Dict[str, torch.Tensor]) -> Tuple[List[_Entry], int]:
+    entries, off = [], 0
+    for k in sorted(tensors):
+        t = tensors[k]
+        off = (off + _ALIGN - 1) // _ALIGN * _ALIGN
+        nb = t.numel() * t.element_size()
+        entries.append(_Entry(k, off, nb, t.dtype, tuple(t.shape)))
+        off += nb
+    return entries, (off + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+def _views(buf: torch.Tensor, entries: List[_Entry]) -> Dict[str, torch.Tensor]:
+    out = {}
+    for e in entries:
+        raw = buf[e.offset:e.offset + e.nbytes]
+        out[e.key] = raw.view(e.dtype).view(e.shape) if e.nbytes else torch.empty(e.shape, dtype=e.dtype, device=buf.device)
+    return out
+
+
+class ShardScheduler:
+    """Pinned host store + device staging ring for layer shards."""
+
+    def __init__(self, num_layers: int, device, ring_slots: int = 2, pin_memory: bool = True):
+        if ring_slots < 1:
+            raise ValueError("ring_slots must be >= 1")
+        self.num_layers = num_layers
+        self.device = torch.device(device)
+        self.ring_slots = ring_slots
+        self.pin_memory = pin_memory
+        self._host: Dict[int, torch.Tensor] = {}
+        self._layout: Dict[int, List[_Entry]] = {}
+        self._meta: Dict[int, Dict[str, dict]] = {}
+        self._slot_bytes = 0
+        self._slots: List[Optional[torch.Tensor]] = [None] * ring_slots
+        self._slot_layer: List[int] = [-1] * ring_slots
+        self._ready: List[Optional[torch.cuda.Event]] = [None] * ring_slots
+        self._free: List[Optional[torch.cuda.Event]] = [None] * ring_slots
+        self._copy_stream: Optional[torch.cuda.Stream] = None
+        self.h2d_bytes = 0
+
+    # ---------------------------------------------------------------- host side
+    def add_layer(self, layer_idx: int, tensors: Dict[str, torch.Tensor]) -> int:
+        """Copy one layer's flat key set into its pinned host arena.  Returns bytes."""
+        base = {k: v for k, v in tensors.items() if "lora_A" not in k and "lora_B" not in k}
+        meta = {}
+        for k in list(base):
+            if k.endswith("quant_state.bitsandbytes__nf4"):
+                meta[k[: -len(".quant_state.bitsandbytes__nf4")]] = json.loads(
+                    bytes(base[k].cpu().tolist()).decode("utf-8"))
+        entries, total = _layout(base)
+        arena = torch.empty(total, dtype=torch.uint8, pin_memory=self.pin_memory)
+        views = _views(arena, entries)
+        for k, t in base.items():
+            views[k].copy_(t.detach().cpu().view(views[k].dtype).view(views[k].shape))
+        self._host[layer_idx] = arena
+        self._layout[layer_idx] = entries
+        self._meta[layer_idx] = meta
+        self._slot_bytes = max(self._slot_bytes, total)
+        return total
+
+    def layer_bytes(self, layer_idx: int) -> int:
+        return int(self._host[layer_idx].numel())
+
+    def host_tensors(self, layer_idx: int) -> Dict[str, torch.Tensor]:
+        return _views(self._host[layer_idx], self._layout[layer_idx])
+
+    def quant_meta(self, layer_idx: int) -> Dict[str, dict]:
+        """Parsed ``<param>.quant_state.bitsandbytes__nf4`` metadata (host, no sync)."""
+        return self._meta[layer_idx]
+
+    # ---------------------------------------------------------------- device ring
+    def _ensure_ring(self):
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        for s in range(self.ring_slots):
+            if self._slots[s] is None or self._slots[s].numel() < self._slot_bytes:
+                self._slots[s] = torch.empty(self._slot_bytes, dtype=torch.uint8, device=self.device)
+                self._slot_layer[s] = -1
+                self._ready[s] = torch.cuda.Event()
+                self._free[s] = None
+
+    def slot_of(self, layer_idx: int) -> int:
+        return layer_idx % self.ring_slots
+
+    def prefetch(self, layer_idx: int) -> None:
+        """Start the async upload of a layer into its ring slot (idempotent)."""
+        if layer_idx < 0 or layer_idx >= self.num_layers:
+            return
+        self._ensure_ring()
+        s = self.slot_of(layer_idx)
+        if self._slot_layer[s] == layer_idx:
+            return
+        cs = self._copy_stream
+        if self._free[s] is not None:
+            cs.wait_event(self._free[s])
+        else:  # slot never released: wait for everything queued so far
+            cs.wait_stream(torch.cuda.current_stream(self.device))
+        self._free[s] = None
+        src = self._host[layer_idx]
+        with torch.cuda.stream(cs):
+            self._slots[s][: src.numel()].copy_(src, non_blocking=True)
+            self._ready[s].record(cs)
+        self._slot_layer[s] = layer_idx
+        self.h2d_bytes += src.numel()
+
+    def get_layer_tensors(self, layer_idx: int, verify_checksums: bool = False) -> Dict[str, torch.Tensor]:
+        """Device views of the layer's tensors; the current stream waits for the upload."""
+        self.prefetch(layer_idx)
+        s = self.slot_of(layer_idx)
+        torch.cuda.current_stream(self.device).wait_event(self._ready[s])
+        return _views(self._slots[s], self._layout[layer_idx])
+
+    def release(self, layer_idx: int) -> None:
+        """Mark the slot reusable once the work queued so far on the current stream is done."""
+        s = self.slot_of(layer_idx)
+        if self._slot_layer[s] != layer_idx:
+            return
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._free[s] = ev
+
+    def invalidate(self) -> None:
+        """Forget which layers the ring holds, so the next get re-uploads."""
+        self._slot_layer = [-1] * self.ring_slots
+
+    # reference-compatible names
+    def prefetch_to_cpu(self, layer_idx: int, verify_checksums: bool = False) -> None:
+        """The host store is resident; warm the device ring instead."""
+        self.prefetch(layer_idx)
+
+    def evict_layer_from_gpu(self, layer_idx: int) -> None:
+        self.release(layer_idx)
+
+    def synchronize(self) -> None:
+        if self._copy_stream is not None:
+            self._copy_stream.synchronize()

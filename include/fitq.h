@@ -173,6 +173,18 @@ FITQ_API size_t fitq_grad_norm_workspace(int64_t n);
 FITQ_API int fitq_grad_clip_coef(const float* grads, int64_t n, float max_norm, float* norm_out,
                         void* workspace, size_t workspace_bytes, fitq_stream_t stream);
 
+/* Launch timing of the tcgen05 GEMM kernel (measurement aid, host-side only):
+ * fitq_timing_enable(capacity) starts recording a CUDA event pair on the
+ * launching stream around each GEMM launch (up to `capacity` launches; 0
+ * stops).  fitq_timing_read waits for the recorded events and writes, per
+ * launch, the device time in ms and the launch's algorithmic FLOPs
+ * (2.M.N.(K + lora_k)); it returns the number of launches (<= max). */
+FITQ_API int fitq_timing_enable(int capacity);
+FITQ_API int fitq_timing_read(float* ms, double* flops, int max);
+
+/* Number of kernels this library has launched in this process so far. */
+FITQ_API long long fitq_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

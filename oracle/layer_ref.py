@@ -1,0 +1,126 @@
+"""CPU restatement of one shard-stationary QLoRA layer step -- TEST / BASELINE
+INFRASTRUCTURE ONLY (tests, __graft_entry__.smoke and bench.py's CPU legs).
+
+What it restates: FitLLM's per-layer work in a training step
+(fitllm/forward.py:480-528 forward without autograd, then
+fitllm/backward.py:206-249 recompute-with-autograd + backward) for a
+Qwen2.5-32B-shaped decoder layer whose projections are NF4 (bitsandbytes
+dequant arithmetic, via the C oracle) with PEFT LoRA on q/v (dropout inactive),
+computed in fp32 on the host cores with torch CPU ops.
+"""
+from __future__ import annotations
+
+import math
+import os
+import time
+from typing import Dict, Tuple
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import nf4 as onf4
+
+PROJ = [("q_proj", "q", True), ("k_proj", "kv", True), ("v_proj", "kv", True),
+        ("o_proj", "o", False), ("gate_proj", "i", False), ("up_proj", "i", False),
+        ("down_proj", "d", False)]
+
+
+def proj_shape(kind: str, hidden: int, heads: int, kv_heads: int, head_dim: int, inter: int):
+    return {"q": (heads * head_dim, hidden), "kv": (kv_heads * head_dim, hidden),
+            "o": (hidden, heads * head_dim), "i": (inter, hidden), "d": (hidden, inter)}[kind]
+
+
+def build_layer(hidden=5120, heads=40, kv_heads=8, head_dim=128, inter=27648, rank=16,
+                alpha=32.0, seed=0) -> Dict[str, torch.Tensor]:
+    """Seeded N(0,0.02) weights -> NF4 (C oracle) -> dequantised fp32 weights
+    (the exact bf16 values bitsandbytes' dequant produces), plus LoRA A/B."""
+    w = {}
+    g = torch.Generator().manual_seed(seed)
+    for name, kind, bias in PROJ:
+        n, k = proj_shape(kind, hidden, heads, kv_heads, head_dim, inter)
+        dense = (torch.randn(n, k, generator=g) * 0.02).numpy()
+        st = onf4.quantize(dense)
+        w[name] = torch.from_numpy(onf4.bf16_bits_to_f32(onf4.dequant(st, "bf16")))
+        if bias:
+            w[name + ".bias"] = (torch.randn(n, generator=g) * 0.02).bfloat16().float()
+    for name in ("q_proj", "v_proj"):
+        n, k = w[name].shape
+        w[name + ".lora_A"] = (torch.rand(rank, k, generator=g) * 2 - 1) / math.sqrt(k)
+        w[name + ".lora_B"] = torch.randn(n, rank, generator=g) * 0.01
+    w["scale"] = torch.tensor(alpha / rank)
+    w["cfg"] = torch.tensor([hidden, heads, kv_heads, head_dim, inter])
+    return w
+
+
+def _rms(x, eps=1e-6):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+
+
+def _rope(seq, head_dim, theta=1e6):
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    f = torch.outer(torch.arange(seq, dtype=torch.float32), inv)
+    e = torch.cat([f, f], -1)
+    return e.cos(), e.sin()
+
+
+def _rot(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), -1)
+
+
+def layer_forward(w, h):
+    hidden, heads, kv_heads, head_dim, inter = [int(v) for v in w["cfg"]]
+    s = float(w["scale"])
+    b, S, _ = h.shape
+
+    def lin(name, x):
+        y = x @ w[name].T
+        if name + ".bias" in w:
+            y = y + w[name + ".bias"]
+        if name + ".lora_A" in w:
+            y = y + s * (x @ w[name + ".lora_A"].T) @ w[name + ".lora_B"].T
+        return y
+
+    x = _rms(h)
+    q = lin("q_proj", x).view(b, S, heads, head_dim).transpose(1, 2)
+    k = lin("k_proj", x).view(b, S, kv_heads, head_dim).transpose(1, 2)
+    v = lin("v_proj", x).view(b, S, kv_heads, head_dim).transpose(1, 2)
+    cos, sin = _rope(S, head_dim)
+    q, k = q * cos + _rot(q) * sin, k * cos + _rot(k) * sin
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+    h1 = h + lin("o_proj", o.transpose(1, 2).reshape(b, S, heads * head_dim))
+    x2 = _rms(h1)
+    return h1 + lin("down_proj", F.silu(lin("gate_proj", x2)) * lin("up_proj", x2))
+
+
+def layer_step(w, h, grad_out) -> Tuple[torch.Tensor, Dict[str, torch.Tensor]]:
+    """Shard-stationary per-layer work: forward (no autograd), recompute with
+    autograd, backward.  Returns (grad wrt h, LoRA grads)."""
+    with torch.no_grad():
+        layer_forward(w, h)
+    params = {k: w[k].clone().requires_grad_(True) for k in w if "lora_" in k}
+    ww = dict(w)
+    ww.update(params)
+    x = h.clone().requires_grad_(True)
+    y = layer_forward(ww, x)
+    y.backward(grad_out)
+    return x.grad, {k: p.grad for k, p in params.items()}
+
+
+def time_cpu_step(seq=2048, microbatches=1, seed=0, threads=None) -> Dict[str, float]:
+    """Time one layer step on the host cores; returns tokens/s and details."""
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    t0 = time.perf_counter()
+    w = build_layer(seed=seed)
+    t_build = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(seed + 5)
+    hidden = int(w["cfg"][0])
+    h = torch.randn(microbatches, seq, hidden, generator=g).bfloat16().float()
+    go = torch.randn(microbatches, seq, hidden, generator=g).bfloat16().float()
+    t0 = time.perf_counter()
+    layer_step(w, h, go)
+    dt = time.perf_counter() - t0
+    return {"tokens_per_s": microbatches * seq / dt, "step_s": dt, "threads": threads,
+            "quantize_s": t_build, "tokens": microbatches * seq}

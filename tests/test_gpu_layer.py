@@ -1,0 +1,242 @@
+"""GPU parity of the module API, the decoder layer and the shard-stationary
+engine against the CPU restatement (oracle/layer_ref.py), on small shapes.
+
+Weights are quantised by the C oracle on the host and loaded through the
+bitsandbytes flat shard keys (fitllm/forward.py:95-109 layout), so these tests
+also cover QuantState (de)serialisation and the scheduler's pinned ring.
+Tolerance: 1e-2 relative Frobenius norm (bf16 operands, fp32 accumulation),
+the north-star contract for outputs and gradients.
+"""
+import json
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import layer_ref
+from oracle import nf4 as onf4
+
+pytestmark = pytest.mark.gpu
+REL = 1e-2
+
+SMALL = dict(hidden=256, heads=4, kv_heads=2, head_dim=64, inter=512)
+
+
+def _cfg():
+    from fitllm_b200.layer import LayerConfig
+    return LayerConfig(hidden=SMALL["hidden"], heads=SMALL["heads"], kv_heads=SMALL["kv_heads"],
+                       head_dim=SMALL["head_dim"], intermediate=SMALL["inter"], lora_rank=16,
+                       lora_alpha=32.0, lora_targets=("q_proj", "v_proj"))
+
+
+def _oracle_shard(seed):
+    """(flat shard dict for my layer, oracle weight dict) built from one seed."""
+    g = torch.Generator().manual_seed(seed)
+    shard, ref = {}, {}
+    names = {"q_proj": "self_attn", "k_proj": "self_attn", "v_proj": "self_attn",
+             "o_proj": "self_attn", "gate_proj": "mlp", "up_proj": "mlp", "down_proj": "mlp"}
+    for name, kind, bias in layer_ref.PROJ:
+        n, k = layer_ref.proj_shape(kind, SMALL["hidden"], SMALL["heads"], SMALL["kv_heads"],
+                                    SMALL["head_dim"], SMALL["inter"])
+        st = onf4.quantize((torch.randn(n, k, generator=g) * 0.02).numpy())
+        key = f"{names[name]}.{name}.weight"
+        shard[key] = torch.from_numpy(st.packed.copy()).view(-1, 1)
+        shard[key + ".absmax"] = torch.from_numpy(st.absmax_code.copy())
+        shard[key + ".quant_map"] = torch.from_numpy(st.quant_map.copy())
+        shard[key + ".nested_absmax"] = torch.from_numpy(st.nested_absmax.copy())
+        shard[key + ".nested_quant_map"] = torch.from_numpy(st.nested_quant_map.copy())
+        meta = {"quant_type": "nf4", "blocksize": 64, "dtype": "bfloat16", "shape": [n, k],
+                "nested_blocksize": 256, "nested_dtype": "float32", "nested_offset": float(st.offset)}
+        shard[key + ".quant_state.bitsandbytes__nf4"] = torch.tensor(
+            list(json.dumps(meta).encode()), dtype=torch.uint8)
+        ref[name] = torch.from_numpy(onf4.bf16_bits_to_f32(onf4.dequant(st, "bf16")))
+        if bias:
+            b = (torch.randn(n, generator=g) * 0.02).bfloat16()
+            shard[f"{names[name]}.{name}.bias"] = b
+            ref[name + ".bias"] = b.float()
+    shard["input_layernorm.weight"] = torch.ones(SMALL["hidden"], dtype=torch.bfloat16)
+    shard["post_attention_layernorm.weight"] = torch.ones(SMALL["hidden"], dtype=torch.bfloat16)
+    for name in ("q_proj", "v_proj"):
+        n, k = ref[name].shape
+        ref[name + ".lora_A"] = (torch.rand(16, k, generator=g) * 2 - 1) / math.sqrt(k)
+        ref[name + ".lora_B"] = torch.randn(n, 16, generator=g) * 0.02
+    ref["scale"] = torch.tensor(2.0)
+    ref["cfg"] = torch.tensor([SMALL["hidden"], SMALL["heads"], SMALL["kv_heads"],
+                               SMALL["head_dim"], SMALL["inter"]])
+    return shard, ref
+
+
+def _layer_from_shard(shard, ref, dev):
+    from fitllm_b200.layer import DecoderLayer, add_lora_
+    layer = DecoderLayer(_cfg(), device=dev)
+    missing, unexpected = layer.load_state_dict({k: v for k, v in shard.items()}, strict=False)
+    add_lora_(layer, 16, 32.0, ("q_proj", "v_proj"), seed=0)
+    with torch.no_grad():
+        for name in ("q_proj", "v_proj"):
+            mod = layer.self_attn.get_submodule(name)
+            mod.lora_A["default"].weight.copy_(ref[name + ".lora_A"])
+            mod.lora_B["default"].weight.copy_(ref[name + ".lora_B"])
+    return layer
+
+
+def test_qlora_linear_module_autograd(cuda_dev):
+    from fitllm_b200.qlora import Linear4bit, QLoRALinear4bit, QLoRAManager
+    n, k, m = 384, 512, 200
+    g = torch.Generator().manual_seed(3)
+    st = onf4.quantize((torch.randn(n, k, generator=g) * 0.02).numpy())
+    w = onf4.bf16_bits_to_f32(onf4.dequant(st, "bf16"))
+    lin = Linear4bit(k, n, bias=True, device=cuda_dev)
+    sd = {"weight": torch.from_numpy(st.packed.copy()).view(-1, 1),
+          "weight.absmax": torch.from_numpy(st.absmax_code.copy()),
+          "weight.quant_map": torch.from_numpy(st.quant_map.copy()),
+          "weight.nested_absmax": torch.from_numpy(st.nested_absmax.copy()),
+          "weight.nested_quant_map": torch.from_numpy(st.nested_quant_map.copy()),
+          "weight.quant_state.bitsandbytes__nf4": torch.tensor(list(json.dumps(
+              {"quant_type": "nf4", "blocksize": 64, "dtype": "bfloat16", "shape": [n, k],
+               "nested_blocksize": 256, "nested_dtype": "float32",
+               "nested_offset": float(st.offset)}).encode()), dtype=torch.uint8),
+          "bias": (torch.randn(n, generator=g) * 0.1).bfloat16()}
+    lin.load_state_dict(sd)
+    # dequantised values through the module are the oracle's bits
+    assert np.array_equal(lin.dequantize().view(torch.int16).cpu().numpy().view(np.uint16),
+                          onf4.dequant(st, "bf16"))
+    # state_dict round trip keeps the flat key set
+    sd2 = lin.state_dict()
+    assert set(sd2) == set(sd)
+    q = QLoRALinear4bit(lin, r=16, lora_alpha=32.0)
+    with torch.no_grad():
+        q.lora_B["default"].weight.normal_(0, 0.02)
+    x = torch.randn(m, k, generator=g).bfloat16().to(cuda_dev).requires_grad_(True)
+    y = q(x)
+    dy = torch.randn(m, n, generator=g).bfloat16().to(cuda_dev)
+    y.backward(dy)
+    A = q.lora_A["default"].weight.detach().cpu().numpy()
+    B = q.lora_B["default"].weight.detach().cpu().numpy()
+    bias = sd["bias"].float().numpy()
+    ry = onf4.qlora_forward(x.detach().float().cpu().numpy(), w, A, B, 2.0) + bias
+    assert onf4.rel_err(y.detach().float().cpu().numpy(), ry) < REL
+    rdx, rda, rdb = onf4.qlora_backward(x.detach().float().cpu().numpy(), w, A, B, 2.0,
+                                        dy.float().cpu().numpy())
+    assert onf4.rel_err(x.grad.float().cpu().numpy(), rdx) < REL
+    assert onf4.rel_err(q.lora_A["default"].weight.grad.cpu().numpy(), rda) < REL
+    assert onf4.rel_err(q.lora_B["default"].weight.grad.cpu().numpy(), rdb) < REL
+    assert lin.weight.grad is None and lin.bias.grad is None
+    mgr = QLoRAManager(rank=16, alpha=32.0, targets=("q_proj",))
+    assert "lora_A.default.weight" in dict(q.named_parameters())
+
+
+def test_lora_linear_own_layout_on_nf4(cuda_dev):
+    """fitllm/lora.py layout (A [in, r], B [r, out]) over an NF4 base."""
+    from fitllm_b200.lora import LoRALinear
+    from fitllm_b200.qlora import Linear4bit
+    n, k, m = 256, 256, 96
+    g = torch.Generator(device=cuda_dev).manual_seed(1)
+    base = Linear4bit.from_float(torch.randn(n, k, generator=g, device=cuda_dev) * 0.02)
+    lora = LoRALinear(base, rank=16, alpha=32.0)
+    with torch.no_grad():
+        lora.lora_B.normal_(0, 0.02)
+    x = torch.randn(m, k, device=cuda_dev).bfloat16().requires_grad_(True)
+    y = lora(x)
+    w = base.dequantize().float()
+    ref = x.detach().float() @ w.T + 2.0 * (x.detach().float() @ lora.lora_A.detach()) @ lora.lora_B.detach()
+    assert onf4.rel_err(y.detach().float().cpu().numpy(), ref.cpu().numpy()) < REL
+    y.float().sum().backward()
+    assert lora.lora_A.grad is not None and lora.lora_B.grad is not None
+    assert lora.lora_A.grad.shape == (k, 16) and lora.lora_B.grad.shape == (16, n)
+
+
+def test_decoder_layer_vs_restatement(cuda_dev):
+    shard, ref = _oracle_shard(11)
+    layer = _layer_from_shard(shard, ref, cuda_dev)
+    g = torch.Generator().manual_seed(12)
+    h = torch.randn(2, 128, SMALL["hidden"], generator=g).bfloat16()
+    go = torch.randn(2, 128, SMALL["hidden"], generator=g).bfloat16()
+    hd = h.to(cuda_dev).requires_grad_(True)
+    y = layer(hd)
+    y.backward(go.to(cuda_dev))
+    rgx, rg = layer_ref.layer_step(ref, h.float(), go.float())
+    ry = layer_ref.layer_forward(ref, h.float())
+    assert onf4.rel_err(y.detach().float().cpu().numpy(), ry.detach().numpy()) < REL
+    assert onf4.rel_err(hd.grad.float().cpu().numpy(), rgx.numpy()) < REL
+    for name in ("q_proj", "v_proj"):
+        mod = layer.self_attn.get_submodule(name)
+        assert onf4.rel_err(mod.lora_A["default"].weight.grad.cpu().numpy(),
+                            rg[name + ".lora_A"].numpy()) < REL
+        assert onf4.rel_err(mod.lora_B["default"].weight.grad.cpu().numpy(),
+                            rg[name + ".lora_B"].numpy()) < REL
+
+
+def test_engine_two_layers_vs_restatement(cuda_dev):
+    """Shard-stationary forward + recompute backward over 2 layers streamed
+    through the pinned host ring, LoRA grads accumulated in the flat store."""
+    from fitllm_b200.engine import ShardStationaryEngine, lora_entries
+    from fitllm_b200.layer import DecoderLayer, add_lora_
+    from fitllm_b200.optimizer import LoRAStore
+    from fitllm_b200.scheduler import ShardScheduler
+    cfg = _cfg()
+    shards, refs = [], []
+    for l in range(2):
+        s, r = _oracle_shard(20 + l)
+        shards.append(s)
+        refs.append(r)
+    sched = ShardScheduler(2, cuda_dev, ring_slots=2)
+    for l in range(2):
+        sched.add_layer(l, shards[l])
+    proto = DecoderLayer(cfg, device=cuda_dev)
+    add_lora_(proto, 16, 32.0, cfg.lora_targets, seed=0)
+    store = LoRAStore(2, lora_entries(proto), cuda_dev)
+    for l in range(2):
+        store.init_layer_(l, {f"self_attn.{n}.lora_{ab}.default.weight": refs[l][f"{n}.lora_{ab}"]
+                              for n in ("q_proj", "v_proj") for ab in ("A", "B")})
+    eng = ShardStationaryEngine(cfg, sched, store, cuda_dev, mb_chunk=1)
+    g = torch.Generator().manual_seed(30)
+    h = torch.randn(3, 64, SMALL["hidden"], generator=g).bfloat16()
+    go = torch.randn(3, 64, SMALL["hidden"], generator=g).bfloat16()
+    store.zero_grad()
+    acts = eng.forward(h.to(cuda_dev))
+    gin = eng.backward(acts, go.to(cuda_dev))
+    # CPU restatement with autograd through both layers
+    params = {l: {k: refs[l][k].clone().requires_grad_(True) for k in refs[l] if "lora_" in k}
+              for l in range(2)}
+    x = h.float().clone().requires_grad_(True)
+    y = x
+    for l in range(2):
+        ww = dict(refs[l])
+        ww.update(params[l])
+        y = layer_ref.layer_forward(ww, y)
+    y.backward(go.float())
+    assert onf4.rel_err(acts[2].float().cpu().numpy(), y.detach().numpy()) < REL
+    assert onf4.rel_err(gin.float().cpu().numpy(), x.grad.numpy()) < REL
+    for l in range(2):
+        gv = store.views(store.grad, l)
+        for n in ("q_proj", "v_proj"):
+            for ab in ("A", "B"):
+                got = gv[f"self_attn.{n}.lora_{ab}.default.weight"].cpu().numpy()
+                assert onf4.rel_err(got, params[l][f"{n}.lora_{ab}"].grad.numpy()) < REL
+
+
+def test_optimizer_step_matches_reference_math(cuda_dev):
+    """Device AdamW + clip vs the reference update order restated in fp32 torch."""
+    from fitllm_b200 import ops
+    g = torch.Generator().manual_seed(2)
+    p = torch.randn(10000, generator=g)
+    grads = [torch.randn(10000, generator=g) * 0.3 for _ in range(3)]
+    m = torch.zeros_like(p)
+    v = torch.zeros_like(p)
+    pd, md, vd = p.to(cuda_dev), m.to(cuda_dev), v.to(cuda_dev)
+    lr, b1, b2, eps, wd = 2e-4, 0.9, 0.999, 1e-8, 0.01
+    for t, gr in enumerate(grads, start=1):
+        total = float(gr.norm())
+        coef = 1.0 / (total + 1e-6) if total > 1.0 else 1.0
+        gc = gr * coef if total > 1.0 else gr
+        m = b1 * m + (1 - b1) * gc
+        v = b2 * v + (1 - b2) * gc * gc
+        mh = m / (1 - b1 ** t)
+        vh = v / (1 - b2 ** t)
+        p = p - lr * (mh / (vh.sqrt() + eps) + wd * p)
+        gd = gr.to(cuda_dev)
+        clip = ops.grad_clip_coef(gd, 1.0)
+        ops.adamw_step(pd, gd, md, vd, t, lr, b1, b2, eps, wd, clip=clip)
+        assert abs(float(clip[0]) - total) / total < 1e-5
+    assert torch.allclose(pd.cpu(), p, rtol=1e-5, atol=1e-7)

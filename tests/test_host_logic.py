@@ -1,0 +1,247 @@
+"""Host-side logic on CPU (no GPU): the C-ABI library loads and exports every
+symbol include/fitq.h declares, reference-API behaviour of LoRALinear /
+LoRAManager on dense bases (restating fitllm's own tests), the golden outputs
+of FitLLM's pure-torch code, QuantState serialisation, the shard store
+layout, micro-batch splitting, and the per-layer gradient all-reduce on two
+gloo ranks."""
+import ctypes
+import json
+import os
+import re
+import socket
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+ROOT = Path(__file__).resolve().parent.parent
+GOLD = ROOT / "tests" / "golden"
+
+
+# ---------------------------------------------------------------- C ABI
+def test_library_loads_and_exports_header_symbols():
+    from fitllm_b200 import _lib, build
+    build.build()
+    header = (ROOT / "include" / "fitq.h").read_text()
+    declared = set(re.findall(r"FITQ_API\s+[\w\s\*]+?\b(fitq_\w+)\s*\(", header))
+    assert len(declared) >= 16
+    L = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(_lib.SIGNATURES) == declared
+    assert _lib.version().startswith("fitq")
+
+
+def test_abi_rejects_bad_arguments_without_a_device():
+    from fitllm_b200 import _lib
+    L = _lib.load()
+    w = _lib.Nf4WeightC(packed=None, quant_map=None, n_out=64, k_in=64)
+    rc = L.fitq_nf4_dequant(ctypes.byref(w), None, 0, 0, None)
+    assert rc == 1  # FITQ_ERR_ARG: checked before any device call
+    w2 = _lib.Nf4WeightC(packed=16, quant_map=16, absmax_f32=16, n_out=64, k_in=100)
+    assert L.fitq_nf4_dequant(ctypes.byref(w2), 16, 0, 0, None) == 2  # K % 64 != 0
+    assert L.fitq_gemm_bf16_tn(16, 16, 16, None, 128, 100, 64, None) == 2  # N % 16 != 0
+    assert b"N % 16 == 0" in L.fitq_last_error()
+    assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) > 5120 * 5120 * 2
+
+
+# ---------------------------------------------------------------- reference API
+class _Tiny(nn.Module):
+    def __init__(self, h=16):
+        super().__init__()
+        self.q_proj = nn.Linear(h, h, bias=False)
+        self.k_proj = nn.Linear(h, h, bias=False)
+        self.v_proj = nn.Linear(h, h, bias=False)
+        self.o_proj = nn.Linear(h, h, bias=False)
+        self.mlp = nn.Linear(h, h, bias=False)
+
+    def forward(self, x):
+        return self.o_proj(self.q_proj(x) + self.k_proj(x) + self.v_proj(x)) + self.mlp(x)
+
+
+def test_lora_linear_reference_behaviour():
+    from fitllm_b200.lora import LoRALinear
+    base = nn.Linear(16, 32, bias=False)
+    lora = LoRALinear(base, rank=4, alpha=8.0)
+    assert lora(torch.randn(2, 8, 16)).shape == (2, 8, 32)
+    assert lora.scale == 2.0
+    assert torch.all(lora.lora_B == 0) and lora.lora_A.abs().sum() > 0
+    assert not base.weight.requires_grad and lora.lora_A.requires_grad
+
+
+def test_lora_manager_inject_state_dict_and_grads():
+    from fitllm_b200.lora import LoRALinear, LoRAManager
+    torch.manual_seed(0)
+    model = _Tiny()
+    mgr = LoRAManager()
+    mgr.inject_lora(model, rank=2, alpha=4.0, targets=("q_proj", "v_proj"))
+    assert isinstance(model.q_proj, LoRALinear) and isinstance(model.k_proj, nn.Linear)
+    assert mgr.num_lora_layers == 2
+    mgr.freeze_base_model(model)
+    out = model(torch.randn(3, 16)).sum()
+    out.backward()
+    named = dict(model.named_parameters())
+    for n, p in named.items():
+        if "lora_" in n:
+            assert p.grad is not None
+        else:
+            assert p.grad is None
+    sd = mgr.state_dict()
+    assert set(sd) == {"q_proj.lora_A", "q_proj.lora_B", "v_proj.lora_A", "v_proj.lora_B"}
+    model2 = _Tiny()
+    mgr2 = LoRAManager()
+    mgr2.inject_lora(model2, rank=2, alpha=4.0, targets=("q_proj", "v_proj"))
+    mgr2.load_state_dict(sd)
+    for k, v in mgr2.state_dict().items():
+        assert torch.equal(v, sd[k])
+    assert len(list(mgr.trainable_parameters())) == 4
+
+
+def test_lora_linear_matches_reference_golden():
+    """Dense-base LoRALinear against fitllm.lora.LoRALinear outputs."""
+    from fitllm_b200.lora import LoRALinear
+    d = torch.load(GOLD / "reference_torch.pt", weights_only=False)["lora"]
+    base = nn.Linear(32, 48, bias=False)
+    lora = LoRALinear(base, rank=16, alpha=32.0)
+    with torch.no_grad():
+        base.weight.copy_(d["base_w"])
+        lora.lora_A.copy_(d["A"])
+        lora.lora_B.copy_(d["B"])
+    x = d["x"].clone().requires_grad_(True)
+    y = lora(x)
+    y.backward(d["gy"])
+    assert torch.equal(y, d["y"])
+    assert torch.equal(x.grad, d["gx"])
+    assert torch.equal(lora.lora_A.grad, d["gA"]) and torch.equal(lora.lora_B.grad, d["gB"])
+
+
+def test_cosine_lr_matches_reference_golden():
+    from fitllm_b200.optimizer import cosine_lr_scale
+    for s, w, m, v in torch.load(GOLD / "reference_torch.pt", weights_only=False)["cosine"]:
+        assert cosine_lr_scale(s, w, m) == v
+
+
+def _adamw_restated(p, g, m, v, t, lr, b1, b2, eps, wd):
+    m = b1 * m + (1 - b1) * g
+    v = b2 * v + (1 - b2) * g * g
+    mh, vh = m / (1 - b1 ** t), v / (1 - b2 ** t)
+    return p - lr * (mh / (vh.sqrt() + eps) + wd * p), m, v
+
+
+def test_adamw_order_matches_reference_golden():
+    """The update order the device kernel implements (restated in fp32 torch)
+    reproduces ShardOptimizer.step_from_memory bit for bit."""
+    d = torch.load(GOLD / "reference_torch.pt", weights_only=False)["adamw"]
+    layer_of = {n: int(n.split("layers.")[1].split(".")[0]) for n in d["names"]}
+    for n in d["names"]:
+        p, m, v = d["init"][n].clone(), torch.zeros(4, 6), torch.zeros(4, 6)
+        for t, grads in enumerate(d["grads"], start=1):
+            local = n.split(f"layers.{layer_of[n]}.")[1]
+            p, m, v = _adamw_restated(p, grads[layer_of[n]][local], m, v, t, d["lr"], d["beta1"],
+                                      d["beta2"], d["eps"], d["wd"])
+        assert torch.equal(p, d["final"][n]), n
+
+
+def test_clip_golden():
+    d = torch.load(GOLD / "reference_torch.pt", weights_only=False)["clip"]
+    flat = torch.cat([d["before"][0]["a"], d["before"][1]["b"]]).double()
+    norm = float(flat.norm())
+    assert abs(norm - d["norm"]) / d["norm"] < 1e-6
+    coef = d["max_norm"] / (norm + 1e-6)
+    assert torch.allclose(d["before"][1]["b"] * coef, d["after"][1]["b"], rtol=1e-6)
+
+
+# ---------------------------------------------------------------- formats
+def test_quant_state_dict_round_trip():
+    from fitllm_b200.nf4 import QuantState
+    qs = QuantState(absmax=torch.arange(16, dtype=torch.uint8), shape=(8, 128),
+                    quant_map=torch.linspace(-1, 1, 16), nested_absmax=torch.tensor([0.5]),
+                    nested_quant_map=torch.linspace(-1, 1, 256), offset=0.125)
+    d = qs.as_dict(packed=True)
+    assert set(d) == {"absmax", "quant_map", "nested_absmax", "nested_quant_map",
+                      "quant_state.bitsandbytes__nf4"}
+    meta = json.loads(bytes(d["quant_state.bitsandbytes__nf4"].tolist()))
+    assert meta["quant_type"] == "nf4" and meta["blocksize"] == 64 and meta["nested_offset"] == 0.125
+    back = QuantState.from_dict(d, device="cpu")
+    assert back.shape == (8, 128) and back.offset == 0.125 and back.nested
+    assert torch.equal(back.absmax, qs.absmax)
+
+
+def test_shard_store_layout_drops_lora_keys():
+    from fitllm_b200.scheduler import ShardScheduler
+    s = ShardScheduler(2, "cpu", ring_slots=2, pin_memory=False)
+    meta = torch.tensor(list(json.dumps({"shape": [4, 64], "nested_offset": 0.5}).encode()),
+                        dtype=torch.uint8)
+    t = {"a.weight": torch.arange(128, dtype=torch.uint8).view(-1, 1),
+         "a.weight.absmax": torch.ones(4, dtype=torch.uint8),
+         "a.weight.quant_state.bitsandbytes__nf4": meta,
+         "n.weight": torch.randn(64).bfloat16(),
+         "q.lora_A.default.weight": torch.randn(2, 2)}
+    nb = s.add_layer(0, t)
+    assert nb % 256 == 0
+    host = s.host_tensors(0)
+    assert "q.lora_A.default.weight" not in host
+    assert torch.equal(host["a.weight"], t["a.weight"]) and torch.equal(host["n.weight"], t["n.weight"])
+    assert s.quant_meta(0)["a.weight"]["nested_offset"] == 0.5
+
+
+def test_microbatch_split():
+    from fitllm_b200.distributed import microbatch_range
+    for n in (16, 15, 3):
+        for world in (1, 2, 4, 8):
+            spans = [microbatch_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            sizes = [b - a for a, b in spans]
+            assert max(sizes) - min(sizes) <= 1
+
+
+# ---------------------------------------------------------------- multi-rank (gloo)
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q):
+    import torch.distributed as dist
+    from fitllm_b200.distributed import LoRAGradComm, microbatch_range
+    from fitllm_b200.optimizer import LoRAStore
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    store = LoRAStore(3, [("a", (4, 8)), ("b", (8, 4))], "cpu")
+    # per-rank grads: each rank owns micro-batches [s, e); grad of mb i is i+1 everywhere
+    s, e = microbatch_range(6, rank, world)
+    for layer in range(3):
+        store.layer_slice(store.grad, layer).fill_(float(sum(range(s + 1, e + 1))) * (layer + 1))
+    comm = LoRAGradComm(store)
+    for layer in reversed(range(3)):
+        comm.allreduce_layer(layer)
+    comm.wait()
+    uniform = all(bool(torch.all(store.layer_slice(store.grad, l) == store.layer_slice(store.grad, l)[0]))
+                  for l in range(3))
+    q.put((rank, [float(store.layer_slice(store.grad, l)[0]) for l in range(3)], uniform))
+    dist.destroy_process_group()
+
+
+def test_per_layer_allreduce_two_gloo_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    total = sum(range(1, 7))
+    for _, vals, uniform in res:
+        assert vals == [total * 1.0, total * 2.0, total * 3.0]
+        assert uniform
