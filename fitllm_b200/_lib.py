@@ -54,6 +54,7 @@ SIGNATURES = {
     "fitq_timing_enable": (I32, [I32]),
     "fitq_timing_read": (I32, [P, P, I32]),
     "fitq_launch_count": (ctypes.c_longlong, []),
+    "fitq_nf4_gemv_noalloc": (I32, [WP, P, I64, P, P, I32, F32, P, P, P, P]),
 }
 
 

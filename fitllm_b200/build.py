@@ -22,7 +22,8 @@ OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "libfitq.so"
 INCLUDE = PKG.parent / "include"
 
-SOURCES = ["nf4.cu", "gemm_sm100.cu", "lora.cu", "gemv.cu", "optim.cu", "abi.cu"]
+SOURCES = ["nf4.cu", "gemm_sm100.cu", "lora.cu", "gemv.cu", "optim.cu", "abi.cu",
+           "gemv_noalloc.cu"]
 HEADERS = ["common.cuh", "kernels.cuh"]
 
 NVCC_FLAGS = [

@@ -568,3 +568,8 @@ namespace fitq {
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 }  // namespace fitq
 extern "C" long long fitq_launch_count(void) { return g_launches.load(); }
+
+namespace fitq {
+// Lets entry points defined in other files report through fitq_last_error().
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace fitq

@@ -81,6 +81,8 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
 int timing_begin(cudaStream_t st, double flops);
 // Counts kernel launches made by the library (read by fitq_launch_count).
 void note_launch();
+// Sets the text returned by fitq_last_error() for the calling thread.
+void set_last_error(const char* msg);
 void timing_end(int slot, cudaStream_t st);
 
 // Optimizer kernels (optim.cu).

@@ -185,6 +185,27 @@ FITQ_API int fitq_timing_read(float* ms, double* flops, int max);
 /* Number of kernels this library has launched in this process so far. */
 FITQ_API long long fitq_launch_count(void);
 
+/* fitq_nf4_gemv without a workspace argument, for callers that cannot
+ * allocate device memory (no counterpart in the reference: FitLLM always runs
+ * with PyTorch's allocator).  Meant for runtimes that drive the decode step
+ * through this ABI but own no CUDA allocator, or must account for every
+ * device allocation up front: they pass the inputs and outputs they hold, and
+ * the scratch comes from one fixed array of FITQ_GEMV_NOALLOC_SCRATCH_BYTES
+ * (8 MiB) built into the library, which every GPU that loads the library
+ * keeps until the process exits.  Same arguments and arithmetic as
+ * fitq_nf4_gemv (M <= 64, N % 64 == 0, K % 64 == 0, rank 0/16/32/48/64);
+ * shapes whose scratch exceeds the array return FITQ_ERR_WORKSPACE with the
+ * needed size in fitq_last_error().  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current, so
+ * make it before any stream capture.  All calls share the array and each one
+ * overwrites what it uses; calls that overlap on the GPU (two streams, two
+ * host threads) race on it and must be serialised by the caller. */
+#define FITQ_GEMV_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+FITQ_API int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
+                                   const float* lora_a, const float* lora_b, int rank,
+                                   float scale, const void* bias, void* y, const void* y_add,
+                                   fitq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
