@@ -573,3 +573,73 @@ namespace fitq {
 // Lets entry points defined in other files report through fitq_last_error().
 void set_last_error(const char* msg) { g_last_error = msg; }
 }  // namespace fitq
+
+// ---------------------------------------------------------------- layer kernels
+extern "C" {
+
+int fitq_rmsnorm_fwd(const void* x, const void* weight, void* y, int64_t rows, int64_t cols,
+                     float eps, fitq_stream_t stream) {
+  if (!x || !weight || !y) return fail(FITQ_ERR_ARG, "rmsnorm: NULL tensor");
+  if (rows <= 0 || cols <= 0 || cols % 8 != 0 || rows >= (1ll << 31))
+    return fail(FITQ_ERR_SHAPE, "rmsnorm: need cols %% 8 == 0 (rows=%lld cols=%lld)",
+                (long long)rows, (long long)cols);
+  if (!al16(x) || !al16(weight) || !al16(y)) return fail(FITQ_ERR_ALIGN, "rmsnorm: 16-byte alignment");
+  int rc;
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_rmsnorm_fwd(x, weight, y, rows, cols, eps,
+                                                static_cast<cudaStream_t>(stream)), "rmsnorm_fwd");
+}
+
+int fitq_rmsnorm_bwd(const void* dy, const void* x, const void* weight, void* dx, int64_t rows,
+                     int64_t cols, float eps, fitq_stream_t stream) {
+  if (!dy || !x || !weight || !dx) return fail(FITQ_ERR_ARG, "rmsnorm_bwd: NULL tensor");
+  if (rows <= 0 || cols <= 0 || cols % 8 != 0 || rows >= (1ll << 31))
+    return fail(FITQ_ERR_SHAPE, "rmsnorm_bwd: need cols %% 8 == 0");
+  if (!al16(dy) || !al16(x) || !al16(weight) || !al16(dx))
+    return fail(FITQ_ERR_ALIGN, "rmsnorm_bwd: 16-byte alignment");
+  int rc;
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_rmsnorm_bwd(dy, x, weight, dx, rows, cols, eps,
+                                                static_cast<cudaStream_t>(stream)), "rmsnorm_bwd");
+}
+
+int fitq_rope(const void* t, void* out, const float* cos_half, const float* sin_half, int64_t rows,
+              int heads, int head_dim, int64_t seq, int backward, fitq_stream_t stream) {
+  if (!t || !out || !cos_half || !sin_half) return fail(FITQ_ERR_ARG, "rope: NULL tensor");
+  if (rows <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 16 != 0 || seq <= 0)
+    return fail(FITQ_ERR_SHAPE, "rope: need head_dim %% 16 == 0");
+  if (!al16(t) || !al16(out) || !al16(cos_half) || !al16(sin_half))
+    return fail(FITQ_ERR_ALIGN, "rope: 16-byte alignment");
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms) return rc;
+  return launch_status(fitq::launch_rope(t, out, cos_half, sin_half, rows, heads, head_dim, seq,
+                                         backward, static_cast<cudaStream_t>(stream), sms), "rope");
+}
+
+int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n, fitq_stream_t stream) {
+  if (!gate || !up || !act) return fail(FITQ_ERR_ARG, "swiglu: NULL tensor");
+  if (n <= 0 || n % 8 != 0) return fail(FITQ_ERR_SHAPE, "swiglu: need n %% 8 == 0");
+  if (!al16(gate) || !al16(up) || !al16(act)) return fail(FITQ_ERR_ALIGN, "swiglu: 16-byte alignment");
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms) return rc;
+  return launch_status(fitq::launch_swiglu_fwd(gate, up, act, n, static_cast<cudaStream_t>(stream), sms),
+                       "swiglu_fwd");
+}
+
+int fitq_swiglu_bwd(const void* d_act, const void* gate, const void* up, void* d_gate, void* d_up,
+                    int64_t n, fitq_stream_t stream) {
+  if (!d_act || !gate || !up || !d_gate || !d_up) return fail(FITQ_ERR_ARG, "swiglu_bwd: NULL tensor");
+  if (n <= 0 || n % 8 != 0) return fail(FITQ_ERR_SHAPE, "swiglu_bwd: need n %% 8 == 0");
+  if (!al16(d_act) || !al16(gate) || !al16(up) || !al16(d_gate) || !al16(d_up))
+    return fail(FITQ_ERR_ALIGN, "swiglu_bwd: 16-byte alignment");
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms) return rc;
+  return launch_status(fitq::launch_swiglu_bwd(d_act, gate, up, d_gate, d_up, n,
+                                               static_cast<cudaStream_t>(stream), sms),
+                       "swiglu_bwd");
+}
+
+}  // extern "C"

@@ -85,6 +85,18 @@ void note_launch();
 void set_last_error(const char* msg);
 void timing_end(int slot, cudaStream_t st);
 
+// Decoder-layer row / elementwise kernels (layer_ops.cu).
+int launch_rmsnorm_fwd(const void* x, const void* w, void* y, int64_t rows, int64_t cols,
+                       float eps, cudaStream_t st);
+int launch_rmsnorm_bwd(const void* dy, const void* x, const void* w, void* dx, int64_t rows,
+                       int64_t cols, float eps, cudaStream_t st);
+int launch_rope(const void* t, void* out, const float* cs, const float* sn, int64_t rows,
+                int heads, int dim, int64_t seq, int backward, cudaStream_t st, int num_sms);
+int launch_swiglu_fwd(const void* g, const void* u, void* act, int64_t n, cudaStream_t st,
+                      int num_sms);
+int launch_swiglu_bwd(const void* d, const void* g, const void* u, void* dg, void* du, int64_t n,
+                      cudaStream_t st, int num_sms);
+
 // Optimizer kernels (optim.cu).
 int launch_adamw(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
                  float b2, float eps, float wd, int step, const float* clip, cudaStream_t st);

@@ -31,7 +31,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from .distributed import LoRAGradComm
-from .layer import DecoderLayer, LayerConfig, add_lora_, rotary_cos_sin
+from .layer import DecoderLayer, LayerConfig, add_lora_, rotary_tables
 from .nf4 import QuantState
 from .optimizer import LoRAStore
 from .qlora import Linear4bit, Params4bit, QLoRALinear4bit
@@ -96,7 +96,7 @@ class ShardStationaryEngine:
 
     def position_embeddings(self, seq_len: int, dtype=torch.bfloat16):
         if self._pe is None or self._pe[0].shape[0] != seq_len:
-            self._pe = rotary_cos_sin(seq_len, self.cfg.head_dim, self.cfg.rope_theta, self.device, dtype)
+            self._pe = rotary_tables(seq_len, self.cfg.head_dim, self.cfg.rope_theta, self.device)
         return self._pe
 
     def _load(self, l: int) -> None:
@@ -118,9 +118,13 @@ class ShardStationaryEngine:
         for l in range(self.num_layers):
             self.scheduler.prefetch(l + 1)
             self._load(l)
-            out = torch.empty_like(h)
-            for a, b in self._chunks(h.shape[0]):
-                out[a:b] = self.layer(h[a:b], position_embeddings=pe)
+            chunks = self._chunks(h.shape[0])
+            if len(chunks) == 1:
+                out = self.layer(h, position_embeddings=pe)
+            else:
+                out = torch.empty_like(h)
+                for a, b in chunks:
+                    out[a:b] = self.layer(h[a:b], position_embeddings=pe)
             self.scheduler.release(l)
             h = out
             acts.append(h)
@@ -138,13 +142,17 @@ class ShardStationaryEngine:
             self.scheduler.prefetch(l - 1)
             self._load(l)
             h_prev = acts[l]
-            g_in = torch.empty_like(h_prev)
-            for a, b in self._chunks(h_prev.shape[0]):
+            chunks = self._chunks(h_prev.shape[0])
+            g_in = None if len(chunks) == 1 else torch.empty_like(h_prev)
+            for a, b in chunks:
                 x = h_prev[a:b].detach().requires_grad_(True)
                 with torch.enable_grad():
                     y = self.layer(x, position_embeddings=pe)
                 y.backward(g[a:b])
-                g_in[a:b] = x.grad
+                if g_in is None:
+                    g_in = x.grad
+                else:
+                    g_in[a:b] = x.grad
                 del x, y
             self.scheduler.release(l)
             if self.comm is not None:

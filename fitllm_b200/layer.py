@@ -11,7 +11,8 @@ shard keys of fitllm/forward.py:95-109 load unchanged, and runs:
 * every projection as an NF4 ``Linear4bit`` / ``QLoRALinear4bit`` on the
   sm_100a kernels (the residual adds of o_proj and down_proj ride in the GEMM
   epilogue);
-* attention with torch SDPA (library kernel), norms / RoPE / SiLU as torch ops.
+* RMSNorm, the rotary embedding and SwiGLU as fused one-pass kernels of the
+  same library (layer_ops.cu); attention with torch SDPA (library kernel).
 """
 from __future__ import annotations
 
@@ -22,6 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .layer_ops import rms_norm, rope, swiglu
 from .qlora import Linear4bit, QLoRALinear4bit
 
 
@@ -64,9 +66,7 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return self.weight * xf.to(x.dtype)
+        return rms_norm(x, self.weight, self.eps)
 
 
 def rotary_cos_sin(seq_len: int, head_dim: int, theta: float, device, dtype=torch.bfloat16,
@@ -78,6 +78,26 @@ def rotary_cos_sin(seq_len: int, head_dim: int, theta: float, device, dtype=torc
     freqs = torch.outer(pos, inv)
     emb = torch.cat([freqs, freqs], dim=-1)
     return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def rotary_tables(seq_len: int, head_dim: int, theta: float, device,
+                  position_ids: Optional[torch.Tensor] = None):
+    """fp32 (cos, sin) [S, head_dim/2] of the rotary frequencies (the fused
+    kernel duplicates them over the two halves, as HF's cat([f, f]) does)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device, dtype=torch.float32) / head_dim))
+    pos = torch.arange(seq_len, device=device, dtype=torch.float32) if position_ids is None \
+        else position_ids.to(device, torch.float32)
+    f = torch.outer(pos, inv)
+    return f.cos().contiguous(), f.sin().contiguous()
+
+
+def _as_half_tables(pe, head_dim):
+    cos, sin = pe
+    if cos.shape[-1] == head_dim:  # HF-style full (cos, sin): keep the first half in fp32
+        cos, sin = cos[..., : head_dim // 2], sin[..., : head_dim // 2]
+    if cos.dim() == 3:
+        cos, sin = cos[0], sin[0]
+    return cos.float().contiguous(), sin.float().contiguous()
 
 
 def _rotate_half(x):
@@ -103,10 +123,9 @@ class Attention(nn.Module):
     def forward(self, x, residual, cos, sin, attn_mask: Optional[torch.Tensor] = None):
         cfg = self.cfg
         b, s, _ = x.shape
-        q = self.q_proj(x).view(b, s, cfg.heads, cfg.head_dim).transpose(1, 2)
-        k = self.k_proj(x).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        q = rope(self.q_proj(x), cos, sin, cfg.heads).view(b, s, cfg.heads, cfg.head_dim).transpose(1, 2)
+        k = rope(self.k_proj(x), cos, sin, cfg.kv_heads).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
         v = self.v_proj(x).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
-        q, k = apply_rotary(q, k, cos, sin)
         if attn_mask is None:
             o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         else:
@@ -123,7 +142,7 @@ class MLP(nn.Module):
         self.down_proj = Linear4bit(cfg.intermediate, cfg.hidden, device=device)
 
     def forward(self, x, residual):
-        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x), residual=residual)
+        return self.down_proj(swiglu(self.gate_proj(x), self.up_proj(x)), residual=residual)
 
 
 class DecoderLayer(nn.Module):
@@ -139,9 +158,9 @@ class DecoderLayer(nn.Module):
 
     def forward(self, h: torch.Tensor, position_embeddings=None, attention_mask=None, **_):
         if position_embeddings is None:
-            position_embeddings = rotary_cos_sin(h.shape[1], self.cfg.head_dim, self.cfg.rope_theta,
-                                                 h.device, h.dtype)
-        cos, sin = position_embeddings
+            position_embeddings = rotary_tables(h.shape[1], self.cfg.head_dim, self.cfg.rope_theta,
+                                                h.device)
+        cos, sin = _as_half_tables(position_embeddings, self.cfg.head_dim)
         h1 = self.self_attn(self.input_layernorm(h), h, cos, sin, attention_mask)
         return self.mlp(self.post_attention_layernorm(h1), h1)
 

@@ -1,0 +1,116 @@
+"""Autograd wrappers of the fused decoder-layer kernels (RMSNorm, rotary
+embedding, SwiGLU) that surround the QLoRA projections.  CUDA bf16 only."""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _st(t) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _c(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+class RMSNormFn(torch.autograd.Function):
+    """Qwen2RMSNorm with frozen weight: y = w * bf16(x * rsqrt(mean(x^2) + eps))."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps: float):
+        x = _c(x)
+        cols = x.shape[-1]
+        rows = x.numel() // cols
+        y = torch.empty_like(x)
+        L = _lib.load()
+        with torch.cuda.device(x.device):
+            _lib.check(L.fitq_rmsnorm_fwd(x.data_ptr(), weight.data_ptr(), y.data_ptr(), rows, cols,
+                                          float(eps), _st(x)), "fitq_rmsnorm_fwd")
+        ctx.save_for_backward(x, weight)
+        ctx.eps = eps
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dy = _c(dy.to(x.dtype))
+        cols = x.shape[-1]
+        rows = x.numel() // cols
+        dx = torch.empty_like(x)
+        L = _lib.load()
+        with torch.cuda.device(x.device):
+            _lib.check(L.fitq_rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), weight.data_ptr(), dx.data_ptr(),
+                                          rows, cols, float(ctx.eps), _st(x)), "fitq_rmsnorm_bwd")
+        return dx, None, None
+
+
+class RoPEFn(torch.autograd.Function):
+    """Rotate-half rotary embedding of t [B, S, heads*head_dim] (bf16) with fp32
+    half tables cos/sin [S, head_dim/2]; returns a new tensor of t's shape."""
+
+    @staticmethod
+    def forward(ctx, t, cos_half, sin_half, heads: int):
+        t = _c(t)
+        seq = t.shape[-2]
+        dim = t.shape[-1] // heads
+        rows = t.numel() // (heads * dim)
+        out = torch.empty_like(t)
+        L = _lib.load()
+        with torch.cuda.device(t.device):
+            _lib.check(L.fitq_rope(t.data_ptr(), out.data_ptr(), cos_half.data_ptr(), sin_half.data_ptr(),
+                                   rows, heads, dim, seq, 0, _st(t)), "fitq_rope")
+        ctx.save_for_backward(cos_half, sin_half)
+        ctx.meta = (heads, dim, seq, rows)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        cos_half, sin_half = ctx.saved_tensors
+        heads, dim, seq, rows = ctx.meta
+        g = _c(g)
+        out = torch.empty_like(g)
+        L = _lib.load()
+        with torch.cuda.device(g.device):
+            _lib.check(L.fitq_rope(g.data_ptr(), out.data_ptr(), cos_half.data_ptr(), sin_half.data_ptr(),
+                                   rows, heads, dim, seq, 1, _st(g)), "fitq_rope")
+        return out, None, None, None
+
+
+class SwiGLUFn(torch.autograd.Function):
+    """act = silu(gate) * up."""
+
+    @staticmethod
+    def forward(ctx, gate, up):
+        gate, up = _c(gate), _c(up)
+        act = torch.empty_like(gate)
+        L = _lib.load()
+        with torch.cuda.device(gate.device):
+            _lib.check(L.fitq_swiglu_fwd(gate.data_ptr(), up.data_ptr(), act.data_ptr(), gate.numel(),
+                                         _st(gate)), "fitq_swiglu_fwd")
+        ctx.save_for_backward(gate, up)
+        return act
+
+    @staticmethod
+    def backward(ctx, d):
+        gate, up = ctx.saved_tensors
+        d = _c(d.to(gate.dtype))
+        dg, du = torch.empty_like(gate), torch.empty_like(up)
+        L = _lib.load()
+        with torch.cuda.device(gate.device):
+            _lib.check(L.fitq_swiglu_bwd(d.data_ptr(), gate.data_ptr(), up.data_ptr(), dg.data_ptr(),
+                                         du.data_ptr(), gate.numel(), _st(gate)), "fitq_swiglu_bwd")
+        return dg, du
+
+
+def rms_norm(x, weight, eps):
+    return RMSNormFn.apply(x, weight, eps)
+
+
+def rope(t, cos_half, sin_half, heads):
+    return RoPEFn.apply(t, cos_half, sin_half, heads)
+
+
+def swiglu(gate, up):
+    return SwiGLUFn.apply(gate, up)

@@ -182,6 +182,28 @@ FITQ_API int fitq_grad_clip_coef(const float* grads, int64_t n, float max_norm, 
 FITQ_API int fitq_timing_enable(int capacity);
 FITQ_API int fitq_timing_read(float* ms, double* flops, int max);
 
+/* Decoder-layer kernels around the projections (HF Qwen2DecoderLayer as
+ * FitLLM runs it, fitllm/forward.py:657-701; torch ops in the reference).
+ * bf16 tensors, fp32 arithmetic, one pass each.
+ * RMSNorm (Qwen2RMSNorm): y = w * bf16(x * rsqrt(mean(x^2) + eps)) per row of
+ * `cols` (cols % 8 == 0); the backward returns dx only (w is frozen).
+ * Rotary embedding (rotate-half) on t[rows, heads, head_dim], position =
+ * row % seq, cos_half/sin_half fp32 [seq, head_dim/2]; backward != 0 applies
+ * the transposed rotation (the gradient).  head_dim % 16 == 0.
+ * SwiGLU: act = silu(gate) * up over n elements (n % 8 == 0) and its
+ * gradients d_gate, d_up. */
+FITQ_API int fitq_rmsnorm_fwd(const void* x, const void* weight, void* y, int64_t rows,
+                              int64_t cols, float eps, fitq_stream_t stream);
+FITQ_API int fitq_rmsnorm_bwd(const void* dy, const void* x, const void* weight, void* dx,
+                              int64_t rows, int64_t cols, float eps, fitq_stream_t stream);
+FITQ_API int fitq_rope(const void* t, void* out, const float* cos_half, const float* sin_half,
+                       int64_t rows, int heads, int head_dim, int64_t seq, int backward,
+                       fitq_stream_t stream);
+FITQ_API int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n,
+                             fitq_stream_t stream);
+FITQ_API int fitq_swiglu_bwd(const void* d_act, const void* gate, const void* up, void* d_gate,
+                             void* d_up, int64_t n, fitq_stream_t stream);
+
 /* Number of kernels this library has launched in this process so far. */
 FITQ_API long long fitq_launch_count(void);
 

@@ -240,3 +240,49 @@ def test_optimizer_step_matches_reference_math(cuda_dev):
         ops.adamw_step(pd, gd, md, vd, t, lr, b1, b2, eps, wd, clip=clip)
         assert abs(float(clip[0]) - total) / total < 1e-5
     assert torch.allclose(pd.cpu(), p, rtol=1e-5, atol=1e-7)
+
+
+def test_fused_layer_kernels_vs_torch(cuda_dev):
+    """RMSNorm / rotary / SwiGLU kernels (forward and gradient) against fp32
+    torch restatements of the HF ops."""
+    from fitllm_b200.layer import rotary_tables
+    from fitllm_b200.layer_ops import rms_norm, rope, swiglu
+    g = torch.Generator(device=cuda_dev).manual_seed(0)
+    x = torch.randn(3, 40, 5120, generator=g, device=cuda_dev).bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(5120, generator=g, device=cuda_dev)).bfloat16()
+    y = rms_norm(x, w, 1e-6)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_(True)
+    yr = w.float() * (xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6))
+    yr.backward(dy.float())
+    assert onf4.rel_err(y.detach().float().cpu().numpy(), yr.detach().cpu().numpy()) < REL
+    assert onf4.rel_err(x.grad.float().cpu().numpy(), xr.grad.cpu().numpy()) < REL
+
+    heads, hd, S = 8, 128, 40
+    t = torch.randn(3, S, heads * hd, generator=g, device=cuda_dev).bfloat16().requires_grad_(True)
+    cos, sin = rotary_tables(S, hd, 1e6, cuda_dev)
+    o = rope(t, cos, sin, heads)
+    do = torch.randn_like(o)
+    o.backward(do)
+    tr = t.detach().float().view(3, S, heads, hd).requires_grad_(True)
+    c = torch.cat([cos, cos], -1)[None, :, None, :]
+    s = torch.cat([sin, sin], -1)[None, :, None, :]
+    rot = torch.cat((-tr[..., hd // 2:], tr[..., : hd // 2]), -1)
+    orf = tr * c + rot * s
+    orf.backward(do.float().view(3, S, heads, hd))
+    assert onf4.rel_err(o.detach().float().cpu().numpy(), orf.detach().reshape(3, S, -1).cpu().numpy()) < REL
+    assert onf4.rel_err(t.grad.float().cpu().numpy(), tr.grad.reshape(3, S, -1).cpu().numpy()) < REL
+
+    gate = torch.randn(4, 27648, generator=g, device=cuda_dev).bfloat16().requires_grad_(True)
+    up = torch.randn(4, 27648, generator=g, device=cuda_dev).bfloat16().requires_grad_(True)
+    a = swiglu(gate, up)
+    da = torch.randn_like(a)
+    a.backward(da)
+    gr = gate.detach().float().requires_grad_(True)
+    ur = up.detach().float().requires_grad_(True)
+    ar = torch.nn.functional.silu(gr) * ur
+    ar.backward(da.float())
+    assert onf4.rel_err(a.detach().float().cpu().numpy(), ar.detach().cpu().numpy()) < REL
+    assert onf4.rel_err(gate.grad.float().cpu().numpy(), gr.grad.cpu().numpy()) < REL
+    assert onf4.rel_err(up.grad.float().cpu().numpy(), ur.grad.cpu().numpy()) < REL
