@@ -22,7 +22,14 @@ B200 differences (same mathematics):
   layer's slice is all-reduced across ranks as soon as its backward is queued;
 * the recompute uses the same dtype and attention mask as the forward
   (the reference's recompute drops autocast and the mask,
-  fitllm/backward.py:222-231, which its own notes call a bug).
+  fitllm/backward.py:222-231, which its own notes call a bug);
+* HBM budget instead of a fixed recompute: the forward runs WITH autograd for
+  the last layers whose saved activations fit the budget
+  (``keep_activations``), and the backward of those layers skips the
+  recompute (identical values, one layer-forward of work less).  The other
+  layers are recomputed as in the reference.  A kept graph references its
+  layer's ring slot and LoRA slices; the backward re-loads the layer (same
+  slot, same views) before using it.
 """
 from __future__ import annotations
 
@@ -78,7 +85,15 @@ def lora_entries(layer: DecoderLayer):
 
 class ShardStationaryEngine:
     def __init__(self, cfg: LayerConfig, scheduler: ShardScheduler, store: LoRAStore, device,
-                 comm: Optional[LoRAGradComm] = None, mb_chunk: Optional[int] = None):
+                 comm: Optional[LoRAGradComm] = None, mb_chunk: Optional[int] = None,
+                 keep_activations="auto", keep_budget_fraction: float = 0.6):
+        """keep_activations: "auto" (as many trailing layers as fit in
+        keep_budget_fraction of the free HBM), an int (that many trailing
+        layers) or 0 (recompute every layer, the reference behaviour)."""
+        self.keep_activations = keep_activations
+        self.keep_budget_fraction = keep_budget_fraction
+        self._graphs: Dict[int, tuple] = {}
+        self.last_kept = 0
         self.cfg = cfg
         self.scheduler = scheduler
         self.store = store
@@ -108,23 +123,50 @@ class ShardStationaryEngine:
         c = self.mb_chunk or b
         return [(i, min(b, i + c)) for i in range(0, b, c)]
 
-    @torch.no_grad()
+    def saved_bytes_per_token(self) -> int:
+        """Autograd state one token leaves in a layer (bf16): normed input, T,
+        q, k, v, attention output (+ LSE), post-attention residual, gate, up."""
+        c = self.cfg
+        qd, kvd = c.heads * c.head_dim, c.kv_heads * c.head_dim
+        return 2 * (c.hidden + 2 * c.lora_rank + 2 * qd + 2 * kvd + c.hidden + 2 * c.intermediate) + 4 * c.heads
+
+    def _layers_to_keep(self, tokens: int) -> int:
+        k = self.keep_activations
+        if k == "auto":
+            free, _ = torch.cuda.mem_get_info(self.device)
+            budget = self.keep_budget_fraction * free
+            per = tokens * self.saved_bytes_per_token()
+            k = int(budget // max(per, 1))
+        return max(0, min(int(k), self.num_layers))
+
     def forward(self, h: torch.Tensor) -> List[torch.Tensor]:
         """h: [B, S, hidden] bf16 (B stacked micro-batches).  Returns the L+1
         boundary activations (activations[i] = hidden state before layer i)."""
         pe = self.position_embeddings(h.shape[1], h.dtype)
         acts = [h]
+        self._graphs.clear()
+        L = self.num_layers
+        keep = self._layers_to_keep(h.shape[0] * h.shape[1])
+        self.last_kept = keep
         self.scheduler.prefetch(0)
-        for l in range(self.num_layers):
+        for l in range(L):
             self.scheduler.prefetch(l + 1)
             self._load(l)
             chunks = self._chunks(h.shape[0])
-            if len(chunks) == 1:
-                out = self.layer(h, position_embeddings=pe)
+            if l >= L - keep and len(chunks) == 1:
+                x = h.detach().requires_grad_(True)
+                with torch.enable_grad():
+                    y = self.layer(x, position_embeddings=pe)
+                self._graphs[l] = (x, y)
+                out = y.detach()
             else:
-                out = torch.empty_like(h)
-                for a, b in chunks:
-                    out[a:b] = self.layer(h[a:b], position_embeddings=pe)
+                with torch.no_grad():
+                    if len(chunks) == 1:
+                        out = self.layer(h, position_embeddings=pe)
+                    else:
+                        out = torch.empty_like(h)
+                        for a, b in chunks:
+                            out[a:b] = self.layer(h[a:b], position_embeddings=pe)
             self.scheduler.release(l)
             h = out
             acts.append(h)
@@ -142,6 +184,16 @@ class ShardStationaryEngine:
             self.scheduler.prefetch(l - 1)
             self._load(l)
             h_prev = acts[l]
+            if l in self._graphs:  # forward kept its autograd state: no recompute
+                x, y = self._graphs.pop(l)
+                y.backward(g)
+                g_in = x.grad
+                del x, y
+                self.scheduler.release(l)
+                if self.comm is not None:
+                    self.comm.allreduce_layer(l)
+                g = g_in
+                continue
             chunks = self._chunks(h_prev.shape[0])
             g_in = None if len(chunks) == 1 else torch.empty_like(h_prev)
             for a, b in chunks:

@@ -167,9 +167,11 @@ def test_decoder_layer_vs_restatement(cuda_dev):
                             rg[name + ".lora_B"].numpy()) < REL
 
 
-def test_engine_two_layers_vs_restatement(cuda_dev):
-    """Shard-stationary forward + recompute backward over 2 layers streamed
-    through the pinned host ring, LoRA grads accumulated in the flat store."""
+@pytest.mark.parametrize("mb_chunk,keep", [(1, 0), (None, 2), (None, 1)])
+def test_engine_two_layers_vs_restatement(cuda_dev, mb_chunk, keep):
+    """Shard-stationary forward + backward over 2 layers streamed through the
+    pinned host ring, LoRA grads accumulated in the flat store; with the
+    recompute (keep=0), without it (keep=2) and mixed (keep=1)."""
     from fitllm_b200.engine import ShardStationaryEngine, lora_entries
     from fitllm_b200.layer import DecoderLayer, add_lora_
     from fitllm_b200.optimizer import LoRAStore
@@ -189,7 +191,7 @@ def test_engine_two_layers_vs_restatement(cuda_dev):
     for l in range(2):
         store.init_layer_(l, {f"self_attn.{n}.lora_{ab}.default.weight": refs[l][f"{n}.lora_{ab}"]
                               for n in ("q_proj", "v_proj") for ab in ("A", "B")})
-    eng = ShardStationaryEngine(cfg, sched, store, cuda_dev, mb_chunk=1)
+    eng = ShardStationaryEngine(cfg, sched, store, cuda_dev, mb_chunk=mb_chunk, keep_activations=keep)
     g = torch.Generator().manual_seed(30)
     h = torch.randn(3, 64, SMALL["hidden"], generator=g).bfloat16()
     go = torch.randn(3, 64, SMALL["hidden"], generator=g).bfloat16()
