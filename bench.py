@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--cpu-seq", type=int, default=2048)
     return ap.parse_args()
 
@@ -122,6 +123,59 @@ def cpu_baseline(a, seq):
             "sample": f"1 micro-batch x {seq} tokens through one layer step (fwd + recompute + bwd), "
                       f"fp32 torch CPU restatement with oracle-dequantised NF4 weights; "
                       f"{r['step_s']:.1f} s step (quantisation {r['quantize_s']:.1f} s untimed)"}
+
+
+def gemv_sweep(dev, peak_gbs, reps=20):
+    """NF4 GEMV decode sweep: HBM GB/s of the weight stream.
+
+    Every shape rotates over enough distinct weights to exceed 2x L2, one
+    pass over them is captured in a CUDA graph and replayed; time = CUDA
+    events around the replays.  Bytes = packed NF4 + absmax codes + nested
+    absmax of one weight per call."""
+    import torch
+    from fitllm_b200 import ops
+    from fitllm_b200.nf4 import Nf4WeightCRef, quantize_nf4
+    out = {}
+    shapes = [("q_proj", 5120, 5120, 16), ("v_proj", 1024, 5120, 16), ("gate_up", 27648, 5120, 0),
+              ("down", 5120, 27648, 0)]
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    g = torch.Generator(device=dev).manual_seed(11)
+    for name, n, k, r in shapes:
+        wbytes = n * k // 2 + n * k // 64 + ((n * k // 64 + 255) // 256) * 4
+        nsets = max(2, int(2 * l2 // wbytes) + 1)
+        sets = []
+        for _ in range(nsets):
+            w = torch.randn(n, k, generator=g, device=dev) * 0.02
+            sets.append(Nf4WeightCRef(*quantize_nf4(w)))
+            del w
+        A = (torch.rand(r, k, generator=g, device=dev) - 0.5) * 0.02 if r else None
+        B = torch.randn(n, r, generator=g, device=dev) * 0.01 if r else None
+        for m in (1, 4, 16, 64):
+            x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+            for wr in sets[:2]:
+                ops.qlora_forward(x, wr, A, B, 2.0, gemv=True)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for wr in sets:
+                    ops.qlora_forward(x, wr, A, B, 2.0, gemv=True)
+            graph.replay()
+            torch.cuda.synchronize()
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            for _ in range(reps):
+                graph.replay()
+            e_ev.record()
+            torch.cuda.synchronize()
+            us = s_ev.elapsed_time(e_ev) * 1000.0 / (reps * nsets)
+            gbs = wbytes / (us * 1e-6) / 1e9
+            out[f"{name}_{n}x{k}_m{m}"] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                                          "frac_of_hbm": round(gbs / peak_gbs, 3),
+                                          "lora": bool(r)}
+            del graph
+        del sets
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_reference(a):
@@ -325,6 +379,12 @@ def main():
         "gpu_launches": int(launches),
         "e2e": e2e,
     }
+    if world == 1 and not a.no_gemv:
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        out["gemv"] = {"metric": "NF4 GEMV decode HBM GB/s (weight bytes / time, CUDA-graph replay, "
+                                 "weights rotated over > 2x L2)", "peak_gbs": hbm,
+                       "peak_source": "of measured (hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
+                       "results": gemv_sweep(dev, hbm)}
     if world == 1 and not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(a, a.cpu_seq)
     print(json.dumps(out), flush=True)

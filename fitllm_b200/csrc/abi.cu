@@ -131,18 +131,20 @@ struct FwdPlan {
   void* t_pad;     // bf16 [M,64]              (rank > 0)
   void* b_pad;     // bf16 [N,64] = s.B        (GEMM path, rank > 0)
   float* partial;  // fp32 [splits,M,N]        (GEMV path)
+  float* t_part;   // fp32 [slices,M,r]        (GEMV path, rank > 0: split T = x.A^T)
 };
 
 size_t plan_fwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, int sms, FwdPlan* p) {
-  p->gemv = (m <= 64) && (n % 64 == 0);
+  p->gemv = (m <= 64) && (n % 64 == 0) && (k % 256 == 0);
   p->wdeq = p->a_bf16 = p->t_pad = p->b_pad = nullptr;
-  p->partial = nullptr;
+  p->partial = p->t_part = nullptr;
   if (rank > 0) {
     p->a_bf16 = c.take(bf16_bytes(static_cast<int64_t>(rank) * k));
     p->t_pad = c.take(bf16_bytes(m * 64));
   }
   if (p->gemv) {
     p->partial = static_cast<float*>(c.take(fitq::gemv_partial_bytes(m, n, k, sms, nullptr)));
+    if (rank > 0) p->t_part = static_cast<float*>(c.take(fitq::lora_rowproj_small_workspace(m, k, rank)));
   } else {
     p->wdeq = c.take(bf16_bytes(n * k));
     if (rank > 0) p->b_pad = c.take(bf16_bytes(n * 64));
@@ -296,8 +298,9 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   FwdPlan p;
   const size_t need = plan_fwd(probe, m, N, K, rank, sms, &p);
   if (force_gemv && !p.gemv)
-    return fail(FITQ_ERR_SHAPE, "nf4_gemv: needs M <= 64 and N %% 64 == 0 (M=%lld N=%lld)",
-                (long long)m, (long long)N);
+    return fail(FITQ_ERR_SHAPE,
+                "nf4_gemv: needs M <= 64, N %% 64 == 0 and K %% 256 == 0 (M=%lld N=%lld K=%lld)",
+                (long long)m, (long long)N, (long long)K);
   if (workspace_bytes < need || (need > 0 && !workspace))
     return fail(FITQ_ERR_WORKSPACE, "qlora_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
   Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
@@ -307,7 +310,9 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   if (rank > 0) {
     rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
     if (rc) return launch_status(rc, "lora_a cast");
-    rc = fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
+    rc = p.gemv ? fitq::launch_lora_rowproj_small(x, K, m, K, p.a_bf16, rank, p.t_part, p.t_pad,
+                                                  t_out, st)
+                : fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
     if (rc) return launch_status(rc, "lora T = x.A^T");
   }
   if (p.gemv) {
@@ -334,7 +339,7 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   g.m = m; g.n = N; g.k = K;
   g.lora_k = rank;
   g.status = status_ptr();
-  return launch_status(fitq::launch_gemm_bf16_tn(g, st, sms), "tcgen05 gemm");
+  return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm");
 }
 
 int fitq_qlora_fwd(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
@@ -434,7 +439,7 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
   g.m = m; g.n = K; g.k = N;
   g.lora_k = rank;
   g.status = status_ptr();
-  return launch_status(fitq::launch_gemm_bf16_tn(g, st, sms), "tcgen05 gemm (dx)");
+  return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm (dx)");
 }
 
 int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, int64_t m,
@@ -457,7 +462,7 @@ int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, 
   g.m = m; g.n = n; g.k = k;
   g.lora_k = 0;
   g.status = status_ptr();
-  return launch_status(fitq::launch_gemm_bf16_tn(g, static_cast<cudaStream_t>(stream), sms),
+  return launch_status(fitq::launch_gemm(g, static_cast<cudaStream_t>(stream), sms),
                        "tcgen05 gemm");
 }
 

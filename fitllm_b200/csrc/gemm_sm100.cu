@@ -12,6 +12,8 @@
 // two more tensor maps and accumulated into the same TMEM accumulator, so the
 // adapter costs r/16 extra MMA instructions per tile and no extra pass.
 // Every mbarrier wait is bounded (common.cuh); no TMA multicast is used.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -36,14 +38,16 @@ struct Params {
   int m, n, k;
   int lora_k;
   int num_m, num_n;
+  int group_m;  // M-tiles per raster group (L2 reuse of the B tiles)
   int* status;
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
-  const int per_group = GROUP_M * num_n;
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb,
+                                            int& nb) {
+  const int per_group = group_m * num_n;
   const int group = tile / per_group;
-  const int first_m = group * GROUP_M;
-  const int gsz = min(num_m - first_m, GROUP_M);
+  const int first_m = group * group_m;
+  const int gsz = min(num_m - first_m, group_m);
   const int local = tile - group * per_group;
   mb = first_m + local % gsz;
   nb = local / gsz;
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t armed = 0, armed_parity = 0;  // per-stage bit: armed / parity of last arm
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         int mb, nb;
-        tile_coords(tile, p.num_m, p.num_n, mb, nb);
+        tile_coords(tile, p.num_m, p.num_n, p.group_m, mb, nb);
         bool ok = true;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
@@ -175,7 +179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
-      tile_coords(tile, p.num_m, p.num_n, mb, nb);
+      tile_coords(tile, p.num_m, p.num_n, p.group_m, mb, nb);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const int row = mb * BM + quarter * 32 + lane;
@@ -304,6 +308,11 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   p.num_m = static_cast<int>((g.m + BM - 1) / BM);
   p.num_n = static_cast<int>((g.n + BN - 1) / BN);
   p.status = g.status;
+  {
+    const char* gm = getenv("FITQ_GEMM_GROUP_M");
+    p.group_m = gm ? atoi(gm) : GROUP_M;
+    if (p.group_m < 1) p.group_m = GROUP_M;
+  }
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -320,6 +329,21 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms) {
+  const char* v = getenv("FITQ_GEMM_VARIANT");
+  bool pair;
+  if (v && v[0] == '1') {
+    pair = false;
+  } else if (v && v[0] == '2') {
+    pair = true;
+  } else {
+    // pair tiles: enough of them for ~4 waves of 74 clusters
+    const int64_t tiles2 = ((g.m + 255) / 256) * ((g.n + 255) / 256);
+    pair = tiles2 >= 4 * static_cast<int64_t>(num_sms / 2);
+  }
+  return pair ? launch_gemm_bf16_tn_2cta(g, st, num_sms) : launch_gemm_bf16_tn(g, st, num_sms);
 }
 
 }  // namespace fitq

@@ -80,9 +80,9 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
   if (!nested && !w->absmax_f32)
     return fail(FITQ_ERR_ARG, "nf4_gemv_noalloc: weight has no absmax");
   const int64_t N = w->n_out, K = w->k_in;
-  if (m < 1 || m > 64 || N <= 0 || K <= 0 || K % 64 != 0 || N % 64 != 0 || N >= (1ll << 31) ||
+  if (m < 1 || m > 64 || N <= 0 || K <= 0 || K % 256 != 0 || N % 64 != 0 || N >= (1ll << 31) ||
       K >= (1ll << 31))
-    return fail(FITQ_ERR_SHAPE, "nf4_gemv_noalloc: needs 1 <= M <= 64, K % 64 == 0, N % 64 == 0");
+    return fail(FITQ_ERR_SHAPE, "nf4_gemv_noalloc: needs 1 <= M <= 64, K % 256 == 0, N % 64 == 0");
   if (!(rank == 0 || rank == 16 || rank == 32 || rank == 48 || rank == 64))
     return fail(FITQ_ERR_UNSUPPORTED, "nf4_gemv_noalloc: rank must be 0, 16, 32, 48 or 64");
   if (rank > 0 && (!lora_a || !lora_b))
@@ -98,11 +98,12 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
       return fail(FITQ_ERR_NO_DEVICE, "nf4_gemv_noalloc: cannot query the device");
     }
   }
-  // Scratch layout: [A as bf16 (r x K)] [T (M x 64 bf16)] [split-K partials].
+  // Scratch layout: [A as bf16 (r x K)] [T (M x 64 bf16)] [T partials] [split-K partials].
   const size_t a_bytes = rank > 0 ? up256(static_cast<size_t>(rank) * K * 2) : 0;
   const size_t t_bytes = rank > 0 ? up256(static_cast<size_t>(m) * 64 * 2) : 0;
+  const size_t tp_bytes = rank > 0 ? up256(fitq::lora_rowproj_small_workspace(m, K, rank)) : 0;
   const size_t p_bytes = up256(fitq::gemv_partial_bytes(m, N, K, sms, nullptr));
-  const size_t need = a_bytes + t_bytes + p_bytes;
+  const size_t need = a_bytes + t_bytes + tp_bytes + p_bytes;
   if (need > kNoAllocScratchBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),
@@ -116,7 +117,8 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
   if (rc) return rc;
   void* a_bf16 = rank > 0 ? base : nullptr;
   void* t_pad = rank > 0 ? base + a_bytes : nullptr;
-  float* partial = reinterpret_cast<float*>(base + a_bytes + t_bytes);
+  float* t_part = rank > 0 ? reinterpret_cast<float*>(base + a_bytes + t_bytes) : nullptr;
+  float* partial = reinterpret_cast<float*>(base + a_bytes + t_bytes + tp_bytes);
 
   fitq::Nf4Args a;
   a.packed = w->packed;
@@ -132,7 +134,7 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
   if (rank > 0) {
     if ((rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, a_bf16, st)))
       return fail(rc, "nf4_gemv_noalloc: lora_a cast launch failed");
-    if ((rc = fitq::launch_lora_rowproj(x, K, m, K, a_bf16, rank, t_pad, nullptr, st, sms)))
+    if ((rc = fitq::launch_lora_rowproj_small(x, K, m, K, a_bf16, rank, t_part, t_pad, nullptr, st)))
       return fail(rc, "nf4_gemv_noalloc: T = x.A^T launch failed");
   }
   int splits = 1;

@@ -43,6 +43,11 @@ struct GemmArgs {
   int* status;  // device status word (bounded-wait timeouts)
 };
 int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms);
+// Same contract on CTA pairs (cta_group::2, 256x256 tiles), gemm_sm100_2cta.cu.
+int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms);
+// Picks the pair kernel when there are enough 256x256 tiles to fill the GPU
+// (FITQ_GEMM_VARIANT=1cta|2cta in the environment forces one).
+int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms);
 
 // LoRA building blocks (lora.cu).
 // out[M, r] = in[M, D] . wt[r, D]^T  (bf16 in, fp32 accumulate); written as
@@ -50,6 +55,13 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms);
 // read, since r % 16 == 0) and, when non-null, into out_dense [M, r].
 int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, const void* wt_bf16,
                         int r, void* out_pad, void* out_dense, cudaStream_t st, int num_sms);
+// The same projection for few rows (M <= 64): D split over CTAs, fp32
+// partials in partial_ws (lora_rowproj_small_workspace bytes), reduced in
+// slice order into out_pad (pitch 64) and out_dense.
+size_t lora_rowproj_small_workspace(int64_t M, int64_t D, int r);
+int launch_lora_rowproj_small(const void* in, int64_t ld_in, int64_t M, int64_t D,
+                              const void* wt_bf16, int r, float* partial_ws, void* out_pad,
+                              void* out_dense, cudaStream_t st);
 // Reduction over rows:  res[r, D] = scale . p[M, r]^T . in[M, D]
 // (p bf16 with row pitch ld_p, a multiple of 8).  layout 0 writes res[r][D],
 // layout 1 res[D][r].  accumulate != 0 adds into res.  partial_ws: fp32

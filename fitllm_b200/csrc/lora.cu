@@ -78,6 +78,73 @@ __global__ void __launch_bounds__(128) lora_rowproj_kernel(const __nv_bfloat16* 
   }
 }
 
+// Few-row variant of the projection (decode / verify, M <= 64): the D axis is
+// split over gridDim.y slices of kRowprojSlice columns so that a handful of
+// rows still spreads over many CTAs; partial[slice][m][j] in fp32, reduced by
+// lora_rowproj_finish_kernel in slice order.
+constexpr int kRowprojSlice = 512;
+
+template <int R>
+__global__ void __launch_bounds__(128) lora_rowproj_split_kernel(
+    const __nv_bfloat16* __restrict__ in, int64_t ld, int64_t M, int64_t D,
+    const __nv_bfloat16* __restrict__ wt, float* __restrict__ partial) {
+  constexpr int NT = R / 8;
+  __shared__ float red[4][16][R];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 16;
+  const int64_t ra = m0 + g, rb = m0 + g + 8;
+  const int64_t d0 = static_cast<int64_t>(blockIdx.y) * kRowprojSlice;
+  const int64_t d1 = d0 + kRowprojSlice < D ? d0 + kRowprojSlice : D;
+  float acc[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int64_t col0 = d0 + warp * 32; col0 < d1; col0 += 128) {
+    const int64_t col = col0 + 8 * q;
+    const uint4 xa = ra < M ? __ldg(reinterpret_cast<const uint4*>(in + ra * ld + col)) : zero;
+    const uint4 xb = rb < M ? __ldg(reinterpret_cast<const uint4*>(in + rb * ld + col)) : zero;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint4 wb = __ldg(reinterpret_cast<const uint4*>(wt + (int64_t)(8 * t + g) * D + col));
+      mma_bf16_16816(acc[t], xa.x, xb.x, xa.y, xb.y, wb.x, wb.y);
+      mma_bf16_16816(acc[t], xa.z, xb.z, xa.w, xb.w, wb.z, wb.w);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    red[warp][g][8 * t + 2 * q] = acc[t][0];
+    red[warp][g][8 * t + 2 * q + 1] = acc[t][1];
+    red[warp][g + 8][8 * t + 2 * q] = acc[t][2];
+    red[warp][g + 8][8 * t + 2 * q + 1] = acc[t][3];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 16 * R; e += 128) {
+    const int row = e / R, col = e % R;
+    const int64_t m = m0 + row;
+    if (m >= M) continue;
+    const float v = red[0][row][col] + red[1][row][col] + red[2][row][col] + red[3][row][col];
+    partial[(static_cast<int64_t>(blockIdx.y) * M + m) * R + col] = v;
+  }
+}
+
+__global__ void lora_rowproj_finish_kernel(const float* __restrict__ partial, int slices,
+                                           int64_t M, int R, __nv_bfloat16* __restrict__ out_pad,
+                                           __nv_bfloat16* __restrict__ out_dense) {
+  const int64_t total = M * R;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int sl = 0; sl < slices; ++sl) s += partial[sl * total + e];
+    const int64_t m = e / R, j = e % R;
+    const __nv_bfloat16 v = __float2bfloat16_rn(s);
+    out_pad[m * 64 + j] = v;
+    if (out_dense) out_dense[e] = v;
+  }
+}
+
 // Partial row reduction:  partial[chunk][j][d] = sum_{m in chunk} p[m][j0+j] * in[m][d]
 // for a 16-wide group of adapter columns j0 = 16*blockIdx.z.  CTA = 8 warps
 // over one 256-column tile of D (8 columns per lane); warps take rows
@@ -232,6 +299,33 @@ int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, con
     case 64: lora_rowproj_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
     default: return FITQ_ERR_UNSUPPORTED;
   }
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+size_t lora_rowproj_small_workspace(int64_t M, int64_t D, int r) {
+  const int64_t slices = (D + kRowprojSlice - 1) / kRowprojSlice;
+  return static_cast<size_t>(slices * M * r) * sizeof(float);
+}
+
+int launch_lora_rowproj_small(const void* in, int64_t ld_in, int64_t M, int64_t D,
+                              const void* wt_bf16, int r, float* partial_ws, void* out_pad,
+                              void* out_dense, cudaStream_t st) {
+  const int64_t slices = (D + kRowprojSlice - 1) / kRowprojSlice;
+  dim3 grid(static_cast<unsigned>((M + 15) / 16), static_cast<unsigned>(slices));
+  auto i = static_cast<const __nv_bfloat16*>(in);
+  auto w = static_cast<const __nv_bfloat16*>(wt_bf16);
+  switch (r) {
+    case 16: lora_rowproj_split_kernel<16><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
+    case 32: lora_rowproj_split_kernel<32><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
+    case 48: lora_rowproj_split_kernel<48><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
+    case 64: lora_rowproj_split_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
+    default: return FITQ_ERR_UNSUPPORTED;
+  }
+  note_launch();
+  lora_rowproj_finish_kernel<<<grid_for(M * r, 256, 148), 256, 0, st>>>(
+      partial_ws, static_cast<int>(slices), M, r, static_cast<__nv_bfloat16*>(out_pad),
+      static_cast<__nv_bfloat16*>(out_dense));
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 

@@ -143,8 +143,9 @@ FITQ_API int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void*
                    fitq_stream_t stream);
 
 /* Decode / speculative-verify projection for M <= 64 rows: the NF4 weight is
- * streamed once from HBM and dequantised in registers.  Same arithmetic
- * contract as fitq_qlora_fwd. */
+ * streamed once from HBM and decoded on the fly into tensor-core operands.
+ * Same arithmetic contract as fitq_qlora_fwd; needs N % 64 == 0 and
+ * K % 256 == 0 (fitq_qlora_fwd uses it for such shapes when M <= 64). */
 FITQ_API size_t fitq_nf4_gemv_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank);
 FITQ_API int fitq_nf4_gemv(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
                   const float* lora_b, int rank, float scale, const void* bias, void* y,
@@ -215,7 +216,7 @@ FITQ_API long long fitq_launch_count(void);
  * the scratch comes from one fixed array of FITQ_GEMV_NOALLOC_SCRATCH_BYTES
  * (8 MiB) built into the library, which every GPU that loads the library
  * keeps until the process exits.  Same arguments and arithmetic as
- * fitq_nf4_gemv (M <= 64, N % 64 == 0, K % 64 == 0, rank 0/16/32/48/64);
+ * fitq_nf4_gemv (M <= 64, N % 64 == 0, K % 256 == 0, rank 0/16/32/48/64);
  * shapes whose scratch exceeds the array return FITQ_ERR_WORKSPACE with the
  * needed size in fitq_last_error().  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) with that device current, so

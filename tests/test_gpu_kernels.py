@@ -81,9 +81,11 @@ def test_quantize_bit_exact(cuda_dev, n, k):
     assert np.float32(qs.offset) == st.offset
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (1, 16, 64), (300, 272, 192),
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (1, 16, 64), (300, 272, 192), (1024, 1024, 4096),
                                    (512, 1024, 512), (1000, 768, 1024)])
-def test_gemm_bf16_tn(cuda_dev, m, n, k):
+@pytest.mark.parametrize("variant", ["1cta", "2cta"])
+def test_gemm_bf16_tn(cuda_dev, m, n, k, variant, monkeypatch):
+    monkeypatch.setenv("FITQ_GEMM_VARIANT", variant)
     from fitllm_b200.ops import gemm_bf16_tn
     g = torch.Generator(device="cpu").manual_seed(m * 7 + n)
     a = _bf16(torch.randn(m, k, generator=g)).to(cuda_dev)
@@ -112,7 +114,9 @@ def _qlora_case(m, n, k, r, seed, dev):
 
 @pytest.mark.parametrize("m,n,k,r", [(512, 256, 512, 16), (200, 512, 256, 16), (130, 128, 128, 32),
                                      (384, 1024, 640, 64), (256, 320, 256, 0)])
-def test_qlora_forward_backward(cuda_dev, m, n, k, r):
+@pytest.mark.parametrize("variant", ["1cta", "2cta"])
+def test_qlora_forward_backward(cuda_dev, m, n, k, r, variant, monkeypatch):
+    monkeypatch.setenv("FITQ_GEMM_VARIANT", variant)
     from fitllm_b200 import ops
     s = 2.0
     st, wref, w_deq, A, B, x, dy = _qlora_case(m, n, k, r, 7 + m, cuda_dev)

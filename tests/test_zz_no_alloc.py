@@ -79,7 +79,7 @@ def test_noalloc_matches_workspace_gemv_two_calls(cuda_dev, m, n, k, rank):
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda_dev):
     from fitllm_b200 import _lib
     L = _lib.load()
-    n, k, m = 65536, 64, 64  # 64 x 65536 fp32 partial products alone exceed 8 MiB
+    n, k, m = 65536, 256, 64  # 64 x 65536 fp32 partial products alone exceed 8 MiB
     packed = torch.zeros(n * k // 2, dtype=torch.uint8, device=cuda_dev)
     absmax = torch.ones(n * k // 64, dtype=torch.float32, device=cuda_dev)
     qm = torch.tensor(onf4.NF4_LEVELS, device=cuda_dev)
