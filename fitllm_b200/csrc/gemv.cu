@@ -90,6 +90,311 @@ __device__ __forceinline__ uint32_t lut(uint32_t v, uint32_t lane4) {
   return *reinterpret_cast<const uint32_t*>(g_gemv_smem + lut_off<J>(v, lane4));
 }
 
+// ---------------------------------------------------------------------------
+// Decode kernel for M <= 8 tokens (one n8 token tile).
+//
+// A CTA owns one K slice of kw*4 blocks and a strided set of 16-row tiles;
+// warp (rg, p) = (warp / kw, warp % kw) covers blocks [4p, 4p+4) of the slice
+// for every rtg-th tile of the CTA.  Because a warp's K range never changes,
+// its x fragments live in registers for the whole kernel.
+//
+// HBM only runs near its peak with 64-100 KB of reads in flight per SM, more
+// than registers can hold next to the decode, so each warp streams its own
+// tiles (16 rows x 128 bytes) into a private 3-stage shared-memory ring with
+// 16-byte cp.async copies: two tiles in flight while the third is decoded,
+// with no cross-warp synchronisation (a warp only reads what it copied).
+// Rows sit at a 160-byte pitch so the 8-byte fragment reads are
+// conflict-free.  The absmax codes and nested scales (8 bytes per row and
+// tile) ride a small register ring two tiles ahead.
+//
+// The code table sits on a 64 KB boundary of the CTA's shared window, so one
+// prmt of (packed byte, lane base) yields the complete shared address of a
+// lane's bf16 pair and the lookup is a single ld.shared.  The nested absmax
+// map lives in the unused upper half of each 256-byte entry (8 copies, one per
+// lane row g): an absmax costs one prmt + one ld.shared + the reference's two
+// rounded fp32 ops.  The kw partial sums of a tile are combined through shared
+// memory once per round of 3 tiles, in k order (deterministic), and written as
+// fp32 split-K partials partial[slice][m][n].
+// ---------------------------------------------------------------------------
+constexpr int kDecKB = 4;                      // blocks per warp and tile
+constexpr int kDecRing = 3;                    // ring stages per warp
+constexpr int kDecDepth = kDecRing - 1;        // tiles in flight ahead of the decoded one
+constexpr int kDecPitch = 160;                 // bytes per staged row (128 used)
+constexpr int kDecStage = 16 * kDecPitch;      // one staged tile
+constexpr int kDecRingBytes = kWarps * kDecRing * kDecStage;
+constexpr int kDecSmem = 232448;               // the whole 227 KB: table alignment slack + table + ring + reduction
+
+struct Gemv8Plan {
+  int kw, rtg, cs, slices;
+  int lkw, lrtg, lqn;  // log2 of kw, rtg and of the token lanes stored per row (qn)
+};
+
+template <bool NESTED>
+struct ScaleBuf {
+  uint32_t ca, cb;  // absmax codes of the 4 blocks of rows a = 16t+g and b = a+8
+  float na, nb;     // nested absmax (a 4-aligned block range stays in one 256-block group)
+  float4 fa, fb;    // fp32 absmax when not double-quantised
+};
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// Shared address of byte J of v in the 64 KB-aligned table: bits 16..31 and
+// 0..7 from base (table | lane offset), bits 8..15 = the byte.
+template <int J>
+__device__ __forceinline__ uint32_t tbl_addr(uint32_t v, uint32_t base) {
+  uint32_t r;
+  constexpr uint32_t sel = 0x7600u | (static_cast<uint32_t>(J) << 4) | 4u;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(base), "n"(sel));
+  return r;
+}
+
+template <int J>
+__device__ __forceinline__ uint32_t tbl_u32(uint32_t v, uint32_t base) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(tbl_addr<J>(v, base)));
+  return r;
+}
+
+template <int J>
+__device__ __forceinline__ float tbl_f32(uint32_t v, uint32_t base) {
+  return __uint_as_float(tbl_u32<J>(v, base));
+}
+
+template <bool NESTED>
+__device__ __forceinline__ void load_scales(ScaleBuf<NESTED>& b, const Nf4Args& w, int fa,
+                                            int nblk8) {
+  if (NESTED) {
+    b.ca = __ldg(reinterpret_cast<const uint32_t*>(w.absmax_code + fa));
+    b.cb = __ldg(reinterpret_cast<const uint32_t*>(w.absmax_code + fa + nblk8));
+    b.na = __ldg(w.nested_absmax + (fa >> 8));
+    b.nb = __ldg(w.nested_absmax + ((fa + nblk8) >> 8));
+  } else {
+    b.fa = __ldg(reinterpret_cast<const float4*>(w.absmax_f32 + fa));
+    b.fb = __ldg(reinterpret_cast<const float4*>(w.absmax_f32 + fa + nblk8));
+  }
+}
+
+__device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+template <int C, bool NESTED>
+__device__ __forceinline__ void block_scales(const ScaleBuf<NESTED>& b, uint32_t nq_base,
+                                             float offset, float& am_a, float& am_b) {
+  if (NESTED) {
+    am_a = __fadd_rn(__fmul_rn(tbl_f32<C>(b.ca, nq_base), b.na), offset);
+    am_b = __fadd_rn(__fmul_rn(tbl_f32<C>(b.cb, nq_base), b.nb), offset);
+  } else {
+    am_a = C == 0 ? b.fa.x : C == 1 ? b.fa.y : C == 2 ? b.fa.z : b.fa.w;
+    am_b = C == 0 ? b.fb.x : C == 1 ? b.fb.y : C == 2 ? b.fb.z : b.fb.w;
+  }
+}
+
+// One 16x64 block: 4 MMAs over the decoded A fragments, scaled per row.
+__device__ __forceinline__ void block_mma(float4& acc, uint2 wa, uint2 wb, uint4 x0, uint4 x1,
+                                          uint32_t lb, float am_a, float am_b) {
+  float t[4];
+  // byte 2i of the lane's 8 bytes -> cols 16q+4i+{0,1}, byte 2i+1 -> cols 16q+4i+{2,3}
+  mma16816_zc(t, tbl_u32<0>(wa.x, lb), tbl_u32<0>(wb.x, lb), tbl_u32<1>(wa.x, lb),
+              tbl_u32<1>(wb.x, lb), x0.x, x0.y);
+  mma16816(t, tbl_u32<2>(wa.x, lb), tbl_u32<2>(wb.x, lb), tbl_u32<3>(wa.x, lb),
+           tbl_u32<3>(wb.x, lb), x0.z, x0.w);
+  mma16816(t, tbl_u32<0>(wa.y, lb), tbl_u32<0>(wb.y, lb), tbl_u32<1>(wa.y, lb),
+           tbl_u32<1>(wb.y, lb), x1.x, x1.y);
+  mma16816(t, tbl_u32<2>(wa.y, lb), tbl_u32<2>(wb.y, lb), tbl_u32<3>(wa.y, lb),
+           tbl_u32<3>(wb.y, lb), x1.z, x1.w);
+  acc.x = fmaf(t[0], am_a, acc.x);
+  acc.y = fmaf(t[1], am_a, acc.y);
+  acc.z = fmaf(t[2], am_b, acc.z);
+  acc.w = fmaf(t[3], am_b, acc.w);
+}
+
+template <int C, bool NESTED>
+__device__ __forceinline__ void stage_block(float4& acc, uint32_t wrow, const ScaleBuf<NESTED>& sb,
+                                            const uint4 (&xr)[kDecKB][2], uint32_t lb,
+                                            uint32_t nq_base, float offset) {
+  float am_a, am_b;
+  block_scales<C>(sb, nq_base, offset, am_a, am_b);
+  const uint2 wa = lds64(wrow + 32 * C), wb = lds64(wrow + 8 * kDecPitch + 32 * C);
+  block_mma(acc, wa, wb, xr[C][0], xr[C][1], lb, am_a, am_b);
+}
+
+// Partial sums of one staged tile: lane (g, q) returns rows (g, g+8) x tokens (2q, 2q+1).
+template <bool NESTED>
+__device__ __forceinline__ float4 compute_tile(uint32_t wrow, const ScaleBuf<NESTED>& sb,
+                                               const uint4 (&xr)[kDecKB][2], uint32_t lb,
+                                               uint32_t nq_base, float offset) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  stage_block<0>(acc, wrow, sb, xr, lb, nq_base, offset);
+  stage_block<1>(acc, wrow, sb, xr, lb, nq_base, offset);
+  stage_block<2>(acc, wrow, sb, xr, lb, nq_base, offset);
+  stage_block<3>(acc, wrow, sb, xr, lb, nq_base, offset);
+  return acc;
+}
+
+template <bool NESTED>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_gemv_dec_kernel(Nf4Args w, const __nv_bfloat16* __restrict__ x, int M, Gemv8Plan pl,
+                        float* __restrict__ partial) {
+  constexpr int R = kDecRing, D = kDecDepth;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int K = static_cast<int>(w.k_in), N = static_cast<int>(w.n_out);
+  const int nblk = K / 64, T = N / 16;
+  const int qn = 1 << pl.lqn;  // token lanes q < qn hold tokens 2q, 2q+1 < 2*qn >= M
+
+  // Shared layout: [slack below the 64 KB boundary][table 64 KB][rest].  Ring
+  // stages fill the slack first, then the rest; the reduction area follows.
+  const uint32_t sbase = smem_u32(g_gemv_smem);
+  const uint32_t tbl = (sbase + 0xFFFFu) & ~0xFFFFu;
+  const int n_slack = static_cast<int>((tbl - sbase) / kDecStage);
+  const uint32_t after = tbl + kTableBytes;
+  const int n_ring = kWarps * R;
+  const uint32_t red_addr =
+      after + static_cast<uint32_t>(n_ring > n_slack ? n_ring - n_slack : 0) * kDecStage;
+  float4* const red = reinterpret_cast<float4*>(g_gemv_smem + (red_addr - sbase));
+  const int red_warp = 8 * qn;  // float4 slots per warp and tile
+
+  // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g
+  uint32_t* table = reinterpret_cast<uint32_t*>(g_gemv_smem + (tbl - sbase));
+  for (int i = threadIdx.x; i < 256 * 40; i += kThreads) {
+    const int e = i / 40, s = i % 40;
+    if (s < 32) table[e * 64 + s] = pack_bf16x2(w.quant_map[e >> 4], w.quant_map[e & 15]);
+    else if (NESTED) table[e * 64 + s] = __float_as_uint(w.nested_quant_map[e]);
+  }
+
+  const int slice = blockIdx.x / pl.cs, j = blockIdx.x % pl.cs;
+  const int p = warp & (pl.kw - 1), rg = warp >> pl.lkw;
+  const int b0 = (slice * pl.kw + p) * kDecKB;  // first block of this warp's K range
+
+  uint4 xr[kDecKB][2];
+#pragma unroll
+  for (int c = 0; c < kDecKB; ++c) {
+    if (g < M) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(g) * K +
+                                                        (b0 + c) * 64 + 16 * q);
+      xr[c][0] = __ldg(src);
+      xr[c][1] = __ldg(src + 1);
+    } else {
+      xr[c][0] = make_uint4(0, 0, 0, 0);
+      xr[c][1] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  // ring stages of this warp
+  uint32_t stage[R];
+#pragma unroll
+  for (int s = 0; s < R; ++s) {
+    const int i = warp * R + s;
+    stage[s] = i < n_slack ? sbase + static_cast<uint32_t>(i) * kDecStage
+                           : after + static_cast<uint32_t>(i - n_slack) * kDecStage;
+  }
+
+  // this warp's tiles: t_u = j + cs * (rg + rtg * u)
+  const int tstride = pl.cs << pl.lrtg;
+  const int t0 = j + pl.cs * rg;
+  const int n_u = t0 < T ? (T - 1 - t0) / tstride + 1 : 0;
+  const int n_u_max = j < T ? (T - 1 - j) / tstride + 1 : 0;  // row group 0 has the most
+  const int rounds = (n_u_max + D) / R;
+  const int nblk8 = 8 * nblk;
+  const int fstep = 16 * tstride * nblk;   // flat-block step between the warp's tiles
+  int f_next = (16 * t0 + g) * nblk + b0;   // flat block of row a of the next tile's scales
+  // copies: lane covers 16 bytes (lane & 7) of rows (lane >> 3) + 4j, j = 0..3
+  const int64_t row_bytes = K / 2;
+  const uint8_t* src = w.packed + (static_cast<int64_t>(16 * t0 + (lane >> 3)) * nblk + b0) * 32 +
+                       16 * (lane & 7);
+  const int64_t src_step = static_cast<int64_t>(16) * tstride * row_bytes;
+  const uint32_t dst_lane = static_cast<uint32_t>((lane >> 3) * kDecPitch + 16 * (lane & 7));
+  const uint32_t rd_lane = static_cast<uint32_t>(g * kDecPitch + 8 * q);  // fragment reads
+  const uint32_t lb = tbl | (static_cast<uint32_t>(lane) << 2);
+  const uint32_t nq_base = tbl | (128u + (static_cast<uint32_t>(g) << 2));
+  const uint64_t pol = evict_first_policy();
+  __syncthreads();  // table ready
+
+  ScaleBuf<NESTED> sb[R];
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+    if (d < n_u) {
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        cp_async16(stage[d] + dst_lane + jj * 4 * kDecPitch, src + jj * 4 * row_bytes, pol);
+      load_scales(sb[d], w, f_next, nblk8);
+    }
+    cp_async_commit();
+    f_next += fstep;
+    src += src_step;
+  }
+  for (int rd = 0; rd < rounds; ++rd) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int u = rd * R + r;
+      __syncwarp();  // every lane is done with the stage refilled below (decoded last step)
+      if (u + D < n_u) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          cp_async16(stage[(r + D) % R] + dst_lane + jj * 4 * kDecPitch, src + jj * 4 * row_bytes,
+                     pol);
+        load_scales(sb[(r + D) % R], w, f_next, nblk8);
+      }
+      cp_async_commit();
+      f_next += fstep;
+      src += src_step;
+      cp_async_wait<D>();  // this lane's copies of tile u have landed
+      __syncwarp();        // ... and every other lane's
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (u < n_u) o = compute_tile(stage[r] + rd_lane, sb[r], xr, lb, nq_base, w.offset);
+      if (q < qn) red[(r * kWarps + warp) * red_warp + (g << pl.lqn) + q] = o;
+    }
+    __syncthreads();
+    // sum the kw parts of each tile of the round in k order; slot f = (g*qn + q)*4 + component
+    const int fbits = 5 + pl.lqn;
+    const int outs = (R << pl.lrtg) << fbits;
+    const float* rf = reinterpret_cast<const float*>(red);
+    for (int e = threadIdx.x; e < outs; e += kThreads) {
+      const int f = e & ((1 << fbits) - 1), hi = e >> fbits;
+      const int rgo = hi & (pl.rtg - 1), r = hi >> pl.lrtg;
+      const int ls = f >> 2, comp = f & 3;
+      const int rr = (ls >> pl.lqn) + 8 * (comp >> 1);
+      const int tk = 2 * (ls & (qn - 1)) + (comp & 1);
+      const int t = j + pl.cs * (rgo + ((rd * R + r) << pl.lrtg));
+      if (tk >= M || t >= T) continue;
+      const float* srcf = rf + (((r * kWarps + (rgo << pl.lkw)) * red_warp) << 2) + f;
+      float s = 0.f;
+      for (int pp = 0; pp < pl.kw; ++pp) s += srcf[(pp * red_warp) << 2];
+      partial[(static_cast<int64_t>(slice) * M + tk) * N + t * 16 + rr] = s;
+    }
+    __syncthreads();  // reduction area rewritten next round
+  }
+  cp_async_wait<0>();
+}
+
 template <int NT8, int CH>
 __global__ void __launch_bounds__(kThreads, 1)
     nf4_gemv_kernel(Nf4Args w, const __nv_bfloat16* __restrict__ x, int M, int rt, int kcb,
@@ -168,6 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (CH == 4) {
           ck.ca = __ldg(reinterpret_cast<const uint32_t*>(w.absmax_code + ba0 + c0));
           ck.cb = __ldg(reinterpret_cast<const uint32_t*>(w.absmax_code + bb0 + c0));
+        } else if (CH == 1) {
+          ck.ca = __ldg(w.absmax_code + ba0 + c0);
+          ck.cb = __ldg(w.absmax_code + bb0 + c0);
         } else {
           ck.ca = __ldg(reinterpret_cast<const uint16_t*>(w.absmax_code + ba0 + c0));
           ck.cb = __ldg(reinterpret_cast<const uint16_t*>(w.absmax_code + bb0 + c0));
@@ -300,50 +608,120 @@ size_t plan_smem(int nt8, int rt, int kcb) {
 Plan make_plan(int64_t m, int64_t N, int64_t K, int num_sms) {
   Plan best{0, 0, 0, 0, 0, 0, 0};
   const int nt8 = static_cast<int>((m + 7) / 8);
-  const int ch = nt8 <= 2 ? 4 : 2;
   const int64_t nblk = K / 64;
-  int64_t best_items = -1;
-  size_t best_partial = 0;
   const int rts[3] = {16, 8, 4};
   const int kcbs[6] = {128, 64, 32, 16, 8, 4};
-  for (int ri = 0; ri < 3; ++ri) {
-    const int rt = rts[ri];
-    const int kw = kWarps / rt;
-    if (N % (16 * rt) != 0) continue;
-    for (int ki = 0; ki < 6; ++ki) {
-      int kcb = kcbs[ki];
-      if (kcb % (kw * ch) != 0 || nblk % (kw * ch) != 0) continue;
-      if (kcb > nblk) kcb = static_cast<int>(nblk);
-      if (plan_smem(nt8, rt, kcb) > 200 * 1024) continue;
-      const int64_t slices = (nblk + kcb - 1) / kcb;
-      const int64_t items = (N / (16 * rt)) * slices;
-      const size_t partial = static_cast<size_t>(slices) * m * N * 4;
-      const bool enough = items >= 2 * num_sms, best_enough = best_items >= 2 * num_sms;
-      bool take = false;
-      if (best_items < 0) take = true;
-      else if (enough && !best_enough) take = true;
-      else if (enough && best_enough) take = partial < best_partial;
-      else if (!enough && !best_enough) take = items > best_items;
-      if (take) {
-        best = Plan{nt8, rt, kcb, ch, slices, N / (16 * rt), plan_smem(nt8, rt, kcb)};
-        best_items = items;
-        best_partial = partial;
+  // preferred chunk first; smaller chunks only when no plan fits (few K blocks)
+  for (int ch = nt8 <= 2 ? 4 : 2; ch >= 1 && best.rt == 0; ch /= 2) {
+    int64_t best_items = -1;
+    size_t best_partial = 0;
+    for (int ri = 0; ri < 3; ++ri) {
+      const int rt = rts[ri];
+      const int kw = kWarps / rt;
+      if (N % (16 * rt) != 0) continue;
+      for (int ki = 0; ki < 6; ++ki) {
+        int kcb = kcbs[ki];
+        if (kcb % (kw * ch) != 0 || nblk % (kw * ch) != 0) continue;
+        if (kcb > nblk) kcb = static_cast<int>(nblk);
+        if (plan_smem(nt8, rt, kcb) > 200 * 1024) continue;
+        const int64_t slices = (nblk + kcb - 1) / kcb;
+        const int64_t items = (N / (16 * rt)) * slices;
+        const size_t partial = static_cast<size_t>(slices) * m * N * 4;
+        const bool enough = items >= 2 * num_sms, best_enough = best_items >= 2 * num_sms;
+        bool take = false;
+        if (best_items < 0) take = true;
+        else if (enough && !best_enough) take = true;
+        else if (enough && best_enough) take = partial < best_partial;
+        else if (!enough && !best_enough) take = items > best_items;
+        if (take) {
+          best = Plan{nt8, rt, kcb, ch, slices, N / (16 * rt), plan_smem(nt8, rt, kcb)};
+          best_items = items;
+          best_partial = partial;
+        }
       }
     }
   }
   return best;
 }
 
+int ilog2(int v) {
+  int l = 0;
+  while ((1 << l) < v) ++l;
+  return l;
+}
+
+// M <= 8 plan: slice = 4*kw blocks dividing K/64; cs = CTAs per slice (at
+// most one per tile); the estimate is the tiles of the busiest warp, ties
+// broken towards fewer slices (less partial-sum traffic).
+Gemv8Plan make_plan8(int64_t m, int64_t N, int64_t K, int num_sms) {
+  Gemv8Plan best{};
+  const int64_t nblk = K / 64, T = N / 16;
+  int64_t best_cost = -1;
+  const int qn = m <= 2 ? 1 : m <= 4 ? 2 : 4;
+  for (int kw = 16; kw >= 1; kw /= 2) {
+    if (nblk % (kw * kDecKB) != 0) continue;
+    const int64_t slices = nblk / (kw * kDecKB);
+    if (slices > num_sms) continue;
+    const int64_t cs = num_sms / slices < T ? num_sms / slices : T;
+    const int rtg = kWarps / kw;
+    const int64_t per_cta = (T + cs - 1) / cs;
+    const int64_t cost = (per_cta + rtg - 1) / rtg;
+    if (best_cost < 0 || cost < best_cost) {
+      best = Gemv8Plan{kw, rtg, static_cast<int>(cs), static_cast<int>(slices),
+                       ilog2(kw), ilog2(rtg), ilog2(qn)};
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+// The M <= 8 kernel when a plan exists (FITQ_GEMV_WIDE=1 forces the general kernel).
+bool use_m8(int64_t m, int64_t N, int64_t K, int num_sms, Gemv8Plan* pl) {
+  const char* e = getenv("FITQ_GEMV_WIDE");
+  if (m > 8 || (e != nullptr && e[0] == '1')) return false;
+  *pl = make_plan8(m, N, K, num_sms);
+  return pl->kw != 0;
+}
+
+template <bool NESTED>
+cudaError_t launch_dec(const Nf4Args& w, const __nv_bfloat16* x, int M, const Gemv8Plan& pl,
+                       float* partial, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(nf4_gemv_dec_kernel<NESTED>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  nf4_gemv_dec_kernel<NESTED><<<pl.cs * pl.slices, kThreads, kDecSmem, st>>>(w, x, M, pl, partial);
+  note_launch();
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t gemv_partial_bytes(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* splits_out) {
-  const Plan p = make_plan(m, n_out, k_in, num_sms);
-  if (splits_out) *splits_out = static_cast<int>(p.slices);
-  return static_cast<size_t>(p.slices * m * n_out) * sizeof(float);
+  Gemv8Plan pl8;
+  int64_t slices;
+  if (use_m8(m, n_out, k_in, num_sms, &pl8)) slices = pl8.slices;
+  else slices = make_plan(m, n_out, k_in, num_sms).slices;
+  if (splits_out) *splits_out = static_cast<int>(slices);
+  return static_cast<size_t>(slices * m * n_out) * sizeof(float);
 }
 
 int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* partial,
                          cudaStream_t st, int num_sms, int* splits_out) {
+  Gemv8Plan pl;
+  if (use_m8(m, w.n_out, w.k_in, num_sms, &pl)) {
+    if (w.n_out % 16 != 0 || w.n_out * w.k_in / 2 >= (1ll << 31)) return FITQ_ERR_UNSUPPORTED;
+    auto xb = static_cast<const __nv_bfloat16*>(x);
+    const cudaError_t e = w.absmax_f32 == nullptr
+                              ? launch_dec<true>(w, xb, static_cast<int>(m), pl, partial, st)
+                              : launch_dec<false>(w, xb, static_cast<int>(m), pl, partial, st);
+    if (e != cudaSuccess) return FITQ_ERR_CUDA;
+    *splits_out = pl.slices;
+    return FITQ_OK;
+  }
   const Plan p = make_plan(m, w.n_out, w.k_in, num_sms);
   if (p.rt == 0 || p.nt8 < 1 || p.nt8 > 8) return FITQ_ERR_UNSUPPORTED;
   if ((w.k_in / 64) % 4 != 0 || w.n_out * w.k_in / 2 >= (1ll << 31)) return FITQ_ERR_UNSUPPORTED;
@@ -351,14 +729,14 @@ int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* part
   const int grid = static_cast<int>(items < num_sms ? items : num_sms);
   auto xb = static_cast<const __nv_bfloat16*>(x);
   const int M = static_cast<int>(m);
-  static bool attr[9][2] = {};
+  static bool attr[9][3] = {};
   cudaError_t e = cudaSuccess;
 #define FITQ_GEMV_CASE(T, C)                                                                      \
   if (p.nt8 == T && p.ch == C) {                                                                  \
-    if (!attr[T][C / 4]) {                                                                        \
+    if (!attr[T][C / 2]) {                                                                        \
       e = cudaFuncSetAttribute(nf4_gemv_kernel<T, C>,                                             \
                                cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);          \
-      attr[T][C / 4] = (e == cudaSuccess);                                                        \
+      attr[T][C / 2] = (e == cudaSuccess);                                                        \
     }                                                                                             \
     nf4_gemv_kernel<T, C><<<grid, kThreads, p.smem, st>>>(w, xb, M, p.rt, p.kcb,                  \
                                                            static_cast<int>(p.row_groups),        \
@@ -373,6 +751,16 @@ int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* part
   FITQ_GEMV_CASE(6, 2)
   FITQ_GEMV_CASE(7, 2)
   FITQ_GEMV_CASE(8, 2)
+  FITQ_GEMV_CASE(1, 2)
+  FITQ_GEMV_CASE(2, 2)
+  FITQ_GEMV_CASE(1, 1)
+  FITQ_GEMV_CASE(2, 1)
+  FITQ_GEMV_CASE(3, 1)
+  FITQ_GEMV_CASE(4, 1)
+  FITQ_GEMV_CASE(5, 1)
+  FITQ_GEMV_CASE(6, 1)
+  FITQ_GEMV_CASE(7, 1)
+  FITQ_GEMV_CASE(8, 1)
 #undef FITQ_GEMV_CASE
   if (e != cudaSuccess) return FITQ_ERR_CUDA;
   *splits_out = static_cast<int>(p.slices);

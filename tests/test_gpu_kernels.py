@@ -158,3 +158,31 @@ def test_gemv_paths(cuda_dev, m, n, k, r):
     # the GEMM path on the same inputs agrees too
     y2, _ = ops.qlora_forward(x.to(cuda_dev), wref, Ad, Bd, s, bias=bias.to(cuda_dev))
     assert onf4.rel_err(y2.float().cpu().numpy(), ref) < REL_TOL
+
+
+@pytest.mark.parametrize("variant", ["m8", "wide"])
+@pytest.mark.parametrize("m,n,k,r,nested", [(1, 2048, 5120, 16, True), (3, 512, 27648, 0, True),
+                                            (8, 3072, 1024, 16, False), (5, 1024, 5120, 0, False),
+                                            (1, 64, 256, 0, True)])
+def test_gemv_decode_kernels(cuda_dev, monkeypatch, variant, m, n, k, r, nested):
+    """The M <= 8 decode kernel (several K slices, reduction rounds and ring
+    depths across these shapes) and the general skinny kernel, on
+    double-quantised and plain fp32 absmax weights."""
+    monkeypatch.setenv("FITQ_GEMV_WIDE", "1" if variant == "wide" else "0")
+    from fitllm_b200 import ops
+    from fitllm_b200.nf4 import Nf4WeightCRef, QuantState
+    s = 2.0
+    st, wref, w_deq, A, B, x, dy = _qlora_case(m, n, k, r, 57 + m + n, cuda_dev)
+    if not nested:  # same block scales, as fp32 absmax
+        packed, _ = _state_to_device(st, cuda_dev)
+        qs = QuantState(absmax=torch.from_numpy(onf4.absmax_decode(st).astype(np.float32)).to(cuda_dev),
+                        shape=st.shape, quant_map=torch.from_numpy(st.quant_map.copy()).to(cuda_dev))
+        wref = Nf4WeightCRef(packed, qs)
+    Ad = A.to(cuda_dev) if r else None
+    Bd = B.to(cuda_dev) if r else None
+    y, _ = ops.qlora_forward(x.to(cuda_dev), wref, Ad, Bd, s, gemv=True)
+    Anp = A.numpy() if r else np.zeros((0, k), np.float32)
+    Bnp = B.numpy() if r else np.zeros((n, 0), np.float32)
+    ref = onf4.qlora_forward(x.float().numpy(), w_deq, Anp, Bnp, s)
+    assert onf4.rel_err(y.float().cpu().numpy(), ref) < REL_TOL
+    assert ops.device_status() == 0
