@@ -125,19 +125,27 @@ int launch_status(int rc, const char* what) {
 
 // Workspace layout of the forward (shared by the size query and the call).
 struct FwdPlan {
-  bool gemv;
+  bool gemv;       // M <= 64 skinny path
+  bool dec;        // M <= 8 single-launch decode kernel
+  int slices;      // decode K slices
   void* wdeq;      // bf16 [N,K]               (GEMM path)
-  void* a_bf16;    // bf16 [r,K]               (rank > 0)
-  void* t_pad;     // bf16 [M,64]              (rank > 0)
+  void* a_bf16;    // bf16 [r,K]               (rank > 0, not decode)
+  void* t_pad;     // bf16 [M,64]              (rank > 0, not decode)
   void* b_pad;     // bf16 [N,64] = s.B        (GEMM path, rank > 0)
-  float* partial;  // fp32 [splits,M,N]        (GEMV path)
-  float* t_part;   // fp32 [slices,M,r]        (GEMV path, rank > 0: split T = x.A^T)
+  float* partial;  // fp32 [splits,M,N]        (GEMV paths)
+  float* t_part;   // fp32 partials of T = x.A^T (GEMV paths, rank > 0)
 };
 
 size_t plan_fwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, int sms, FwdPlan* p) {
+  *p = FwdPlan{};
   p->gemv = (m <= 64) && (n % 64 == 0) && (k % 256 == 0);
-  p->wdeq = p->a_bf16 = p->t_pad = p->b_pad = nullptr;
-  p->partial = p->t_part = nullptr;
+  p->dec = p->gemv && fitq::gemv_dec_plan(m, n, k, sms, &p->slices);
+  if (p->dec) {
+    if (fitq::gemv_dec_needs_partial(p->slices, rank))
+      p->partial = static_cast<float*>(c.take(static_cast<size_t>(p->slices * m * n) * sizeof(float)));
+    if (rank > 0) p->t_part = static_cast<float*>(c.take(fitq::lora_t_workspace(m, k, rank)));
+    return c.used;
+  }
   if (rank > 0) {
     p->a_bf16 = c.take(bf16_bytes(static_cast<int64_t>(rank) * k));
     p->t_pad = c.take(bf16_bytes(m * 64));
@@ -287,6 +295,7 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   if (m <= 0 || m >= (1ll << 31)) return fail(FITQ_ERR_SHAPE, "qlora_fwd: bad M=%lld", (long long)m);
   if (!valid_rank(rank)) return fail(FITQ_ERR_UNSUPPORTED, "qlora_fwd: rank %d not in {0,16,32,48,64}", rank);
   if (rank > 0 && (!lora_a || !lora_b)) return fail(FITQ_ERR_ARG, "qlora_fwd: lora_a/lora_b required for rank > 0");
+  if (rank > 0 && !al16(lora_b)) return fail(FITQ_ERR_ALIGN, "qlora_fwd: lora_b must be 16-byte aligned");
   if (a.n_out % 16 != 0) return fail(FITQ_ERR_SHAPE, "qlora_fwd: N=%lld not a multiple of 16", (long long)a.n_out);
   if (!al16(x) || !al16(y) || (y_add && !al16(y_add)) || (t_out && !al16(t_out)) ||
       (bias && !al16(bias)))
@@ -307,6 +316,21 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   plan_fwd(c, m, N, K, rank, sms, &p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
+  if (p.dec) {
+    // GEMV, then T (overlapping the weight stream), then the finishing sum
+    fitq::GemvEpilogue ep{y, y_add, bias, lora_b, p.t_part, fitq::lora_t_groups(K), t_out,
+                          rank, scale, p.partial};
+    rc = fitq::launch_nf4_gemv_dec(a, x, m, ep, st, sms);
+    if (rc) return launch_status(rc, "nf4_gemv decode");
+    if (rank > 0) {
+      rc = fitq::launch_lora_t(x, m, K, lora_a, rank, p.t_part, st);
+      if (rc) return launch_status(rc, "lora T = x.A^T");
+    }
+    if (p.partial)
+      return launch_status(fitq::launch_nf4_gemv_dec_finish(m, N, p.slices, ep, st, sms),
+                           "nf4_gemv decode finish");
+    return FITQ_OK;
+  }
   if (rank > 0) {
     rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
     if (rc) return launch_status(rc, "lora_a cast");

@@ -28,6 +28,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Upper bound of any single wait inside a kernel (about 2 s).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialisation attribute may start while its predecessor finishes;
+// pdl_wait() blocks until the predecessor grid has completed and its memory is
+// visible (a no-op without such a predecessor).  Only L2 prefetches may precede
+// it.  pdl_launch_dependents() lets the next such kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

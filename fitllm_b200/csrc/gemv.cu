@@ -91,7 +91,7 @@ __device__ __forceinline__ uint32_t lut(uint32_t v, uint32_t lane4) {
 }
 
 // ---------------------------------------------------------------------------
-// Decode kernel for M <= 8 tokens (one n8 token tile).
+// Decode kernel for M <= 8 tokens (one n8 token tile), one launch per GEMV.
 //
 // A CTA owns one K slice of kw*4 blocks and a strided set of 16-row tiles;
 // warp (rg, p) = (warp / kw, warp % kw) covers blocks [4p, 4p+4) of the slice
@@ -103,9 +103,11 @@ __device__ __forceinline__ uint32_t lut(uint32_t v, uint32_t lane4) {
 // tiles (16 rows x 128 bytes) into a private 3-stage shared-memory ring with
 // 16-byte cp.async copies: two tiles in flight while the third is decoded,
 // with no cross-warp synchronisation (a warp only reads what it copied).
-// Rows sit at a 160-byte pitch so the 8-byte fragment reads are
-// conflict-free.  The absmax codes and nested scales (8 bytes per row and
-// tile) ride a small register ring two tiles ahead.
+// Within a staged row, 16-byte chunk k is stored at chunk k ^ 2*(row & 3),
+// which makes the 8-byte fragment reads conflict-free without padding.  The
+// absmax codes and nested scales (8 bytes per row and tile) ride a small
+// register ring two tiles ahead; each lane decodes the absmax of one (row,
+// block) pair of the tile and the warp shares them through shared memory.
 //
 // The code table sits on a 64 KB boundary of the CTA's shared window, so one
 // prmt of (packed byte, lane base) yields the complete shared address of a
@@ -113,15 +115,24 @@ __device__ __forceinline__ uint32_t lut(uint32_t v, uint32_t lane4) {
 // map lives in the unused upper half of each 256-byte entry (8 copies, one per
 // lane row g): an absmax costs one prmt + one ld.shared + the reference's two
 // rounded fp32 ops.  The kw partial sums of a tile are combined through shared
-// memory once per round of 3 tiles, in k order (deterministic), and written as
-// fp32 split-K partials partial[slice][m][n].
+// memory once per round of 3 tiles, in k order (deterministic).
+//
+// Epilogue: with one K slice and no LoRA the sums go straight to y (+ bias +
+// y_add, bf16) in this kernel.  Otherwise each slice writes fp32 partials
+// partial[slice][m][n] and gemv_dec_finish_kernel sums them in slice order
+// (deterministic) and adds scale * T.B^T + bias + y_add; the LoRA T kernel
+// runs between the two, on the SMs this grid leaves free, while the weights
+// stream.
+//
+// Launched with programmatic dependent launch: before griddepcontrol.wait the
+// kernel only prefetches its first weight tiles into L2 (safe even if the
+// predecessor writes them: L2 is the point of coherence), so the DRAM latency
+// of the stream's start overlaps the predecessor's tail.
 // ---------------------------------------------------------------------------
 constexpr int kDecKB = 4;                      // blocks per warp and tile
 constexpr int kDecRing = 3;                    // ring stages per warp
 constexpr int kDecDepth = kDecRing - 1;        // tiles in flight ahead of the decoded one
-constexpr int kDecPitch = 160;                 // bytes per staged row (128 used)
-constexpr int kDecStage = 16 * kDecPitch;      // one staged tile
-constexpr int kDecRingBytes = kWarps * kDecRing * kDecStage;
+constexpr int kDecStage = 16 * 128;            // one staged tile (16 rows x 128 bytes, swizzled)
 constexpr int kDecSmem = 232448;               // the whole 227 KB: table alignment slack + table + ring + reduction
 
 struct Gemv8Plan {
@@ -153,10 +164,27 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 v;
   asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
   return v;
+}
+
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void sts32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 // Shared address of byte J of v in the 64 KB-aligned table: bits 16..31 and
@@ -176,9 +204,12 @@ __device__ __forceinline__ uint32_t tbl_u32(uint32_t v, uint32_t base) {
   return r;
 }
 
-template <int J>
-__device__ __forceinline__ float tbl_f32(uint32_t v, uint32_t base) {
-  return __uint_as_float(tbl_u32<J>(v, base));
+// Same with the byte chosen at run time (sel = 0x7604 | byte << 4).
+__device__ __forceinline__ float tbl_f32_sel(uint32_t v, uint32_t base, uint32_t sel) {
+  uint32_t a, r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(v), "r"(base), "r"(sel));
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(a));
+  return __uint_as_float(r);
 }
 
 template <bool NESTED>
@@ -205,18 +236,6 @@ __device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
 
-template <int C, bool NESTED>
-__device__ __forceinline__ void block_scales(const ScaleBuf<NESTED>& b, uint32_t nq_base,
-                                             float offset, float& am_a, float& am_b) {
-  if (NESTED) {
-    am_a = __fadd_rn(__fmul_rn(tbl_f32<C>(b.ca, nq_base), b.na), offset);
-    am_b = __fadd_rn(__fmul_rn(tbl_f32<C>(b.cb, nq_base), b.nb), offset);
-  } else {
-    am_a = C == 0 ? b.fa.x : C == 1 ? b.fa.y : C == 2 ? b.fa.z : b.fa.w;
-    am_b = C == 0 ? b.fb.x : C == 1 ? b.fb.y : C == 2 ? b.fb.z : b.fb.w;
-  }
-}
-
 // One 16x64 block: 4 MMAs over the decoded A fragments, scaled per row.
 __device__ __forceinline__ void block_mma(float4& acc, uint2 wa, uint2 wb, uint4 x0, uint4 x1,
                                           uint32_t lb, float am_a, float am_b) {
@@ -236,33 +255,80 @@ __device__ __forceinline__ void block_mma(float4& acc, uint2 wa, uint2 wb, uint4
   acc.w = fmaf(t[3], am_b, acc.w);
 }
 
-template <int C, bool NESTED>
-__device__ __forceinline__ void stage_block(float4& acc, uint32_t wrow, const ScaleBuf<NESTED>& sb,
-                                            const uint4 (&xr)[kDecKB][2], uint32_t lb,
-                                            uint32_t nq_base, float offset) {
-  float am_a, am_b;
-  block_scales<C>(sb, nq_base, offset, am_a, am_b);
-  const uint2 wa = lds64(wrow + 32 * C), wb = lds64(wrow + 8 * kDecPitch + 32 * C);
-  block_mma(acc, wa, wb, xr[C][0], xr[C][1], lb, am_a, am_b);
+// frag[c]: the lane's fragment offset of block c of row g inside a stage
+// (row g + 8 is 1024 bytes further, same swizzle); am_a / am_b: the absmax of
+// blocks 0..3 of rows g and g + 8.
+template <int C>
+__device__ __forceinline__ void stage_block(float4& acc, uint32_t stage,
+                                            const uint32_t (&frag)[kDecKB], float4 am_a,
+                                            float4 am_b, const uint4 (&xr)[kDecKB][2],
+                                            uint32_t lb) {
+  const uint32_t a = stage + frag[C];
+  const uint2 wa = lds64(a), wb = lds64(a + 8 * 128);
+  const float sa = C == 0 ? am_a.x : C == 1 ? am_a.y : C == 2 ? am_a.z : am_a.w;
+  const float sb = C == 0 ? am_b.x : C == 1 ? am_b.y : C == 2 ? am_b.z : am_b.w;
+  block_mma(acc, wa, wb, xr[C][0], xr[C][1], lb, sa, sb);
 }
 
 // Partial sums of one staged tile: lane (g, q) returns rows (g, g+8) x tokens (2q, 2q+1).
-template <bool NESTED>
-__device__ __forceinline__ float4 compute_tile(uint32_t wrow, const ScaleBuf<NESTED>& sb,
-                                               const uint4 (&xr)[kDecKB][2], uint32_t lb,
-                                               uint32_t nq_base, float offset) {
+__device__ __forceinline__ float4 compute_tile(uint32_t stage, const uint32_t (&frag)[kDecKB],
+                                               float4 am_a, float4 am_b,
+                                               const uint4 (&xr)[kDecKB][2], uint32_t lb) {
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  stage_block<0>(acc, wrow, sb, xr, lb, nq_base, offset);
-  stage_block<1>(acc, wrow, sb, xr, lb, nq_base, offset);
-  stage_block<2>(acc, wrow, sb, xr, lb, nq_base, offset);
-  stage_block<3>(acc, wrow, sb, xr, lb, nq_base, offset);
+  stage_block<0>(acc, stage, frag, am_a, am_b, xr, lb);
+  stage_block<1>(acc, stage, frag, am_a, am_b, xr, lb);
+  stage_block<2>(acc, stage, frag, am_a, am_b, xr, lb);
+  stage_block<3>(acc, stage, frag, am_a, am_b, xr, lb);
   return acc;
+}
+
+// Absmax of blocks 0..3 of rows g and g + 8 of the tile.  Double-quantised:
+// lane (g, q) decodes block q of both rows and the warp exchanges them through
+// its 256-byte scale area (rows x blocks, fp32).
+template <bool NESTED>
+__device__ __forceinline__ void tile_scales(const ScaleBuf<NESTED>& b, uint32_t nq_base,
+                                            uint32_t sel_q, float offset, uint32_t sc_w,
+                                            uint32_t sc_lane, int g, float4& am_a,
+                                            float4& am_b) {
+  if (NESTED) {
+    sts32(sc_lane, __fadd_rn(__fmul_rn(tbl_f32_sel(b.ca, nq_base, sel_q), b.na), offset));
+    sts32(sc_lane + 128, __fadd_rn(__fmul_rn(tbl_f32_sel(b.cb, nq_base, sel_q), b.nb), offset));
+    __syncwarp();
+    am_a = lds128f(sc_w + 16 * g);
+    am_b = lds128f(sc_w + 128 + 16 * g);
+  } else {
+    am_a = b.fa;
+    am_b = b.fb;
+  }
+}
+
+// y[tk, n] = bf16(s + scale * T[tk].B[n] + bias[n] + y_add[tk, n]); t: T as
+// fp32 [M, rank] (bf16-rounded values), null when rank == 0.
+__device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* t, int N, int tk,
+                                          int n, float s) {
+  if (o.rank > 0) {
+    const float4* bl = reinterpret_cast<const float4*>(o.lora_b + static_cast<int64_t>(n) * o.rank);
+    const float* tl = t + tk * o.rank;
+    float l = 0.f;
+    for (int j = 0; j < o.rank; j += 4) {
+      const float4 b = __ldg(bl + j / 4);
+      l = fmaf(tl[j], b.x, l);
+      l = fmaf(tl[j + 1], b.y, l);
+      l = fmaf(tl[j + 2], b.z, l);
+      l = fmaf(tl[j + 3], b.w, l);
+    }
+    s += o.scale * l;
+  }
+  const int64_t e = static_cast<int64_t>(tk) * N + n;
+  if (o.bias) s += __bfloat162float(static_cast<const __nv_bfloat16*>(o.bias)[n]);
+  if (o.y_add) s += __bfloat162float(static_cast<const __nv_bfloat16*>(o.y_add)[e]);
+  static_cast<__nv_bfloat16*>(o.y)[e] = __float2bfloat16_rn(s);
 }
 
 template <bool NESTED>
 __global__ void __launch_bounds__(kThreads, 1)
     nf4_gemv_dec_kernel(Nf4Args w, const __nv_bfloat16* __restrict__ x, int M, Gemv8Plan pl,
-                        float* __restrict__ partial) {
+                        GemvEpilogue out) {
   constexpr int R = kDecRing, D = kDecDepth;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -270,8 +336,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nblk = K / 64, T = N / 16;
   const int qn = 1 << pl.lqn;  // token lanes q < qn hold tokens 2q, 2q+1 < 2*qn >= M
 
+  const int slice = blockIdx.x / pl.cs, j = blockIdx.x % pl.cs;
+  const int p = warp & (pl.kw - 1), rg = warp >> pl.lkw;
+  const int b0 = (slice * pl.kw + p) * kDecKB;  // first block of this warp's K range
+  // this warp's tiles: t_u = j + cs * (rg + rtg * u)
+  const int tstride = pl.cs << pl.lrtg;
+  const int t0 = j + pl.cs * rg;
+  const int n_u = t0 < T ? (T - 1 - t0) / tstride + 1 : 0;
+
+  // Before the dependency wait: L2 prefetch of this warp's first tiles only.
+  if (lane < 16 && (reinterpret_cast<uintptr_t>(w.packed) & 15) == 0) {
+    for (int u = 0; u < kDecDepth && u < n_u; ++u)
+      prefetch_l2(w.packed + (static_cast<int64_t>(16 * (t0 + u * tstride) + lane) * nblk + b0) * 32,
+                  kDecKB * 32);
+  }
+  // Wait first, then let dependents launch: a LoRA T kernel launched right
+  // behind this one reads x without waiting (see launch_lora_t).
+  pdl_wait();
+  pdl_launch_dependents();
+
   // Shared layout: [slack below the 64 KB boundary][table 64 KB][rest].  Ring
-  // stages fill the slack first, then the rest; the reduction area follows.
+  // stages fill the slack first, then the rest; the reduction area, the
+  // per-warp scale areas and the round's tile flags follow.
   const uint32_t sbase = smem_u32(g_gemv_smem);
   const uint32_t tbl = (sbase + 0xFFFFu) & ~0xFFFFu;
   const int n_slack = static_cast<int>((tbl - sbase) / kDecStage);
@@ -281,18 +367,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       after + static_cast<uint32_t>(n_ring > n_slack ? n_ring - n_slack : 0) * kDecStage;
   float4* const red = reinterpret_cast<float4*>(g_gemv_smem + (red_addr - sbase));
   const int red_warp = 8 * qn;  // float4 slots per warp and tile
+  const uint32_t sc_addr = red_addr + static_cast<uint32_t>(R * kWarps * 8 * 4 * 16);  // 256 B per warp
 
-  // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g
-  uint32_t* table = reinterpret_cast<uint32_t*>(g_gemv_smem + (tbl - sbase));
-  for (int i = threadIdx.x; i < 256 * 40; i += kThreads) {
-    const int e = i / 40, s = i % 40;
-    if (s < 32) table[e * 64 + s] = pack_bf16x2(w.quant_map[e >> 4], w.quant_map[e & 15]);
-    else if (NESTED) table[e * 64 + s] = __float_as_uint(w.nested_quant_map[e]);
+  // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g;
+  // two threads per entry, 16-byte stores
+  {
+    uint4* table = reinterpret_cast<uint4*>(g_gemv_smem + (tbl - sbase));
+    const int e = threadIdx.x >> 1, h = threadIdx.x & 1;
+    const uint32_t v = pack_bf16x2(__ldg(w.quant_map + (e >> 4)), __ldg(w.quant_map + (e & 15)));
+    const uint4 vv = make_uint4(v, v, v, v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) table[e * 16 + h * 4 + i] = vv;
+    if (NESTED) {
+      const uint32_t nv = __float_as_uint(__ldg(w.nested_quant_map + e));
+      table[e * 16 + 8 + h] = make_uint4(nv, nv, nv, nv);
+    }
   }
-
-  const int slice = blockIdx.x / pl.cs, j = blockIdx.x % pl.cs;
-  const int p = warp & (pl.kw - 1), rg = warp >> pl.lkw;
-  const int b0 = (slice * pl.kw + p) * kDecKB;  // first block of this warp's K range
 
   uint4 xr[kDecKB][2];
 #pragma unroll
@@ -317,10 +407,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                            : after + static_cast<uint32_t>(i - n_slack) * kDecStage;
   }
 
-  // this warp's tiles: t_u = j + cs * (rg + rtg * u)
-  const int tstride = pl.cs << pl.lrtg;
-  const int t0 = j + pl.cs * rg;
-  const int n_u = t0 < T ? (T - 1 - t0) / tstride + 1 : 0;
   const int n_u_max = j < T ? (T - 1 - j) / tstride + 1 : 0;  // row group 0 has the most
   const int rounds = (n_u_max + D) / R;
   const int nblk8 = 8 * nblk;
@@ -331,10 +417,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint8_t* src = w.packed + (static_cast<int64_t>(16 * t0 + (lane >> 3)) * nblk + b0) * 32 +
                        16 * (lane & 7);
   const int64_t src_step = static_cast<int64_t>(16) * tstride * row_bytes;
-  const uint32_t dst_lane = static_cast<uint32_t>((lane >> 3) * kDecPitch + 16 * (lane & 7));
-  const uint32_t rd_lane = static_cast<uint32_t>(g * kDecPitch + 8 * q);  // fragment reads
+  // staged row r (r & 3 == lane >> 3 for every copy of this lane): chunk k at k ^ 2*(r & 3)
+  const uint32_t dst_lane =
+      static_cast<uint32_t>((lane >> 3) * 128 + 16 * ((lane & 7) ^ (2 * (lane >> 3))));
+  uint32_t frag[kDecKB];  // fragment reads: row g, bytes 32c + 8q, swizzled
+#pragma unroll
+  for (int c = 0; c < kDecKB; ++c)
+    frag[c] = static_cast<uint32_t>(g * 128 + 32 * (c ^ (g & 3)) + 8 * q);
   const uint32_t lb = tbl | (static_cast<uint32_t>(lane) << 2);
   const uint32_t nq_base = tbl | (128u + (static_cast<uint32_t>(g) << 2));
+  const uint32_t sel_q = 0x7604u | (static_cast<uint32_t>(q) << 4);  // byte q of a code word
+  const uint32_t sc_w = sc_addr + static_cast<uint32_t>(warp) * 256u;
+  const uint32_t sc_lane = sc_w + static_cast<uint32_t>(g * 16 + 4 * q);
   const uint64_t pol = evict_first_policy();
   __syncthreads();  // table ready
 
@@ -344,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (d < n_u) {
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj)
-        cp_async16(stage[d] + dst_lane + jj * 4 * kDecPitch, src + jj * 4 * row_bytes, pol);
+        cp_async16(stage[d] + dst_lane + jj * 512, src + jj * 4 * row_bytes, pol);
       load_scales(sb[d], w, f_next, nblk8);
     }
     cp_async_commit();
@@ -359,8 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (u + D < n_u) {
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
-          cp_async16(stage[(r + D) % R] + dst_lane + jj * 4 * kDecPitch, src + jj * 4 * row_bytes,
-                     pol);
+          cp_async16(stage[(r + D) % R] + dst_lane + jj * 512, src + jj * 4 * row_bytes, pol);
         load_scales(sb[(r + D) % R], w, f_next, nblk8);
       }
       cp_async_commit();
@@ -369,7 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       cp_async_wait<D>();  // this lane's copies of tile u have landed
       __syncwarp();        // ... and every other lane's
       float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (u < n_u) o = compute_tile(stage[r] + rd_lane, sb[r], xr, lb, nq_base, w.offset);
+      if (u < n_u) {
+        float4 am_a, am_b;
+        tile_scales(sb[r], nq_base, sel_q, w.offset, sc_w, sc_lane, g, am_a, am_b);
+        o = compute_tile(stage[r], frag, am_a, am_b, xr, lb);
+      }
       if (q < qn) red[(r * kWarps + warp) * red_warp + (g << pl.lqn) + q] = o;
     }
     __syncthreads();
@@ -388,11 +485,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* srcf = rf + (((r * kWarps + (rgo << pl.lkw)) * red_warp) << 2) + f;
       float s = 0.f;
       for (int pp = 0; pp < pl.kw; ++pp) s += srcf[(pp * red_warp) << 2];
-      partial[(static_cast<int64_t>(slice) * M + tk) * N + t * 16 + rr] = s;
+      if (out.partial == nullptr) dec_store(out, nullptr, N, tk, t * 16 + rr, s);
+      else out.partial[(static_cast<int64_t>(slice) * M + tk) * N + t * 16 + rr] = s;
     }
     __syncthreads();  // reduction area rewritten next round
   }
   cp_async_wait<0>();
+}
+
+// Finishing pass of the decode GEMV: y = sum over slices of partial (in slice
+// order) + scale * T.B^T + bias + y_add.  With a LoRA term each CTA first sums
+// the T kernel's group partials into shared memory (all loads in flight, then
+// a fixed-order sum per (m, j)) and rounds T to bf16.  Launched with
+// programmatic dependent launch right behind the T kernel (or the GEMV), so
+// its launch overlaps their tails; pdl_wait() orders it after both.
+constexpr int kFinStage = 6144;  // floats of T partials staged per chunk
+
+__global__ void __launch_bounds__(256)
+    gemv_dec_finish_kernel(int M, int N, int slices, GemvEpilogue out) {
+  extern __shared__ float s_fin[];  // T [M * rank], then the staging chunk
+  pdl_launch_dependents();
+  pdl_wait();
+  if (out.rank > 0) {
+    const int pairs = M * out.rank, G = out.t_groups;
+    float* stg = s_fin + pairs;
+    const int np_max = kFinStage / G;  // pairs per chunk (>= 1: G <= kFinStage)
+    for (int p0 = 0; p0 < pairs; p0 += np_max) {
+      const int np = pairs - p0 < np_max ? pairs - p0 : np_max;
+      const int items = np * G;
+      for (int b = threadIdx.x; b < items; b += 8 * 256) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = b + u * 256;
+          v[u] = i < items ? __ldcg(out.t_part + static_cast<int64_t>(i / np) * pairs + p0 + i % np) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (b + u * 256 < items) stg[b + u * 256] = v[u];
+      }
+      __syncthreads();
+      for (int pl = threadIdx.x; pl < np; pl += 256) {
+        float v = 0.f;
+        for (int g = 0; g < G; ++g) v += stg[g * np + pl];
+        const __nv_bfloat16 tb = __float2bfloat16_rn(v);
+        s_fin[p0 + pl] = __bfloat162float(tb);
+        if (blockIdx.x == 0 && out.t_dense) static_cast<__nv_bfloat16*>(out.t_dense)[p0 + pl] = tb;
+      }
+      __syncthreads();
+    }
+  }
+  const int64_t total = static_cast<int64_t>(M) * N;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v = 0.f;
+    for (int sl = 0; sl < slices; ++sl) v += __ldcg(out.partial + sl * total + e);
+    dec_store(out, s_fin, N, static_cast<int>(e / N), static_cast<int>(e % N), v);
+  }
 }
 
 template <int NT8, int CH>
@@ -683,45 +832,67 @@ bool use_m8(int64_t m, int64_t N, int64_t K, int num_sms, Gemv8Plan* pl) {
   return pl->kw != 0;
 }
 
-template <bool NESTED>
-cudaError_t launch_dec(const Nf4Args& w, const __nv_bfloat16* x, int M, const Gemv8Plan& pl,
-                       float* partial, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(nf4_gemv_dec_kernel<NESTED>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  nf4_gemv_dec_kernel<NESTED><<<pl.cs * pl.slices, kThreads, kDecSmem, st>>>(w, x, M, pl, partial);
-  note_launch();
-  return cudaGetLastError();
-}
-
 }  // namespace
 
+bool gemv_dec_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slices) {
+  Gemv8Plan pl;
+  if (n_out % 16 != 0 || k_in % 256 != 0 || n_out * k_in / 2 >= (1ll << 31)) return false;
+  if (!use_m8(m, n_out, k_in, num_sms, &pl)) return false;
+  if (slices) *slices = pl.slices;
+  return true;
+}
+
+bool gemv_dec_needs_partial(int slices, int rank) { return slices > 1 || rank > 0; }
+
+int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEpilogue& out,
+                        cudaStream_t st, int num_sms) {
+  Gemv8Plan pl;
+  if (!gemv_dec_plan(m, w.n_out, w.k_in, num_sms, nullptr) || !use_m8(m, w.n_out, w.k_in, num_sms, &pl))
+    return FITQ_ERR_UNSUPPORTED;
+  auto xb = static_cast<const __nv_bfloat16*>(x);
+  const int M = static_cast<int>(m);
+  const dim3 grid(static_cast<unsigned>(pl.cs * pl.slices));
+  static bool attr[2] = {false, false};
+  const bool nested = w.absmax_f32 == nullptr;
+  if (!attr[nested]) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        nested ? nf4_gemv_dec_kernel<true> : nf4_gemv_dec_kernel<false>,
+        cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
+    if (e != cudaSuccess) return FITQ_ERR_CUDA;
+    attr[nested] = true;
+  }
+  cudaError_t e =
+      nested ? launch_pdl(nf4_gemv_dec_kernel<true>, grid, dim3(kThreads), kDecSmem, st, w, xb, M, pl, out)
+             : launch_pdl(nf4_gemv_dec_kernel<false>, grid, dim3(kThreads), kDecSmem, st, w, xb, M, pl, out);
+  note_launch();
+  return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
+                               cudaStream_t st, int num_sms) {
+  cudaError_t e;
+  {
+    const int64_t total = m * n_out;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > static_cast<int64_t>(num_sms) * 4) blocks = static_cast<int64_t>(num_sms) * 4;
+    if (out.rank > 0 && out.t_groups > kFinStage) return FITQ_ERR_UNSUPPORTED;
+    const size_t smem = out.rank > 0 ? (static_cast<size_t>(m) * out.rank + kFinStage) * sizeof(float) : 0;
+    e = launch_pdl(gemv_dec_finish_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), smem, st,
+                   static_cast<int>(m), static_cast<int>(n_out), slices, out);
+    note_launch();
+    if (e != cudaSuccess) return FITQ_ERR_CUDA;
+  }
+  return FITQ_OK;
+}
+
 size_t gemv_partial_bytes(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* splits_out) {
-  Gemv8Plan pl8;
-  int64_t slices;
-  if (use_m8(m, n_out, k_in, num_sms, &pl8)) slices = pl8.slices;
-  else slices = make_plan(m, n_out, k_in, num_sms).slices;
+  const int64_t slices = make_plan(m, n_out, k_in, num_sms).slices;
   if (splits_out) *splits_out = static_cast<int>(slices);
   return static_cast<size_t>(slices * m * n_out) * sizeof(float);
 }
 
 int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* partial,
                          cudaStream_t st, int num_sms, int* splits_out) {
-  Gemv8Plan pl;
-  if (use_m8(m, w.n_out, w.k_in, num_sms, &pl)) {
-    if (w.n_out % 16 != 0 || w.n_out * w.k_in / 2 >= (1ll << 31)) return FITQ_ERR_UNSUPPORTED;
-    auto xb = static_cast<const __nv_bfloat16*>(x);
-    const cudaError_t e = w.absmax_f32 == nullptr
-                              ? launch_dec<true>(w, xb, static_cast<int>(m), pl, partial, st)
-                              : launch_dec<false>(w, xb, static_cast<int>(m), pl, partial, st);
-    if (e != cudaSuccess) return FITQ_ERR_CUDA;
-    *splits_out = pl.slices;
-    return FITQ_OK;
-  }
   const Plan p = make_plan(m, w.n_out, w.k_in, num_sms);
   if (p.rt == 0 || p.nt8 < 1 || p.nt8 > 8) return FITQ_ERR_UNSUPPORTED;
   if ((w.k_in / 64) % 4 != 0 || w.n_out * w.k_in / 2 >= (1ll << 31)) return FITQ_ERR_UNSUPPORTED;

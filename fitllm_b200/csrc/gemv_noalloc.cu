@@ -98,12 +98,26 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
       return fail(FITQ_ERR_NO_DEVICE, "nf4_gemv_noalloc: cannot query the device");
     }
   }
-  // Scratch layout: [A as bf16 (r x K)] [T (M x 64 bf16)] [T partials] [split-K partials].
-  const size_t a_bytes = rank > 0 ? up256(static_cast<size_t>(rank) * K * 2) : 0;
-  const size_t t_bytes = rank > 0 ? up256(static_cast<size_t>(m) * 64 * 2) : 0;
-  const size_t tp_bytes = rank > 0 ? up256(fitq::lora_rowproj_small_workspace(m, K, rank)) : 0;
-  const size_t p_bytes = up256(fitq::gemv_partial_bytes(m, N, K, sms, nullptr));
-  const size_t need = a_bytes + t_bytes + tp_bytes + p_bytes;
+  if (rank > 0 && !al16(lora_b))
+    return fail(FITQ_ERR_ALIGN, "nf4_gemv_noalloc: lora_b must be 16-byte aligned");
+  // Scratch layout: for the decode kernel (M <= 8): [split-K partials]
+  // [T partials]; otherwise [A as bf16 (r x K)][T (M x 64 bf16)]
+  // [T partials][split-K partials].
+  int slices = 1;
+  const bool dec = fitq::gemv_dec_plan(m, N, K, sms, &slices);
+  size_t need = 0;
+  size_t p_bytes, tp_bytes, t_bytes = 0, a_bytes = 0;
+  if (dec) {
+    p_bytes = fitq::gemv_dec_needs_partial(slices, rank) ? up256(static_cast<size_t>(slices) * m * N * 4) : 0;
+    tp_bytes = rank > 0 ? up256(fitq::lora_t_workspace(m, K, rank)) : 0;
+    need += p_bytes + tp_bytes;
+  } else {
+    a_bytes = rank > 0 ? up256(static_cast<size_t>(rank) * K * 2) : 0;
+    t_bytes = rank > 0 ? up256(static_cast<size_t>(m) * 64 * 2) : 0;
+    tp_bytes = rank > 0 ? up256(fitq::lora_rowproj_small_workspace(m, K, rank)) : 0;
+    p_bytes = up256(fitq::gemv_partial_bytes(m, N, K, sms, nullptr));
+    need += a_bytes + t_bytes + tp_bytes + p_bytes;
+  }
   if (need > kNoAllocScratchBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),
@@ -115,10 +129,7 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
   uint8_t* base = nullptr;
   int rc = scratch_for_current_device(&base);
   if (rc) return rc;
-  void* a_bf16 = rank > 0 ? base : nullptr;
-  void* t_pad = rank > 0 ? base + a_bytes : nullptr;
-  float* t_part = rank > 0 ? reinterpret_cast<float*>(base + a_bytes + t_bytes) : nullptr;
-  float* partial = reinterpret_cast<float*>(base + a_bytes + t_bytes + tp_bytes);
+  uint8_t* rest = base;
 
   fitq::Nf4Args a;
   a.packed = w->packed;
@@ -131,6 +142,23 @@ int fitq_nf4_gemv_noalloc(const fitq_nf4_weight* w, const void* x, int64_t m,
   a.n_out = N;
   a.k_in = K;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dec) {
+    float* partial = p_bytes ? reinterpret_cast<float*>(rest) : nullptr;
+    float* t_part = rank > 0 ? reinterpret_cast<float*>(rest + p_bytes) : nullptr;
+    fitq::GemvEpilogue ep{y, y_add, bias, lora_b, t_part, fitq::lora_t_groups(K), nullptr,
+                          rank, scale, partial};
+    if ((rc = fitq::launch_nf4_gemv_dec(a, x, m, ep, st, sms)))
+      return fail(rc, "nf4_gemv_noalloc: decode launch failed");
+    if (rank > 0 && (rc = fitq::launch_lora_t(x, m, K, lora_a, rank, t_part, st)))
+      return fail(rc, "nf4_gemv_noalloc: T = x.A^T launch failed");
+    if (partial && (rc = fitq::launch_nf4_gemv_dec_finish(m, N, slices, ep, st, sms)))
+      return fail(rc, "nf4_gemv_noalloc: finishing launch failed");
+    return FITQ_OK;
+  }
+  void* a_bf16 = rank > 0 ? rest : nullptr;
+  void* t_pad = rank > 0 ? rest + a_bytes : nullptr;
+  float* t_part = rank > 0 ? reinterpret_cast<float*>(rest + a_bytes + t_bytes) : nullptr;
+  float* partial = reinterpret_cast<float*>(rest + a_bytes + t_bytes + tp_bytes);
   if (rank > 0) {
     if ((rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, a_bf16, st)))
       return fail(rc, "nf4_gemv_noalloc: lora_a cast launch failed");

@@ -1,6 +1,7 @@
 // Internal launcher declarations shared by the .cu files of libfitq.
 #pragma once
 #include <cstdint>
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -53,6 +54,39 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms);
 // out[M, r] = in[M, D] . wt[r, D]^T  (bf16 in, fp32 accumulate); written as
 // bf16 into out_pad (row pitch 64; columns r..63 are left untouched and never
 // read, since r % 16 == 0) and, when non-null, into out_dense [M, r].
+// Launch with programmatic stream serialisation (see pdl_wait in common.cuh)
+// unless FITQ_PDL=0 is set in the environment.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  static const bool off = [] {
+    const char* e = getenv("FITQ_PDL");
+    return e != nullptr && e[0] == '0';
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = off ? 0 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Partials of T = x.A^T for M <= 64 rows in one launch (lora.cu): bf16 x
+// [M, K], fp32 A [r, K] (rounded to bf16 like autocast does), fp32
+// accumulate; part_ws [K/128][M][r] fp32 (lora_t_workspace bytes), summed in
+// group order by the decode finishing kernel.  K % 128 == 0, r % 4 == 0.
+// Must be launched right behind launch_nf4_gemv_dec (it reads x without
+// waiting).
+size_t lora_t_workspace(int64_t M, int64_t K, int r);
+int lora_t_groups(int64_t K);
+int launch_lora_t(const void* x, int64_t M, int64_t K, const float* a, int r, float* part_ws,
+                  cudaStream_t st);
+
 int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, const void* wt_bf16,
                         int r, void* out_pad, void* out_dense, cudaStream_t st, int num_sms);
 // The same projection for few rows (M <= 64): D split over CTAs, fp32
@@ -77,6 +111,34 @@ int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, in
 int launch_f32_to_bf16(const float* in, int64_t n, void* out, cudaStream_t st);
 // fp32 [rows, cols] -> bf16 [cols, rows] (transposed).
 int launch_f32_to_bf16_t(const float* in, int64_t rows, int cols, void* out, cudaStream_t st);
+
+// NF4 decode GEMV for M <= 8 (gemv.cu): y = sum + scale * T.B^T + bias +
+// y_add (bf16) in the kernel when K is one slice; otherwise fp32 split-K
+// partials and a finishing launch right behind it (programmatic dependent
+// launch).
+struct GemvEpilogue {
+  void* y;               // bf16 [M, N]
+  const void* y_add;     // bf16 [M, N] or null
+  const void* bias;      // bf16 [N] or null
+  const float* lora_b;   // fp32 [N, rank] or null
+  const float* t_part;   // fp32 [t_groups, M, rank] partials of T = x.A^T, or null
+  int t_groups;
+  void* t_dense;         // bf16 [M, rank]: receives T when non-null
+  int rank;
+  float scale;
+  float* partial;        // fp32 [slices, M, N] when the finishing kernel runs
+};
+// True when the decode kernel takes (m, N, K); *slices = its K slices.
+bool gemv_dec_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slices);
+// Whether the decode GEMV writes fp32 partials (several K slices, or a LoRA
+// term: T is computed while the weights stream) and needs the finishing
+// launch; the order is launch_nf4_gemv_dec, launch_lora_t (rank > 0), then
+// launch_nf4_gemv_dec_finish.
+bool gemv_dec_needs_partial(int slices, int rank);
+int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEpilogue& out,
+                        cudaStream_t st, int num_sms);
+int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
+                               cudaStream_t st, int num_sms);
 
 // NF4 GEMV / skinny GEMM for M <= 64 (gemv.cu): split-K partial products
 // [splits, M, N] fp32, then a finishing pass adding LoRA / y_add -> bf16.

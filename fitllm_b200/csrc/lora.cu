@@ -282,6 +282,89 @@ void colproj_geometry(int64_t M, int64_t D, int num_sms, int64_t* rows_per_chunk
   *nchunks = (M + rpc - 1) / rpc;
 }
 
+// Partial T[m][j] = sum_k x[m,k] * bf16(A[j,k]) over one 128-column group per
+// CTA, for the decode / verify row counts: CTA c stages columns
+// [128c, 128c+128) of A (rounded to bf16, as the reference's bf16 lora_A
+// projection under autocast does: fitllm/qlora.py:74-83,
+// fitllm/forward.py:254-257) and of x in shared memory (row pitch 129 floats:
+// conflict-free), splits each (m, j) dot product over a group of `tp` lanes
+// closed by a fixed butterfly, and writes part[c][m][j] (fp32).  The
+// finishing kernel sums the groups in order.
+//
+// Launch order (programmatic dependent launch): the decode GEMV, then this
+// kernel, then the finishing kernel.  The GEMV waits for its own predecessor
+// before letting this kernel launch, so x is complete and this kernel reads it
+// without waiting, on the SMs the GEMV leaves free; CTA 0 waits for the GEMV
+// before exiting, so the finishing kernel's wait on this grid covers the
+// GEMV's partial sums too.
+constexpr int kTCols = 128;
+
+__global__ void __launch_bounds__(256)
+    lora_t_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, const float* __restrict__ a,
+                  int r, int tp, float* __restrict__ part) {
+  extern __shared__ float s_lt[];
+  pdl_launch_dependents();
+  constexpr int pitch = kTCols + 1;
+  const int c0 = blockIdx.x * kTCols;
+  float* as = s_lt;
+  float* xs = s_lt + r * pitch;
+  // staging: 16-byte loads, all issued before the shared-memory stores
+  {
+    constexpr int per_row4 = kTCols / 4;  // float4 per A row
+    const int na = r * per_row4;
+    for (int b = threadIdx.x; b < na; b += 4 * 256) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = b + u * 256;
+        if (i < na)
+          v[u] = __ldg(reinterpret_cast<const float4*>(a + static_cast<int64_t>(i / per_row4) * K + c0) +
+                       i % per_row4);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = b + u * 256;
+        if (i < na) {
+          float* d = as + (i / per_row4) * pitch + 4 * (i % per_row4);
+          d[0] = __bfloat162float(__float2bfloat16_rn(v[u].x));
+          d[1] = __bfloat162float(__float2bfloat16_rn(v[u].y));
+          d[2] = __bfloat162float(__float2bfloat16_rn(v[u].z));
+          d[3] = __bfloat162float(__float2bfloat16_rn(v[u].w));
+        }
+      }
+    }
+    constexpr int per_row8 = kTCols / 8;  // 8 bf16 per uint4
+    for (int i = threadIdx.x; i < M * per_row8; i += 256) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(i / per_row8) * K + c0) +
+                            i % per_row8);
+      float* d = xs + (i / per_row8) * pitch + 8 * (i % per_row8);
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        d[2 * h] = __uint_as_float(w4[h] << 16);
+        d[2 * h + 1] = __uint_as_float(w4[h] & 0xFFFF0000u);
+      }
+    }
+  }
+  __syncthreads();
+  // pair pi = (m, j) handled by lanes [sub*tp, sub*tp + tp) of a group; tp | 32
+  const int groups = blockDim.x / tp, sub = threadIdx.x % tp;
+  const int kper = kTCols / tp;
+  for (int base = 0; base < M * r; base += groups) {
+    const int pi = base + threadIdx.x / tp;
+    float s = 0.f;
+    if (pi < M * r) {
+      const int m = pi / r, j = pi % r;
+      const float* xr = xs + m * pitch + sub * kper;
+      const float* ar = as + j * pitch + sub * kper;
+      for (int k = 0; k < kper; ++k) s = fmaf(xr[k], ar[k], s);
+    }
+    for (int sh = tp / 2; sh > 0; sh >>= 1) s += __shfl_xor_sync(0xffffffffu, s, sh);
+    if (sub == 0 && pi < M * r) part[static_cast<int64_t>(blockIdx.x) * M * r + pi] = s;
+  }
+  if (blockIdx.x == 0) pdl_wait();  // this grid completes after the GEMV launched before it
+}
+
 }  // namespace
 
 int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, const void* wt_bf16,
@@ -327,6 +410,32 @@ int launch_lora_rowproj_small(const void* in, int64_t ld_in, int64_t M, int64_t 
       static_cast<__nv_bfloat16*>(out_dense));
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+size_t lora_t_workspace(int64_t M, int64_t K, int r) {
+  return static_cast<size_t>((K / kTCols) * M * r) * sizeof(float);
+}
+
+int lora_t_groups(int64_t K) { return static_cast<int>(K / kTCols); }
+
+int launch_lora_t(const void* x, int64_t M, int64_t K, const float* a, int r, float* part_ws,
+                  cudaStream_t st) {
+  if (K % kTCols != 0 || M < 1 || M > 64 || r < 1 || r > 64 || r % 4 != 0) return FITQ_ERR_UNSUPPORTED;
+  const size_t smem = static_cast<size_t>(r + M) * (kTCols + 1) * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(lora_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (64 + 64) * (kTCols + 1) * static_cast<int>(sizeof(float))) != cudaSuccess)
+      return FITQ_ERR_CUDA;
+    attr = true;
+  }
+  int tp = 32;  // lanes per (m, j) dot product: fill the 256 threads
+  while (tp > 1 && static_cast<int64_t>(256 / tp) < M * r) tp >>= 1;
+  const cudaError_t e = launch_pdl(lora_t_kernel, dim3(static_cast<unsigned>(K / kTCols)), dim3(256),
+                                   smem, st, static_cast<const __nv_bfloat16*>(x), static_cast<int>(M),
+                                   static_cast<int>(K), a, r, tp, part_ws);
+  note_launch();
+  return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 size_t lora_colproj_workspace(int64_t M, int64_t D, int r, int num_sms) {

@@ -121,8 +121,10 @@ FITQ_API int fitq_nf4_quantize(const float* w, int64_t n_out, int64_t k_in, cons
  * x bf16 row-major; lora_a fp32 [rank,K] and lora_b fp32 [N,rank] (PEFT
  * layout), both NULL (rank 0) for a bare Linear4bit; bias bf16 [N] or NULL
  * (Linear4bit's frozen bias); y_add bf16 [M,N] or NULL (fused residual).  t_out, if non-NULL,
- * receives T = x.A^T as bf16 [M,rank] for the backward.  rank in {0,16,32,48,64}.
- * M <= 64 runs the NF4 GEMV kernel, larger M the tcgen05 GEMM. */
+ * receives T = x.A^T as bf16 [M,rank] for the backward.  rank in {0,16,32,48,64};
+ * lora_b 16-byte aligned.  M <= 64 runs the NF4 GEMV kernels (M <= 8: one
+ * launch, plus a LoRA and a finishing launch that overlap it when needed),
+ * larger M the tcgen05 GEMM. */
 FITQ_API size_t fitq_qlora_fwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank);
 FITQ_API int fitq_qlora_fwd(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
                    const float* lora_b, int rank, float scale, const void* bias, void* y,

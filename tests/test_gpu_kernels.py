@@ -186,3 +186,39 @@ def test_gemv_decode_kernels(cuda_dev, monkeypatch, variant, m, n, k, r, nested)
     ref = onf4.qlora_forward(x.float().numpy(), w_deq, Anp, Bnp, s)
     assert onf4.rel_err(y.float().cpu().numpy(), ref) < REL_TOL
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k,r", [(1, 2048, 5120, 16), (4, 1024, 27648, 0), (8, 512, 1024, 32)])
+def test_gemv_decode_deterministic(cuda_dev, monkeypatch, m, n, k, r):
+    """The decode path (GEMV, LoRA T and finishing launches) gives the same
+    bits on three calls over one reused workspace, within the 1e-2 contract of
+    the oracle, and returns T when asked."""
+    monkeypatch.setenv("FITQ_GEMV_WIDE", "0")
+    from fitllm_b200 import _lib
+    L = _lib.load()
+    st, wref, w_deq, A, B, x, dy = _qlora_case(m, n, k, r, 91 + m, cuda_dev)
+    Ad = A.to(cuda_dev).contiguous() if r else None
+    Bd = B.to(cuda_dev).contiguous() if r else None
+    xd = x.to(cuda_dev)
+    nbytes = L.fitq_qlora_fwd_workspace(m, n, k, r)
+    ws = torch.full((max(nbytes, 1),), 0x5A, dtype=torch.uint8, device=cuda_dev)  # not zeroed
+    outs, ts = [], []
+    for _ in range(3):
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda_dev)
+        t = torch.empty(m, max(r, 1), dtype=torch.bfloat16, device=cuda_dev)
+        rc = L.fitq_qlora_fwd(wref.ref, xd.data_ptr(), m, _lib.ptr(Ad), _lib.ptr(Bd), r, 2.0, None,
+                              y.data_ptr(), None, t.data_ptr() if r else None, ws.data_ptr(),
+                              nbytes, torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, L.fitq_last_error()
+        torch.cuda.synchronize()
+        outs.append(y.clone())
+        ts.append(t.clone())
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    Anp = A.numpy() if r else np.zeros((0, k), np.float32)
+    Bnp = B.numpy() if r else np.zeros((n, 0), np.float32)
+    ref = onf4.qlora_forward(x.float().numpy(), w_deq, Anp, Bnp, 2.0)
+    assert onf4.rel_err(outs[0].float().cpu().numpy(), ref) < REL_TOL
+    if r:
+        assert all(torch.equal(ts[0], t) for t in ts[1:])
+        t_ref = x.float().numpy() @ A.bfloat16().float().numpy().T
+        assert onf4.rel_err(ts[0].float().cpu().numpy(), t_ref) < REL_TOL

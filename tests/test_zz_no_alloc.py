@@ -47,7 +47,7 @@ def _call_workspace(L, w, x, a, b, rank, scale, bias, y):
     p = lambda t: None if t is None else t.data_ptr()
     n, k = w.c.n_out, w.c.k_in
     nbytes = L.fitq_nf4_gemv_workspace(x.shape[0], n, k, rank)
-    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    ws = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=x.device)  # zero counter prefix
     rc = L.fitq_nf4_gemv(w.ref, x.data_ptr(), x.shape[0], p(a), p(b), rank, scale, p(bias),
                          y.data_ptr(), None, ws.data_ptr(), nbytes,
                          torch.cuda.current_stream().cuda_stream)
