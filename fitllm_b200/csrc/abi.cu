@@ -127,6 +127,7 @@ int launch_status(int rc, const char* what) {
 struct FwdPlan {
   bool gemv;       // M <= 64 skinny path
   bool dec;        // M <= 8 single-launch decode kernel
+  bool tc;         // M <= 64 tcgen05 skinny GEMM (weights decoded into TMEM)
   int slices;      // decode K slices
   void* wdeq;      // bf16 [N,K]               (GEMM path)
   void* a_bf16;    // bf16 [r,K]               (rank > 0, not decode)
@@ -140,8 +141,9 @@ size_t plan_fwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, int sms, Fw
   *p = FwdPlan{};
   p->gemv = (m <= 64) && (n % 64 == 0) && (k % 256 == 0);
   p->dec = p->gemv && fitq::gemv_dec_plan(m, n, k, sms, &p->slices);
-  if (p->dec) {
-    if (fitq::gemv_dec_needs_partial(p->slices, rank))
+  p->tc = p->gemv && !p->dec && fitq::gemv_tc_plan(m, n, k, sms, &p->slices);
+  if (p->dec || p->tc) {
+    if (p->tc || fitq::gemv_dec_needs_partial(p->slices, rank))
       p->partial = static_cast<float*>(c.take(static_cast<size_t>(p->slices * m * n) * sizeof(float)));
     if (rank > 0) p->t_part = static_cast<float*>(c.take(fitq::lora_t_workspace(m, k, rank)));
     return c.used;
@@ -316,12 +318,13 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   plan_fwd(c, m, N, K, rank, sms, &p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  if (p.dec) {
+  if (p.dec || p.tc) {
     // GEMV, then T (overlapping the weight stream), then the finishing sum
     fitq::GemvEpilogue ep{y, y_add, bias, lora_b, p.t_part, fitq::lora_t_groups(K), t_out,
                           rank, scale, p.partial};
-    rc = fitq::launch_nf4_gemv_dec(a, x, m, ep, st, sms);
-    if (rc) return launch_status(rc, "nf4_gemv decode");
+    rc = p.dec ? fitq::launch_nf4_gemv_dec(a, x, m, ep, st, sms)
+               : fitq::launch_nf4_gemv_tc(a, x, m, p.partial, status_ptr(), st, sms);
+    if (rc) return launch_status(rc, p.dec ? "nf4_gemv decode" : "nf4_gemv tcgen05");
     if (rank > 0) {
       rc = fitq::launch_lora_t(x, m, K, lora_a, rank, p.t_part, st);
       if (rc) return launch_status(rc, "lora T = x.A^T");

@@ -35,7 +35,6 @@ namespace {
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTableBytes = 256 * 256;  // entry e at e*256, lane l at +4l
-constexpr int kChunk = 4;               // blocks per double-buffer chunk
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -44,12 +43,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
@@ -69,12 +62,6 @@ __device__ __forceinline__ uint32_t lut_off(uint32_t v, uint32_t lane4) {
   constexpr uint32_t sel = 0x5500u | (static_cast<uint32_t>(J) << 4) | 4u;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(lane4), "n"(sel));
   return r;
-}
-
-__device__ __forceinline__ float block_absmax(const Nf4Args& w, int64_t blk, const float* s_nqm) {
-  if (w.absmax_f32 != nullptr) return __ldg(w.absmax_f32 + blk);
-  return __fadd_rn(__fmul_rn(s_nqm[__ldg(w.absmax_code + blk)], __ldg(w.nested_absmax + (blk >> 8))),
-                   w.offset);
 }
 
 // Work item = (K slice, group of RT row tiles); the grid is persistent (one
@@ -302,13 +289,12 @@ __device__ __forceinline__ void tile_scales(const ScaleBuf<NESTED>& b, uint32_t 
   }
 }
 
-// y[tk, n] = bf16(s + scale * T[tk].B[n] + bias[n] + y_add[tk, n]); t: T as
-// fp32 [M, rank] (bf16-rounded values), null when rank == 0.
-__device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* t, int N, int tk,
+// y[tk, n] = bf16(s + scale * T[tk].B[n] + bias[n] + y_add[tk, n]); tl: row tk of
+// T as fp32 (bf16-rounded values), null when rank == 0.
+__device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* tl, int N, int tk,
                                           int n, float s) {
   if (o.rank > 0) {
     const float4* bl = reinterpret_cast<const float4*>(o.lora_b + static_cast<int64_t>(n) * o.rank);
-    const float* tl = t + tk * o.rank;
     float l = 0.f;
     for (int j = 0; j < o.rank; j += 4) {
       const float4 b = __ldg(bl + j / 4);
@@ -493,54 +479,59 @@ __global__ void __launch_bounds__(kThreads, 1)
   cp_async_wait<0>();
 }
 
-// Finishing pass of the decode GEMV: y = sum over slices of partial (in slice
-// order) + scale * T.B^T + bias + y_add.  With a LoRA term each CTA first sums
-// the T kernel's group partials into shared memory (all loads in flight, then
-// a fixed-order sum per (m, j)) and rounds T to bf16.  Launched with
-// programmatic dependent launch right behind the T kernel (or the GEMV), so
+// Finishing pass of the split-K decode / skinny GEMMs: y[tk, :] = sum over
+// slices of partial (in slice order) + scale * T[tk].B^T + bias + y_add, one
+// grid row (blockIdx.y) per token.  With a LoRA term each CTA first sums the T
+// kernel's group partials of its token (all loads in flight, then a
+// fixed-order sum per rank) and rounds T[tk] to bf16.  Launched with
+// programmatic dependent launch right behind the T kernel (or the GEMM), so
 // its launch overlaps their tails; pdl_wait() orders it after both.
-constexpr int kFinStage = 6144;  // floats of T partials staged per chunk
+constexpr int kFinStage = 8192;  // floats of T partials staged per chunk
 
 __global__ void __launch_bounds__(256)
     gemv_dec_finish_kernel(int M, int N, int slices, GemvEpilogue out) {
-  extern __shared__ float s_fin[];  // T [M * rank], then the staging chunk
+  __shared__ float s_t[64];
+  extern __shared__ float s_stg[];  // T partials of this token, [t_groups][rank]
   pdl_launch_dependents();
   pdl_wait();
+  const int tk = blockIdx.y;
   if (out.rank > 0) {
-    const int pairs = M * out.rank, G = out.t_groups;
-    float* stg = s_fin + pairs;
-    const int np_max = kFinStage / G;  // pairs per chunk (>= 1: G <= kFinStage)
-    for (int p0 = 0; p0 < pairs; p0 += np_max) {
-      const int np = pairs - p0 < np_max ? pairs - p0 : np_max;
-      const int items = np * G;
+    const int r = out.rank, G = out.t_groups;
+    const int gc = kFinStage / r;  // groups staged per chunk
+    const float* src = out.t_part + static_cast<int64_t>(tk) * r;  // [g][M][r]
+    float acc = 0.f;                                               // thread j < r: rank j
+    for (int g0 = 0; g0 < G; g0 += gc) {
+      const int ng = G - g0 < gc ? G - g0 : gc, items = ng * r;
       for (int b = threadIdx.x; b < items; b += 8 * 256) {
         float v[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int i = b + u * 256;
-          v[u] = i < items ? __ldcg(out.t_part + static_cast<int64_t>(i / np) * pairs + p0 + i % np) : 0.f;
+          v[u] = i < items ? __ldcg(src + static_cast<int64_t>(g0 + i / r) * M * r + i % r) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-          if (b + u * 256 < items) stg[b + u * 256] = v[u];
+          if (b + u * 256 < items) s_stg[b + u * 256] = v[u];
       }
       __syncthreads();
-      for (int pl = threadIdx.x; pl < np; pl += 256) {
-        float v = 0.f;
-        for (int g = 0; g < G; ++g) v += stg[g * np + pl];
-        const __nv_bfloat16 tb = __float2bfloat16_rn(v);
-        s_fin[p0 + pl] = __bfloat162float(tb);
-        if (blockIdx.x == 0 && out.t_dense) static_cast<__nv_bfloat16*>(out.t_dense)[p0 + pl] = tb;
-      }
+      if (threadIdx.x < r)
+        for (int g = 0; g < ng; ++g) acc += s_stg[g * r + threadIdx.x];
       __syncthreads();
     }
+    if (threadIdx.x < r) {
+      const __nv_bfloat16 tb = __float2bfloat16_rn(acc);
+      s_t[threadIdx.x] = __bfloat162float(tb);
+      if (blockIdx.x == 0 && out.t_dense)
+        static_cast<__nv_bfloat16*>(out.t_dense)[static_cast<int64_t>(tk) * r + threadIdx.x] = tb;
+    }
+    __syncthreads();
   }
   const int64_t total = static_cast<int64_t>(M) * N;
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    const int64_t e = static_cast<int64_t>(tk) * N + n;
     float v = 0.f;
     for (int sl = 0; sl < slices; ++sl) v += __ldcg(out.partial + sl * total + e);
-    dec_store(out, s_fin, N, static_cast<int>(e / N), static_cast<int>(e % N), v);
+    dec_store(out, out.rank > 0 ? s_t : nullptr, N, tk, n, v);
   }
 }
 
@@ -870,19 +861,16 @@ int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEp
 
 int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
                                cudaStream_t st, int num_sms) {
-  cudaError_t e;
-  {
-    const int64_t total = m * n_out;
-    int64_t blocks = (total + 255) / 256;
-    if (blocks > static_cast<int64_t>(num_sms) * 4) blocks = static_cast<int64_t>(num_sms) * 4;
-    if (out.rank > 0 && out.t_groups > kFinStage) return FITQ_ERR_UNSUPPORTED;
-    const size_t smem = out.rank > 0 ? (static_cast<size_t>(m) * out.rank + kFinStage) * sizeof(float) : 0;
-    e = launch_pdl(gemv_dec_finish_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), smem, st,
-                   static_cast<int>(m), static_cast<int>(n_out), slices, out);
-    note_launch();
-    if (e != cudaSuccess) return FITQ_ERR_CUDA;
-  }
-  return FITQ_OK;
+  (void)num_sms;
+  if (out.rank > 64) return FITQ_ERR_UNSUPPORTED;
+  int64_t nb = (n_out + 511) / 512;
+  if (nb > 64) nb = 64;
+  const size_t smem = out.rank > 0 ? kFinStage * sizeof(float) : 0;
+  const cudaError_t e = launch_pdl(gemv_dec_finish_kernel,
+                                   dim3(static_cast<unsigned>(nb), static_cast<unsigned>(m)), dim3(256),
+                                   smem, st, static_cast<int>(m), static_cast<int>(n_out), slices, out);
+  note_launch();
+  return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 size_t gemv_partial_bytes(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* splits_out) {

@@ -78,8 +78,8 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 // Partials of T = x.A^T for M <= 64 rows in one launch (lora.cu): bf16 x
 // [M, K], fp32 A [r, K] (rounded to bf16 like autocast does), fp32
-// accumulate; part_ws [K/128][M][r] fp32 (lora_t_workspace bytes), summed in
-// group order by the decode finishing kernel.  K % 128 == 0, r % 4 == 0.
+// accumulate; part_ws [K/64][M][r] fp32 (lora_t_workspace bytes), summed in
+// group order by the decode finishing kernel.  K % 64 == 0, r % 4 == 0.
 // Must be launched right behind launch_nf4_gemv_dec (it reads x without
 // waiting).
 size_t lora_t_workspace(int64_t M, int64_t K, int r);
@@ -139,6 +139,14 @@ int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEp
                         cudaStream_t st, int num_sms);
 int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
                                cudaStream_t st, int num_sms);
+
+// NF4 skinny GEMM on tcgen05 with the decoded weights in tensor memory
+// (gemv_tc.cu), 8 < M <= 64 (FITQ_GEMV_TC=1: also M <= 8, =0: never);
+// N % 128 == 0, K % 128 == 0.  Writes fp32 split-K partials [slices, M, N]
+// for launch_nf4_gemv_dec_finish.
+bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slices);
+int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
+                       cudaStream_t st, int num_sms);
 
 // NF4 GEMV / skinny GEMM for M <= 64 (gemv.cu): split-K partial products
 // [splits, M, N] fp32, then a finishing pass adding LoRA / y_add -> bf16.

@@ -282,9 +282,9 @@ void colproj_geometry(int64_t M, int64_t D, int num_sms, int64_t* rows_per_chunk
   *nchunks = (M + rpc - 1) / rpc;
 }
 
-// Partial T[m][j] = sum_k x[m,k] * bf16(A[j,k]) over one 128-column group per
+// Partial T[m][j] = sum_k x[m,k] * bf16(A[j,k]) over one 64-column group per
 // CTA, for the decode / verify row counts: CTA c stages columns
-// [128c, 128c+128) of A (rounded to bf16, as the reference's bf16 lora_A
+// [64c, 64c+64) of A (rounded to bf16, as the reference's bf16 lora_A
 // projection under autocast does: fitllm/qlora.py:74-83,
 // fitllm/forward.py:254-257) and of x in shared memory (row pitch 129 floats:
 // conflict-free), splits each (m, j) dot product over a group of `tp` lanes
@@ -297,7 +297,7 @@ void colproj_geometry(int64_t M, int64_t D, int num_sms, int64_t* rows_per_chunk
 // without waiting, on the SMs the GEMV leaves free; CTA 0 waits for the GEMV
 // before exiting, so the finishing kernel's wait on this grid covers the
 // GEMV's partial sums too.
-constexpr int kTCols = 128;
+constexpr int kTCols = 64;
 
 __global__ void __launch_bounds__(256)
     lora_t_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, const float* __restrict__ a,

@@ -160,15 +160,19 @@ def test_gemv_paths(cuda_dev, m, n, k, r):
     assert onf4.rel_err(y2.float().cpu().numpy(), ref) < REL_TOL
 
 
-@pytest.mark.parametrize("variant", ["m8", "wide"])
+@pytest.mark.parametrize("variant", ["default", "wide", "tc"])
 @pytest.mark.parametrize("m,n,k,r,nested", [(1, 2048, 5120, 16, True), (3, 512, 27648, 0, True),
                                             (8, 3072, 1024, 16, False), (5, 1024, 5120, 0, False),
-                                            (1, 64, 256, 0, True)])
+                                            (1, 128, 256, 0, True), (16, 2048, 5120, 16, True),
+                                            (40, 1024, 5120, 16, True), (64, 512, 1024, 0, False),
+                                            (33, 384, 27648, 0, True)])
 def test_gemv_decode_kernels(cuda_dev, monkeypatch, variant, m, n, k, r, nested):
-    """The M <= 8 decode kernel (several K slices, reduction rounds and ring
-    depths across these shapes) and the general skinny kernel, on
-    double-quantised and plain fp32 absmax weights."""
-    monkeypatch.setenv("FITQ_GEMV_WIDE", "1" if variant == "wide" else "0")
+    """The M <= 8 decode kernel, the tcgen05 skinny GEMM with the decoded
+    weights in tensor memory (M <= 64; forced for M <= 8 by "tc") and the
+    general skinny kernel ("wide"), on double-quantised and plain fp32 absmax
+    weights, over several K slices, ring depths and token paddings."""
+    monkeypatch.setenv("FITQ_GEMV_WIDE", "0" if variant == "default" else "1")
+    monkeypatch.setenv("FITQ_GEMV_TC", {"default": "", "wide": "0", "tc": "1"}[variant])
     from fitllm_b200 import ops
     from fitllm_b200.nf4 import Nf4WeightCRef, QuantState
     s = 2.0
