@@ -314,7 +314,7 @@ def main():
         g_host = gout.cpu().pin_memory()
         gin_host = torch.empty_like(h_host).pin_memory()
         lora_host = torch.empty(store.per_layer, dtype=torch.float32).pin_memory()
-        shard_bytes = sched.layer_bytes(0)
+        shard_bytes = sched.upload_bytes(0)  # this rank's share when the upload is sharded
 
         def e2e_step():
             sched.invalidate()  # the layer shard is uploaded from pinned host memory every step
@@ -343,6 +343,8 @@ def main():
                "h2d_bytes_per_step": int(shard_bytes + h_host.numel() * 2 + g_host.numel() * 2),
                "d2h_bytes_per_step": int(gin_host.numel() * 2 + lora_host.numel() * 4),
                "ms_per_step": round(ms_e2e, 3),
+               "shard_upload": "sharded: 1/G of the shard per rank over PCIe + NCCL all-gather"
+                               if sched.shard_upload else "replicated",
                "note": "public API with pinned host buffers: layer shard H2D through the staging "
                        "ring, hidden states and upstream grad H2D, input grad and LoRA grads D2H"}
 

@@ -17,6 +17,12 @@ resident-pinned-weights design the reference documents for itself
   cache eviction, no synchronisation in the loop.
 
 LoRA keys found in a shard are dropped, as fitllm/forward.py:733-734 does.
+
+Data-parallel ranks (``group`` with more than one rank, NCCL): every rank
+needs the whole layer, but PCIe is per GPU while NVLink is shared by all, so
+by default each rank uploads only its 1/G byte range of the arena into its
+part of the slot and one in-place NCCL all-gather over NVLink fills in the
+rest (``shard_upload=False`` restores the replicated upload).
 """
 from __future__ import annotations
 
@@ -25,6 +31,7 @@ from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
 import torch
+import torch.distributed as dist
 
 _ALIGN = 256
 
@@ -49,6 +56,18 @@ def _layout(tensors: Dict[str, torch.Tensor]) -> Tuple[List[_Entry], int]:
     return entries, (off + _ALIGN - 1) // _ALIGN * _ALIGN
 
 
+def shard_ranges(total: int, world: int) -> Tuple[int, List[Tuple[int, int]]]:
+    """Per-rank byte ranges [start, stop) of an arena of `total` bytes split over
+    `world` ranks in equal 256-byte aligned chunks (the last ones may be short
+    or empty).  Returns (chunk, ranges); chunk * world >= total."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    chunk = -(-max(total, 1) // world)
+    chunk = (chunk + _ALIGN - 1) // _ALIGN * _ALIGN
+    ranges = [(min(i * chunk, total), min((i + 1) * chunk, total)) for i in range(world)]
+    return chunk, ranges
+
+
 def _views(buf: torch.Tensor, entries: List[_Entry]) -> Dict[str, torch.Tensor]:
     out = {}
     for e in entries:
@@ -60,9 +79,15 @@ def _views(buf: torch.Tensor, entries: List[_Entry]) -> Dict[str, torch.Tensor]:
 class ShardScheduler:
     """Pinned host store + device staging ring for layer shards."""
 
-    def __init__(self, num_layers: int, device, ring_slots: int = 2, pin_memory: bool = True):
+    def __init__(self, num_layers: int, device, ring_slots: int = 2, pin_memory: bool = True,
+                 group=None, shard_upload: bool = True):
         if ring_slots < 1:
             raise ValueError("ring_slots must be >= 1")
+        self.group = group
+        multi = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+        self.shard_upload = bool(shard_upload and multi)
+        self.rank = dist.get_rank(group) if multi else 0
+        self.world = dist.get_world_size(group) if multi else 1
         self.num_layers = num_layers
         self.device = torch.device(device)
         self.ring_slots = ring_slots
@@ -101,6 +126,15 @@ class ShardScheduler:
     def layer_bytes(self, layer_idx: int) -> int:
         return int(self._host[layer_idx].numel())
 
+    def upload_bytes(self, layer_idx: int) -> int:
+        """Bytes this rank copies host -> device for one layer."""
+        total = self.layer_bytes(layer_idx)
+        if not self.shard_upload:
+            return total
+        _, ranges = shard_ranges(total, self.world)
+        a, b = ranges[self.rank]
+        return b - a
+
     def host_tensors(self, layer_idx: int) -> Dict[str, torch.Tensor]:
         return _views(self._host[layer_idx], self._layout[layer_idx])
 
@@ -112,9 +146,13 @@ class ShardScheduler:
     def _ensure_ring(self):
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(device=self.device)
+        need = self._slot_bytes
+        if self.shard_upload:  # room for world equal chunks of the largest arena
+            chunk, _ = shard_ranges(self._slot_bytes, self.world)
+            need = chunk * self.world
         for s in range(self.ring_slots):
-            if self._slots[s] is None or self._slots[s].numel() < self._slot_bytes:
-                self._slots[s] = torch.empty(self._slot_bytes, dtype=torch.uint8, device=self.device)
+            if self._slots[s] is None or self._slots[s].numel() < need:
+                self._slots[s] = torch.empty(need, dtype=torch.uint8, device=self.device)
                 self._slot_layer[s] = -1
                 self._ready[s] = torch.cuda.Event()
                 self._free[s] = None
@@ -138,10 +176,21 @@ class ShardScheduler:
         self._free[s] = None
         src = self._host[layer_idx]
         with torch.cuda.stream(cs):
-            self._slots[s][: src.numel()].copy_(src, non_blocking=True)
+            if self.shard_upload:
+                chunk, ranges = shard_ranges(src.numel(), self.world)
+                a, b = ranges[self.rank]
+                if b > a:
+                    self._slots[s][a:b].copy_(src[a:b], non_blocking=True)
+                mine = self._slots[s][self.rank * chunk:(self.rank + 1) * chunk]
+                # in place: this rank's chunk is already in position inside the output
+                dist.all_gather_into_tensor(self._slots[s][: chunk * self.world], mine,
+                                            group=self.group)
+                self.h2d_bytes += b - a
+            else:
+                self._slots[s][: src.numel()].copy_(src, non_blocking=True)
+                self.h2d_bytes += src.numel()
             self._ready[s].record(cs)
         self._slot_layer[s] = layer_idx
-        self.h2d_bytes += src.numel()
 
     def get_layer_tensors(self, layer_idx: int, verify_checksums: bool = False) -> Dict[str, torch.Tensor]:
         """Device views of the layer's tensors; the current stream waits for the upload."""

@@ -245,3 +245,18 @@ def test_per_layer_allreduce_two_gloo_ranks():
     for _, vals, uniform in res:
         assert vals == [total * 1.0, total * 2.0, total * 3.0]
         assert uniform
+
+
+def test_shard_ranges_cover_arena():
+    """The per-rank upload ranges tile the arena exactly, in equal 256-byte
+    aligned chunks (short or empty at the end)."""
+    from fitllm_b200.scheduler import shard_ranges
+    for total in (1, 255, 256, 257, 251_531_520, 4096 * 7 + 13):
+        for world in (1, 2, 3, 4, 8):
+            chunk, ranges = shard_ranges(total, world)
+            assert chunk % 256 == 0 and chunk * world >= total
+            pos = 0
+            for i, (a, b) in enumerate(ranges):
+                assert a == min(i * chunk, total) and a == pos and a <= b <= total
+                pos = b
+            assert pos == total
