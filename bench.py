@@ -178,6 +178,91 @@ def gemv_sweep(dev, peak_gbs, reps=20):
     return out
 
 
+def qproj_linear(dev, reps=20):
+    """BASELINE config 1 on the GPU: one NF4 QLoRA q_proj (5120 -> 5120, r=16,
+    alpha 32) forward + backward (dX, dA, dB) over x [512, 5120] through the
+    module API.  FLOPs per call = M (4 N K + 6 r (N + K))."""
+    import torch
+    from fitllm_b200.qlora import Linear4bit, QLoRALinear4bit
+    m, n, k, r = 512, 5120, 5120, 16
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(n, k, generator=g, device=dev) * 0.02
+    mod = QLoRALinear4bit(Linear4bit.from_float(w, None), r=r, lora_alpha=32.0).to(dev)
+    del w
+    with torch.no_grad():
+        mod.lora_B["default"].weight.normal_(0.0, 0.01, generator=g)
+    x = torch.randn(m, k, generator=g, device=dev).bfloat16().requires_grad_(True)
+    dy = torch.randn(m, n, generator=g, device=dev).bfloat16()
+
+    def call():
+        mod.zero_grad(set_to_none=True)
+        x.grad = None
+        mod(x).backward(dy)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(reps):
+        call()
+    e_ev.record()
+    torch.cuda.synchronize()
+    ms = s_ev.elapsed_time(e_ev) / reps
+    flops = m * (4 * n * k + 6 * r * (n + k))
+    return {"metric": "NF4 QLoRA q_proj fwd+bwd (x [512, 5120], r=16)", "ms": round(ms, 4),
+            "tokens_per_s": round(m / (ms / 1000.0), 1),
+            "tflops": round(flops / (ms / 1000.0) / 1e12, 1), "flop_per_call": flops}
+
+
+def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, reps=10):
+    """one speculative-verify pass over 64 random-init NF4
+    Qwen2.5-32B-shaped layers (LoRA r=16 on q/v), batch 8 x (4 draft + 1)
+    tokens against a 4096-position KV cache -> every projection an M = 40 NF4
+    GEMM.  CUDA-graph replay; bytes = NF4 weights + KV read per pass."""
+    import torch
+    from fitllm_b200.layer import DecoderLayer, LayerConfig, add_lora_, quantize_layer_
+    from fitllm_b200.verify import KVCache, verify_pass
+    cfg = LayerConfig.qwen25_32b()
+    t = drafts + 1
+    layers = []
+    for i in range(layers_n):
+        layer = DecoderLayer(cfg, device=dev)
+        quantize_layer_(layer, seed=1000 + i)
+        add_lora_(layer, cfg.lora_rank, cfg.lora_alpha, cfg.lora_targets, seed=i, b_std=0.01)
+        layer.eval()
+        layers.append(layer)
+    cache = KVCache(layers_n, batch, cfg.kv_heads, cfg.head_dim, context + t, dev)
+    cache.fill_random_(context, seed=3)
+    g = torch.Generator(device=dev).manual_seed(4)
+    h = (torch.randn(batch, t, cfg.hidden, generator=g, device=dev) * 0.02).bfloat16()
+    verify_pass(layers, h, cache, context)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = verify_pass(layers, h, cache, context)
+    graph.replay()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(reps):
+        graph.replay()
+    e_ev.record()
+    torch.cuda.synchronize()
+    ms = s_ev.elapsed_time(e_ev) / reps
+    wbytes = layers_n * (cfg.nf4_weights_per_layer() // 2 + cfg.nf4_weights_per_layer() // 64 +
+                         4 * ((cfg.nf4_weights_per_layer() // 64 + 255) // 256))
+    kv = cache.bytes_read(context + t)
+    gbs = (wbytes + kv) / (ms / 1000.0) / 1e9
+    del graph, out, layers, cache
+    torch.cuda.empty_cache()
+    return {"metric": "speculative verify pass, 64 NF4 layers, batch 8 x 5 tokens, KV 4096",
+            "ms_per_pass": round(ms, 3), "tokens_per_s": round(batch * t / (ms / 1000.0), 1),
+            "bytes_per_pass": int(wbytes + kv), "GB/s": round(gbs, 1),
+            "frac_of_hbm": round(gbs / peak_gbs, 3), "m_per_projection": batch * t,
+            "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention torch SDPA"}
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -387,6 +472,9 @@ def main():
                                  "weights rotated over > 2x L2)", "peak_gbs": hbm,
                        "peak_source": "of measured (hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
                        "results": gemv_sweep(dev, hbm)}
+    if world == 1 and not a.no_gemv:
+        out["qproj_linear"] = qproj_linear(dev)
+        out["verify"] = verify_bench(dev, peaks.get("hbm_gbs", 6650.0))
     if world == 1 and not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(a, a.cpu_seq)
     print(json.dumps(out), flush=True)

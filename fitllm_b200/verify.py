@@ -1,0 +1,92 @@
+"""KV-cached speculative-verify forward over NF4 QLoRA layers.
+
+FitLLM verifies draft tokens by re-running the full prefix through the model
+(fitllm/inference.py:380-397, the prefill path of fitllm/forward.py:547-655).
+This module runs the same layers over a key/value cache instead: each verify
+step feeds only the draft + 1 new tokens of every sequence (batch B, T tokens
+each), so every projection is a skinny NF4 GEMM with M = B * T rows (the
+decode kernels of this library), attention reads the cached prefix, and the
+new keys/values are written into the cache at positions [P, P + T).
+
+The layer arithmetic is DecoderLayer's (fitllm_b200/layer.py): RMSNorm, q/k/v
+with bias, rotary embedding at the tokens' absolute positions, grouped-query
+attention (causal within the new tokens, full over the prefix), o_proj with
+the residual fused, RMSNorm, SwiGLU MLP with the residual fused.
+"""
+from __future__ import annotations
+
+from typing import List, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from .layer import DecoderLayer, rotary_tables
+from .layer_ops import rope, swiglu
+
+
+class KVCache:
+    """Per-layer key/value cache [B, kv_heads, capacity, head_dim] (bf16)."""
+
+    def __init__(self, num_layers: int, batch: int, kv_heads: int, head_dim: int, capacity: int,
+                 device, dtype=torch.bfloat16):
+        shape = (batch, kv_heads, capacity, head_dim)
+        self.k = [torch.zeros(shape, device=device, dtype=dtype) for _ in range(num_layers)]
+        self.v = [torch.zeros(shape, device=device, dtype=dtype) for _ in range(num_layers)]
+        self.capacity = capacity
+
+    def fill_random_(self, length: int, seed: int = 0) -> None:
+        """Seeded N(0, 1) prefix of `length` positions (a synthetic context)."""
+        g = torch.Generator(device=self.k[0].device).manual_seed(seed)
+        for k, v in zip(self.k, self.v):
+            k[:, :, :length].normal_(generator=g)
+            v[:, :, :length].normal_(generator=g)
+
+    def bytes_read(self, length: int) -> int:
+        """K and V bytes one verify pass reads over `length` cached positions."""
+        b, h, _, d = self.k[0].shape
+        return 2 * len(self.k) * b * h * length * d * self.k[0].element_size()
+
+
+def verify_mask(prefix: int, t: int, device) -> torch.Tensor:
+    """[t, prefix + t] boolean: new token i sees the prefix and new tokens <= i."""
+    cols = torch.arange(prefix + t, device=device)
+    rows = torch.arange(t, device=device)
+    return cols[None, :] <= (prefix + rows)[:, None]
+
+
+def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Tensor,
+                         v_cache: torch.Tensor, prefix: int, tables: Tuple[torch.Tensor, torch.Tensor],
+                         mask: torch.Tensor) -> torch.Tensor:
+    """One layer over the T new tokens of each sequence.  h: [B, T, hidden]
+    bf16; tables: fp32 rotary (cos, sin) half tables of positions
+    [prefix, prefix + T); writes K/V of the new tokens into the caches."""
+    cfg = layer.cfg
+    b, t, _ = h.shape
+    attn = layer.self_attn
+    cos, sin = tables
+    x = layer.input_layernorm(h)
+    q = rope(attn.q_proj(x), cos, sin, cfg.heads).view(b, t, cfg.heads, cfg.head_dim).transpose(1, 2)
+    k = rope(attn.k_proj(x), cos, sin, cfg.kv_heads).view(b, t, cfg.kv_heads, cfg.head_dim)
+    v = attn.v_proj(x).view(b, t, cfg.kv_heads, cfg.head_dim)
+    k_cache[:, :, prefix:prefix + t].copy_(k.transpose(1, 2))
+    v_cache[:, :, prefix:prefix + t].copy_(v.transpose(1, 2))
+    o = F.scaled_dot_product_attention(q, k_cache[:, :, :prefix + t], v_cache[:, :, :prefix + t],
+                                       attn_mask=mask, enable_gqa=True)
+    o = o.transpose(1, 2).reshape(b, t, cfg.heads * cfg.head_dim)
+    h1 = attn.o_proj(o, residual=h)
+    mlp = layer.mlp
+    x2 = layer.post_attention_layernorm(h1)
+    return mlp.down_proj(swiglu(mlp.gate_proj(x2), mlp.up_proj(x2)), residual=h1)
+
+
+@torch.no_grad()
+def verify_pass(layers: List[DecoderLayer], h: torch.Tensor, cache: KVCache, prefix: int) -> torch.Tensor:
+    """All layers over the new tokens; returns the final hidden states."""
+    cfg = layers[0].cfg
+    t = h.shape[1]
+    pos = torch.arange(prefix, prefix + t, device=h.device)
+    tables = rotary_tables(t, cfg.head_dim, cfg.rope_theta, h.device, position_ids=pos)
+    mask = verify_mask(prefix, t, h.device)
+    for i, layer in enumerate(layers):
+        h = verify_layer_forward(layer, h, cache.k[i], cache.v[i], prefix, tables, mask)
+    return h

@@ -288,3 +288,32 @@ def test_fused_layer_kernels_vs_torch(cuda_dev):
     assert onf4.rel_err(a.detach().float().cpu().numpy(), ar.detach().cpu().numpy()) < REL
     assert onf4.rel_err(gate.grad.float().cpu().numpy(), gr.grad.cpu().numpy()) < REL
     assert onf4.rel_err(up.grad.float().cpu().numpy(), ur.grad.cpu().numpy()) < REL
+
+
+def test_verify_pass_matches_full_forward(cuda_dev):
+    """KV-cached verify (fitllm_b200/verify.py): filling the cache with the
+    prefix, then running only the T new tokens of each sequence, gives the
+    same last-T hidden states as the full causal forward over prefix + new
+    tokens (the reference's re-prefill), within 1e-2."""
+    from fitllm_b200.layer import DecoderLayer, LayerConfig, add_lora_, quantize_layer_
+    from fitllm_b200.verify import KVCache, verify_pass
+    cfg = LayerConfig(hidden=256, heads=4, kv_heads=2, head_dim=64, intermediate=512)
+    layers = []
+    for i in range(2):
+        layer = DecoderLayer(cfg, device=cuda_dev)
+        quantize_layer_(layer, seed=40 + i)
+        add_lora_(layer, 16, 32.0, ("q_proj", "v_proj"), seed=i, b_std=0.01)
+        layer.eval()
+        layers.append(layer)
+    b, p, t = 2, 16, 5
+    g = torch.Generator(device=cuda_dev).manual_seed(9)
+    h = torch.randn(b, p + t, cfg.hidden, generator=g, device=cuda_dev).bfloat16()
+    with torch.no_grad():
+        ref = h
+        for layer in layers:
+            ref = layer(ref)
+        cache = KVCache(2, b, cfg.kv_heads, cfg.head_dim, p + t, cuda_dev)
+        verify_pass(layers, h[:, :p].contiguous(), cache, prefix=0)
+        out = verify_pass(layers, h[:, p:].contiguous(), cache, prefix=p)
+    err = (out.float() - ref[:, p:].float()).norm() / ref[:, p:].float().norm()
+    assert float(err) < 1e-2, float(err)
