@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--cpu-seq", type=int, default=2048)
+    ap.add_argument("--full-step", choices=["auto", "on", "off"], default="auto",
+                    help="also time a full 64-layer step with shards streamed from pinned host "
+                         "memory (auto: on one GPU only; every rank builds the 64-layer host store)")
     return ap.parse_args()
 
 
@@ -263,6 +266,58 @@ def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, re
             "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention torch SDPA"}
 
 
+def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, steps=2):
+    """One full synthetic training step over 64 random-init
+    NF4 Qwen2.5-32B-shaped layers whose shards live in pinned host memory and
+    stream through the device ring (sharded upload + NCCL all-gather when
+    world > 1), 16 micro-batches of 1024 tokens split over the ranks, the
+    per-layer LoRA-gradient all-reduce, then clip + AdamW on the q/v adapters.
+    Device time per step (CUDA events, max over ranks)."""
+    import torch
+    from fitllm_b200.distributed import LoRAGradComm, barrier, max_over_ranks, microbatch_range
+    from fitllm_b200.engine import ShardStationaryEngine, build_synthetic_model
+    from fitllm_b200.layer import LayerConfig
+    from fitllm_b200.optimizer import ShardOptimizer
+    cfg = LayerConfig.qwen25_32b()
+    sched, store = build_synthetic_model(cfg, layers_n, dev, seed=7)
+    comm = LoRAGradComm(store)
+    eng = ShardStationaryEngine(cfg, sched, store, dev, comm=comm)
+    opt = ShardOptimizer(store)
+    mb0, mb1 = microbatch_range(microbatches, rank, world)
+    g = torch.Generator(device=dev).manual_seed(8)
+    h0 = (torch.randn(mb1 - mb0, seq, cfg.hidden, generator=g, device=dev) * 0.02).bfloat16()
+    gout = torch.randn(mb1 - mb0, seq, cfg.hidden, generator=g, device=dev).bfloat16()
+
+    def step():
+        store.zero_grad()
+        eng.step(h0, gout)
+        opt.step()
+
+    step()
+    barrier()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(steps):
+        step()
+    e_ev.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(s_ev.elapsed_time(e_ev) / steps, dev)
+    h2d = sum(sched.upload_bytes(l) for l in range(layers_n))
+    out = {"metric": "full 64-layer QLoRA training step tokens/s (16 x 1024 tokens, shards from host)",
+           "value": round(microbatches * seq / (ms / 1000.0), 1), "unit": "tokens/s",
+           "ms_per_step": round(ms, 1), "layers": layers_n,
+           "model_tflops": round(microbatches * seq * layers_n * flops_per_token(seq) / (ms / 1000.0) / 1e12, 1),
+           "layers_kept_without_recompute": eng.last_kept,
+           "h2d_shard_bytes_per_layer_pass_per_rank": int(h2d // layers_n),
+           "note": "each layer's shard is uploaded in the forward and again in the backward "
+                   "(two-slot ring)"}
+    del eng, sched, store, opt, h0, gout
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -433,6 +488,15 @@ def main():
                "note": "public API with pinned host buffers: layer shard H2D through the staging "
                        "ring, hidden states and upstream grad H2D, input grad and LoRA grads D2H"}
 
+    # every rank takes part in the full-step measurement (it has collectives)
+    full_step = None
+    if a.full_step == "on" or (a.full_step == "auto" and world == 1):
+        del eng, sched, store, opt, h0, gout
+        if e2e is not None:
+            del h_host, g_host, gin_host, lora_host
+        torch.cuda.empty_cache()
+        full_step = full_step_bench(dev, rank, world)
+
     if rank != 0:
         return
     peaks = {}
@@ -472,6 +536,8 @@ def main():
                                  "weights rotated over > 2x L2)", "peak_gbs": hbm,
                        "peak_source": "of measured (hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
                        "results": gemv_sweep(dev, hbm)}
+    if full_step is not None:
+        out["full_step"] = full_step
     if world == 1 and not a.no_gemv:
         out["qproj_linear"] = qproj_linear(dev)
         out["verify"] = verify_bench(dev, peaks.get("hbm_gbs", 6650.0))

@@ -133,7 +133,10 @@ class ShardStationaryEngine:
     def _layers_to_keep(self, tokens: int) -> int:
         k = self.keep_activations
         if k == "auto":
+            # free HBM plus what the caching allocator holds but does not use
+            # (the previous step's kept activations come back to it)
             free, _ = torch.cuda.mem_get_info(self.device)
+            free += torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
             budget = self.keep_budget_fraction * free
             per = tokens * self.saved_bytes_per_token()
             k = int(budget // max(per, 1))
