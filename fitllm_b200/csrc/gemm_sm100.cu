@@ -284,6 +284,20 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
 
 }  // namespace
 
+bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   CUtensorMap ta, tb, tpa, tpb;
   if (!make_tmap(&ta, g.a, g.m, g.k, g.lda, BM)) return FITQ_ERR_CUDA;

@@ -12,70 +12,62 @@
 // 64-column block by its absmax (bf16x2 multiply) and writes the bf16 pairs
 // into TMEM with tcgen05.st -- exactly A's TMEM layout (row = lane, two
 // consecutive K elements per 32-bit column).  The tokens (x, padded to NTOK =
-// 16/32/64 rows with zeros) are the B operand, staged in shared memory in the
-// 128-byte-swizzled K-major layout.  The tensor core then does all the
+// 16/32/48/64 rows with zeros) are the B operand, staged in shared memory in
+// the 128-byte-swizzled K-major layout.  The tensor core then does all the
 // multiply-adds for every token at once, so the decode cost per weight does
 // not grow with M.
 //
-// One CTA per SM, one pipeline (10 warps):
-//   warp 0      producer: per stage (two 64-column blocks of one 128-row tile)
-//               16-byte cp.async copies of the packed bytes (rows at an 80-byte
-//               pitch: conflict-free 16-byte reads; small bulk copies would be
-//               issued one request at a time) and of the x tile (zero fill for
-//               pad tokens) into an NST-stage ring;
-//   warp 1      allocates TMEM (512 columns: four A buffers of 64 columns and
-//               the fp32 accumulator) and issues the MMAs from one lane;
-//   warps 2-9   decoders: warp w decodes block (w - 2) / 4 of each stage for
+// A stage is four 64-column blocks (256 K values) of one 128-row tile: its
+// packed bytes (16 KB) and the four matching x tiles.  One CTA per SM, 19 warps:
+//   warp 0      producer: per stage one TMA load of the packed bytes (128 rows
+//               x 128 B, 128-byte swizzle: conflict-free 16-byte reads by row)
+//               and four of the x tiles (tokens >= M read as zeros), issued
+//               together on one barrier.  Loads leave the TMA unit in order,
+//               so x issued later than its weights would wait behind every
+//               weight load queued in between;
+//   warps 1, 2  MMA issuers: one lane each issues the MMAs of blocks 0-1
+//               (warp 1) or 2-3 (warp 2) of every stage into its own fp32
+//               accumulator.  One thread waits about 50 cycles on each
+//               M=128, K=16 MMA whatever N <= 64 is; two issuing threads keep
+//               the tensor core about twice as busy.  Warp 1 also allocates
+//               TMEM (three 128-column A buffers + two accumulators);
+//   warps 3-18  decoders: warp w decodes block (w - 3) / 4 of every stage for
 //               the 32 rows of TMEM sub-partition w % 4; at the end of an item
-//               they drain their half of the accumulator columns and write the
-//               fp32 partials.
+//               each drains NTOK / 4 columns of both accumulators and writes
+//               their sum as the fp32 partials.
 // Work items are (128-row tile, K slice) pairs, walked by the CTAs with a grid
-// stride.  Every mbarrier wait is bounded (common.cuh); no TMA or multicast.
+// stride.  Every mbarrier wait is bounded (common.cuh); no multicast.
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace fitq {
 namespace {
 
-constexpr int kTcWarps = 10;
+constexpr int kTcWarps = 19;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr int kTcRows = 128;          // weight rows per tile (UMMA M)
-constexpr int kTcWPitch = 80;         // staged bytes per row (64 used)
-constexpr int kTcWBytes = kTcRows * kTcWPitch;
+constexpr int kTcDecWarp0 = 3;          // first decoder warp
+constexpr int kTcRows = 128;            // weight rows per tile (UMMA M)
+constexpr int kTcWStage = kTcRows * 128;  // packed bytes of one stage (four blocks per row)
 constexpr int kTcTbl = 256 * 256;       // code-pair table, 64 KB aligned
 constexpr int kTcMaxSt = 8;
 constexpr int kTcSmem = 232448 - 2048;  // dynamic shared memory (static part holds barriers)
 constexpr int kTcTmemCols = 512;
-constexpr int kTcABufs = 4;             // A buffers (64 columns each), then the accumulator
-constexpr int kTcAcc = kTcABufs * 64;
+constexpr int kTcABufs = 3;             // A buffers (128 columns each), then the accumulators
+constexpr int kTcAcc = kTcABufs * 128;  // accumulator of issuer i at kTcAcc + 64 i
 
 struct TcParams {
   Nf4Args w;
-  const __nv_bfloat16* x;
   int M;
   int tiles;        // N / 128
   int slices, bps;  // K slices, 64-column blocks per slice (multiple of 4)
   int items;        // tiles * slices
   int nst;          // ring stages
-  int stage_bytes;  // x part (2 * NTOK * 128) + W part, multiple of 1024
+  int xbytes;       // x bytes of one stage (4 * NTOK * 128)
   float* partial;   // [slices, M, N]
   int* status;
 };
 
 extern __shared__ __align__(1024) uint8_t g_tc_smem[];
-
-// 16-byte async copy; src_bytes = 0 fills the destination with zeros.
-__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-
-// Arrive on bar once all of this thread's earlier cp.async copies have landed
-// (the barrier's expected count includes this arrival).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
 
 __device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
                                              uint32_t idesc, uint32_t accumulate) {
@@ -103,28 +95,11 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-template <int N>
-__device__ __forceinline__ void tmem_ld_32x32b(uint32_t taddr, uint32_t (&r)[N]);
-template <>
-__device__ __forceinline__ void tmem_ld_32x32b<8>(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                 "=r"(r[6]), "=r"(r[7])
+// 32 lanes x 4 consecutive 32-bit columns: thread i reads lane (base + i).
+__device__ __forceinline__ void tmem_ld_32x32b_x4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(taddr));
-}
-template <>
-__device__ __forceinline__ void tmem_ld_32x32b<16>(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-template <>
-__device__ __forceinline__ void tmem_ld_32x32b<32>(uint32_t taddr, uint32_t (&r)[32]) {
-  tmem_ld_32x32b_x32(taddr, r);
 }
 
 // bf16 code pair of byte J of v from the 64 KB-aligned table (see gemv.cu).
@@ -160,54 +135,62 @@ __device__ __forceinline__ uint4 lds128u(uint32_t addr) {
 }
 
 template <int NTOK, bool NESTED>
-__global__ void __launch_bounds__(kTcThreads, 1) nf4_gemv_tc_kernel(const TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1)
+    nf4_gemv_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_x, const TcParams p) {
   __shared__ uint64_t bars[3 * kTcMaxSt + 2 * kTcABufs + 3];
+  __shared__ uint32_t slot_s[2 * kTcMaxSt];  // W slot of stage s at [s], x slot at [kTcMaxSt + s]
   __shared__ uint32_t tmem_slot;
-  __shared__ int abort_s, never_s;
-  uint64_t* full = bars;                 // producer -> decoders + MMA (32 cp.async arrivals)
-  uint64_t* wfree = bars + kTcMaxSt;     // decoders done with the stage's W (count 8)
-  uint64_t* xfree = bars + 2 * kTcMaxSt; // MMAs done with the stage's x (commit)
-  uint64_t* afull = bars + 3 * kTcMaxSt; // [kTcABufs] decoders wrote A buffer (count 8)
-  uint64_t* aempty = afull + kTcABufs;   // [kTcABufs] MMAs done with A buffer (commit)
-  uint64_t* accfull = aempty + kTcABufs; // item's MMAs done (commit)
-  uint64_t* accempty = accfull + 1;      // accumulator drained (count 8)
-  uint64_t* done = accfull + 2;          // every issued MMA retired (commit)
+  __shared__ int abort_s, never_s, layout_ok_s;
+  uint64_t* full = bars;                  // producer -> decoders + MMA (TMA bytes, W and x)
+  uint64_t* wfree = full + kTcMaxSt;      // decoders read the W slot (count 16)
+  uint64_t* xfree = wfree + kTcMaxSt;     // MMAs done with the x slot (2 commits)
+  uint64_t* afull = xfree + kTcMaxSt;     // [kTcABufs] decoders wrote A buffer (count 16)
+  uint64_t* aempty = afull + kTcABufs;    // [kTcABufs] MMAs done with A buffer (2 commits)
+  uint64_t* accfull = aempty + kTcABufs;  // item's MMAs done (2 commits)
+  uint64_t* accempty = accfull + 1;       // accumulators drained (count 16)
+  uint64_t* done = accfull + 2;           // every issued MMA retired (2 commits)
   volatile int* abort_flag = &abort_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = static_cast<int>(p.w.k_in), N = static_cast<int>(p.w.n_out);
   const int nblk = K / 64;
-  const int nst = p.nst, kst = p.bps / 2;
+  const int nst = p.nst, kst = p.bps / 4;
 
-  // Shared layout: stages in [align1024(base), table) then after the table.
+  // Shared layout: the 64 KB-aligned table, ring slots first-fit before and after it.
   const uint32_t sbase = smem_u32(g_tc_smem);
   const uint32_t tbl = (sbase + 0xFFFFu) & ~0xFFFFu;
-  const uint32_t a0 = (sbase + 1023u) & ~1023u;
-  const int n_slack = tbl > a0 ? static_cast<int>((tbl - a0) / p.stage_bytes) : 0;
-  const uint32_t after = tbl + kTcTbl;
-  auto stage_addr = [&](int s) -> uint32_t {
-    return s < n_slack ? a0 + static_cast<uint32_t>(s * p.stage_bytes)
-                       : after + static_cast<uint32_t>((s - n_slack) * p.stage_bytes);
-  };
-  constexpr int kXBytes = 2 * NTOK * 128;  // two 64-column x tiles, 128-byte swizzled
-
   if (threadIdx.x == 0) {
-    for (int s = 0; s < nst; ++s) {
-      mbar_init(&full[s], 32);
-      mbar_init(&wfree[s], 8);
-      mbar_init(&xfree[s], 1);
+    uint32_t cur_a = (sbase + 1023u) & ~1023u, cur_b = tbl + kTcTbl;
+    const uint32_t end = sbase + kTcSmem;
+    bool ok = nst <= kTcMaxSt;
+    auto place = [&](int i, uint32_t bytes) {
+      if (cur_a + bytes <= tbl) { slot_s[i] = cur_a; cur_a += bytes; }
+      else { slot_s[i] = cur_b; cur_b += bytes; }
+    };
+    for (int i = 0; ok && i < nst; ++i) place(kTcMaxSt + i, static_cast<uint32_t>(p.xbytes));
+    for (int i = 0; ok && i < nst; ++i) place(i, kTcWStage);
+    if (cur_b > end) ok = false;
+    layout_ok_s = ok ? 1 : 0;
+    if (!ok) report_device_error(p.status, FITQ_ERR_UNSUPPORTED);
+    for (int s = 0; s < kTcMaxSt; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&wfree[s], 16);
+      mbar_init(&xfree[s], 2);
     }
     for (int a = 0; a < kTcABufs; ++a) {
-      mbar_init(&afull[a], 8);
-      mbar_init(&aempty[a], 1);
+      mbar_init(&afull[a], 16);
+      mbar_init(&aempty[a], 2);
     }
-    mbar_init(accfull, 1);
-    mbar_init(accempty, 8);
-    mbar_init(done, 1);
+    mbar_init(accfull, 2);
+    mbar_init(accempty, 16);
+    mbar_init(done, 2);
     abort_s = 0;
     never_s = 0;
     fence_mbar_init();
   }
+  __syncthreads();
+  if (!layout_ok_s) return;
   if (warp == 1) {
     tmem_alloc(&tmem_slot, kTcTmemCols);
     tmem_relinquish();
@@ -215,10 +198,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) nf4_gemv_tc_kernel(const TcPara
   // Everything below reads data written by the predecessor kernel.
   pdl_wait();
   pdl_launch_dependents();
-  if (warp >= 2) {
+  if (warp >= kTcDecWarp0) {
     // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g
     uint4* table = reinterpret_cast<uint4*>(g_tc_smem + (tbl - sbase));
-    for (int i = threadIdx.x - 64; i < 512; i += kTcThreads - 64) {
+    constexpr int kFill = kTcThreads - 32 * kTcDecWarp0;
+    for (int i = threadIdx.x - 32 * kTcDecWarp0; i < 512; i += kFill) {
       const int e = i >> 1, h = i & 1;
       const uint32_t v = pack_bf16x2(__ldg(p.w.quant_map + (e >> 4)), __ldg(p.w.quant_map + (e & 15)));
       const uint4 vv = make_uint4(v, v, v, v);
@@ -235,74 +219,76 @@ __global__ void __launch_bounds__(kTcThreads, 1) nf4_gemv_tc_kernel(const TcPara
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
   const uint32_t idesc = umma_idesc_bf16_f32(kTcRows, NTOK);
+  constexpr int kXTile = NTOK * 128;  // one 64-column x tile, 128-byte swizzled
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    int st = 0;
-    uint32_t ph = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
-      const int t = it / p.slices, sl = it % p.slices;
-      const int kb0 = sl * p.bps;
-      for (int ks = 0; ks < kst; ++ks) {
-        if (!mbar_wait(&wfree[st], ph ^ 1, abort_flag, p.status) ||
-            !mbar_wait(&xfree[st], ph ^ 1, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
-        const uint32_t sa = stage_addr(st);
-        const int kb = kb0 + 2 * ks;
-        // W: 128 rows x 4 chunks of 16 B; chunk c -> row c >> 2, piece c & 3
-#pragma unroll 4
-        for (int c = lane; c < kTcRows * 4; c += 32) {
-          const int r = c >> 2, q = c & 3;
-          cp_async16_zfill(sa + kXBytes + r * kTcWPitch + q * 16,
-                           p.w.packed + (static_cast<int64_t>(t * kTcRows + r) * nblk + kb) * 32 + q * 16,
-                           16u);
-        }
-        // x tile of each block: NTOK rows x 128 B, chunk q of row tk at q ^ (tk & 7)
-        for (int c = lane; c < NTOK * 16; c += 32) {
-          const int tk = c >> 4, d = (c >> 3) & 1, q = c & 7;
-          const int tks = tk < p.M ? tk : 0;
-          const __nv_bfloat16* src = p.x + static_cast<int64_t>(tks) * K + (kb + d) * 64 + q * 8;
-          cp_async16_zfill(sa + d * (NTOK * 128) + tk * 128 + ((q ^ (tk & 7)) << 4), src,
-                           tk < p.M ? 16u : 0u);
-        }
-        cp_async_arrive_noinc(&full[st]);
-        if (++st == nst) { st = 0; ph ^= 1; }
-      }
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA
     if (lane == 0) {
-      int st = 0, a = 0;
-      uint32_t ph = 0, aph = 0, accph = 0;
+      tma_prefetch_desc(&tm_w);
+      tma_prefetch_desc(&tm_x);
+      int st = 0;
+      uint32_t ph = 0;
+      uint32_t armed = 0, armed_parity = 0;  // per-stage bit: armed / parity of the last arm
       bool ok = true;
-      const uint32_t acc = tmem_base + kTcAcc;
+      for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
+        const int t = it / p.slices, sl = it % p.slices;
+        const int kb0 = sl * p.bps;
+        for (int ks = 0; ks < kst; ++ks) {
+          if (!mbar_wait(&wfree[st], ph ^ 1, abort_flag, p.status) ||
+              !mbar_wait(&xfree[st], ph ^ 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], kTcWStage + p.xbytes);
+          armed |= 1u << st;
+          armed_parity = (armed_parity & ~(1u << st)) | (ph << st);
+          const int kb = kb0 + 4 * ks;
+          // packed bytes: x = byte column kb * 32 (a multiple of 128), y = first row of the tile
+          tma_load_2d(g_tc_smem + (slot_s[st] - sbase), &tm_w, &full[st], kb * 32, t * kTcRows);
+          uint8_t* xd = g_tc_smem + (slot_s[kTcMaxSt + st] - sbase);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) tma_load_2d(xd + b * kXTile, &tm_x, &full[st], (kb + b) * 64, 0);
+          if (++st == nst) { st = 0; ph ^= 1; }
+        }
+      }
+      // Never leave a bulk copy in flight: wait for the last arm of each stage.
+      for (int s = 0; s < nst; ++s)
+        if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never_s, p.status);
+    }
+    __syncwarp();
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
+    if (lane == 0) {
+      const int half = warp - 1;  // blocks 2 half and 2 half + 1 of every stage
+      int xs = 0, a = 0;
+      uint32_t xph = 0, aph = 0, accph = 0;  // x slot = ring stage
+      bool ok = true;
+      const uint32_t acc = tmem_base + kTcAcc + 64 * half;
       for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
         if (!mbar_wait(accempty, accph ^ 1, abort_flag, p.status)) break;
         tc_fence_after();
         for (int ks = 0; ks < kst; ++ks) {
-          if (!mbar_wait(&full[st], ph, abort_flag, p.status) ||
+          if (!mbar_wait(&full[xs], xph, abort_flag, p.status) ||
               !mbar_wait(&afull[a], aph, abort_flag, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = stage_addr(st);
+          // Keep the per-MMA work to two adds: both offsets stay inside the
+          // 14-bit start-address field (shared addresses < 256 KB).
+          const uint64_t xd = umma_smem_desc_sw128(slot_s[kTcMaxSt + xs] + 2 * half * kXTile);
+          const uint32_t ad = tmem_base + a * 128 + 64 * half;
+          umma_bf16_ts(acc, ad, xd, idesc, ks > 0 ? 1u : 0u);
 #pragma unroll
-          for (int d = 0; d < 2; ++d)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_ts(acc, tmem_base + a * 64 + d * 32 + kk * 8,
-                           umma_smem_desc_sw128(sa + d * (NTOK * 128) + kk * 32), idesc,
-                           (ks > 0 || d > 0 || kk > 0) ? 1u : 0u);
+          for (int i = 1; i < 8; ++i) {
+            const int b = i >> 2, kk = i & 3;
+            umma_bf16_ts(acc, ad + b * 32 + kk * 8, xd + static_cast<uint64_t>((b * kXTile + kk * 32) >> 4),
+                         idesc, 1u);
+          }
           umma_commit(&aempty[a]);
-          umma_commit(&xfree[st]);
+          umma_commit(&xfree[xs]);
           if (++a == kTcABufs) { a = 0; aph ^= 1; }
-          if (++st == nst) { st = 0; ph ^= 1; }
+          if (++xs == nst) { xs = 0; xph ^= 1; }
         }
         if (!ok) break;
         umma_commit(accfull);
@@ -315,63 +301,61 @@ __global__ void __launch_bounds__(kTcThreads, 1) nf4_gemv_tc_kernel(const TcPara
     __syncwarp();
   } else {
     // ------------------------------------------------------------ decoders
-    const int d = (warp - 2) >> 2;         // block of the stage this warp decodes
-    const int sub = warp & 3;              // TMEM sub-partition (lanes 32 sub .. + 31)
-    const int r = sub * 32 + lane;         // row within the tile
+    const int d = (warp - kTcDecWarp0) >> 2;  // block of the stage this warp decodes
+    const int sub = warp & 3;                 // TMEM sub-partition (lanes 32 sub .. + 31)
+    const int r = sub * 32 + lane;            // row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const uint32_t lb = tbl | (static_cast<uint32_t>(lane) << 2);
     const uint32_t nq = tbl | (128u + (static_cast<uint32_t>(lane & 7) << 2));
-    int st = 0, a = 0;
-    uint32_t ph = 0, aph = 0, accph = 0;
+    const uint32_t csel = 0x7604u | (static_cast<uint32_t>(d) << 4);  // absmax code byte d
+    // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
+    const uint32_t w_off0 = static_cast<uint32_t>(r * 128) + (((2u * d) ^ (r & 7u)) << 4);
+    const uint32_t w_off1 = static_cast<uint32_t>(r * 128) + (((2u * d + 1u) ^ (r & 7u)) << 4);
+    int ws = 0, a = 0;
+    uint32_t wph = 0, aph = 0, accph = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
       const int t = it / p.slices, sl = it % p.slices;
       const int row = t * kTcRows + r;
-      // Scales, fetched well ahead of use: a 32-bit word of absmax codes covers
-      // blocks 4j..4j+3 of the slice, i.e. this thread's blocks of stages 2j and
-      // 2j+1 (bytes d and d + 2, one 256-block nested group since 4 | 256); three
-      // words (six stages) are in flight.  Plain fp32 absmax: two floats per word.
+      // Scales, fetched three stages ahead: the 32-bit word j of absmax codes
+      // covers blocks 4j..4j+3 of the slice (stage j; one 256-block nested
+      // group since 4 | 256), this warp's block is byte d.
       const int64_t rb = static_cast<int64_t>(row) * nblk + sl * p.bps;  // 4-aligned (plan)
-      const int nwords = p.bps / 4;
       uint32_t c0 = 0, c1 = 0, c2 = 0;
-      float n0 = 0.f, n1 = 0.f, n2 = 0.f, m0 = 0.f, m1 = 0.f, m2 = 0.f;
-      auto fetch = [&](int j, uint32_t& c, float& n, float& m) {
-        if (j >= nwords) return;
+      float n0 = 0.f, n1 = 0.f, n2 = 0.f;
+      auto fetch = [&](int j, uint32_t& c, float& n) {
+        if (j >= kst) return;
         if (NESTED) {
           c = __ldg(reinterpret_cast<const uint32_t*>(p.w.absmax_code + rb) + j);
           n = __ldg(p.w.nested_absmax + ((rb + 4 * j) >> 8));
         } else {
           n = __ldg(p.w.absmax_f32 + rb + 4 * j + d);
-          m = __ldg(p.w.absmax_f32 + rb + 4 * j + 2 + d);
         }
       };
-      fetch(0, c0, n0, m0);
-      fetch(1, c1, n1, m1);
-      fetch(2, c2, n2, m2);
+      fetch(0, c0, n0);
+      fetch(1, c1, n1);
+      fetch(2, c2, n2);
       for (int ks = 0; ks < kst; ++ks) {
-        const bool odd = ks & 1;
         float am;
         if (NESTED) {
-          // code byte d (even stage) or d + 2 (odd stage) of c0 -> nested map entry
-          const uint32_t sel = 0x7604u | (static_cast<uint32_t>(d + (odd ? 2 : 0)) << 4);
           uint32_t ca, nv;
-          asm("prmt.b32 %0, %1, %2, %3;" : "=r"(ca) : "r"(c0), "r"(nq), "r"(sel));
+          asm("prmt.b32 %0, %1, %2, %3;" : "=r"(ca) : "r"(c0), "r"(nq), "r"(csel));
           asm volatile("ld.shared.u32 %0, [%1];" : "=r"(nv) : "r"(ca));
           am = __fadd_rn(__fmul_rn(__uint_as_float(nv), n0), p.w.offset);
         } else {
-          am = odd ? m0 : n0;
+          am = n0;
         }
-        if (odd) {  // word consumed: rotate and fetch three words ahead
-          c0 = c1; n0 = n1; m0 = m1;
-          c1 = c2; n1 = n2; m1 = m2;
-          fetch(ks / 2 + 3, c2, n2, m2);
-        }
+        c0 = c1; n0 = n1;
+        c1 = c2; n1 = n2;
+        fetch(ks + 3, c2, n2);
         const uint32_t am2 = pack_bf16x2(am, am);
-        if (!mbar_wait(&full[st], ph, abort_flag, p.status)) { ok = false; break; }
-        const uint32_t wrow = stage_addr(st) + kXBytes + r * kTcWPitch + d * 32;
-        const uint4 w0 = lds128u(wrow), w1 = lds128u(wrow + 16);
+        if (!mbar_wait(&full[ws], wph, abort_flag, p.status)) { ok = false; break; }
+        const uint32_t wa = slot_s[ws];
+        const uint4 w0 = lds128u(wa + w_off0);
+        const uint4 w1 = lds128u(wa + w_off1);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&wfree[st]);
+        if (lane == 0) mbar_arrive(&wfree[ws]);
+        if (++ws == nst) { ws = 0; wph ^= 1; }
         uint32_t o[32];
         decode_word(w0.x, lb, am2, o + 0);
         decode_word(w0.y, lb, am2, o + 4);
@@ -383,30 +367,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) nf4_gemv_tc_kernel(const TcPara
         decode_word(w1.w, lb, am2, o + 28);
         if (!mbar_wait(&aempty[a], aph ^ 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
-        tmem_st_32x32b_x32(tmem_base + lane_off + a * 64 + d * 32, o);
+        tmem_st_32x32b_x32(tmem_base + lane_off + a * 128 + d * 32, o);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[a]);
         if (++a == kTcABufs) { a = 0; aph ^= 1; }
-        if (++st == nst) { st = 0; ph ^= 1; }
       }
       if (!ok) break;
-      // drain this warp's half of the accumulator columns
+      // drain this warp's quarter of the columns of both accumulators
       if (!mbar_wait(accfull, accph, abort_flag, p.status)) break;
       tc_fence_after();
-      uint32_t v[NTOK / 2];
-      tmem_ld_32x32b<NTOK / 2>(tmem_base + lane_off + kTcAcc + d * (NTOK / 2), v);
-      tmem_ld_wait();
+      constexpr int kQ = NTOK / 4;
+      float v[kQ];
+#pragma unroll
+      for (int q = 0; q < kQ; q += 4) {
+        uint32_t v0[4], v1[4];
+        tmem_ld_32x32b_x4(tmem_base + lane_off + kTcAcc + d * kQ + q, v0);
+        tmem_ld_32x32b_x4(tmem_base + lane_off + kTcAcc + 64 + d * kQ + q, v1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[q + j] = __uint_as_float(v0[j]) + __uint_as_float(v1[j]);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty);
       accph ^= 1;
       float* out = p.partial + static_cast<int64_t>(sl) * p.M * N + row;
 #pragma unroll
-      for (int j = 0; j < NTOK / 2; ++j) {
-        const int tk = d * (NTOK / 2) + j;
-        if (tk < p.M) out[static_cast<int64_t>(tk) * N] = __uint_as_float(v[j]);
+      for (int j = 0; j < kQ; ++j) {
+        const int tk = d * kQ + j;
+        if (tk < p.M) out[static_cast<int64_t>(tk) * N] = v[j];
       }
     }
   }
@@ -419,18 +410,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) nf4_gemv_tc_kernel(const TcPara
 }
 
 struct TcPlan {
-  int ntok, slices, bps, items, grid, nst, stage_bytes;
+  int ntok, slices, bps, items, grid, nst, xbytes;
 };
 
-// Slices (block counts that are multiples of 4 dividing K/64) minimising the busiest CTA's weight
-// bytes plus the split-K partial traffic, over `sms` CTAs.
+// Token padding, ring depth and the K slicing (block counts that are multiples
+// of 4 dividing K/64) minimising the busiest CTA's weight bytes plus the
+// split-K partial traffic, over `sms` CTAs.  Ring depths are those whose slots
+// fit by first-fit around the 64 KB-aligned table for any static shared size
+// up to 2 KB.
 TcPlan make_tc_plan(int64_t m, int64_t N, int64_t K, int sms) {
   TcPlan best{};
   const int64_t nblk = K / 64, tiles = N / kTcRows;
-  const int ntok = m <= 16 ? 16 : m <= 32 ? 32 : 64;
-  const int stage_bytes = 2 * ntok * 128 + ((kTcWBytes + 1023) / 1024) * 1024;
-  int nst = (kTcSmem - 1024 - stage_bytes - kTcTbl) / stage_bytes;
-  if (nst > kTcMaxSt) nst = kTcMaxSt;
+  const int ntok = m <= 16 ? 16 : m <= 32 ? 32 : m <= 48 ? 48 : 64;
+  const int xbytes = 4 * ntok * 128;
+  const int nst = ntok == 16 ? 6 : ntok == 32 ? 4 : 3;
   double best_cost = -1.0;
   for (int64_t bps = 4; bps <= nblk; bps += 4) {
     if (nblk % bps != 0) continue;
@@ -443,7 +436,7 @@ TcPlan make_tc_plan(int64_t m, int64_t N, int64_t K, int sms) {
     const double cost = wbytes + pbytes;
     if (best_cost < 0 || cost < best_cost) {
       best = TcPlan{ntok, static_cast<int>(slices), static_cast<int>(bps), static_cast<int>(items),
-                    static_cast<int>(grid), nst, stage_bytes};
+                    static_cast<int>(grid), nst, xbytes};
       best_cost = cost;
     }
   }
@@ -459,7 +452,7 @@ bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slic
   if (m < lo || m > 64 || n_out % kTcRows != 0 || k_in % 256 != 0) return false;
   if (n_out * k_in / 2 >= (1ll << 31)) return false;
   const TcPlan pl = make_tc_plan(m, n_out, k_in, num_sms);
-  if (pl.slices == 0 || pl.nst < 2) return false;
+  if (pl.slices == 0) return false;
   if (slices) *slices = pl.slices;
   return true;
 }
@@ -467,18 +460,26 @@ bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slic
 int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
                        cudaStream_t st, int num_sms) {
   const TcPlan pl = make_tc_plan(m, w.n_out, w.k_in, num_sms);
-  if (pl.slices == 0 || pl.nst < 2) return FITQ_ERR_UNSUPPORTED;
+  if (pl.slices == 0) return FITQ_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(w.absmax_code) & 3) != 0) return FITQ_ERR_ALIGN;  // word reads
+  if (((reinterpret_cast<uintptr_t>(w.packed) | reinterpret_cast<uintptr_t>(x)) & 15) != 0)
+    return FITQ_ERR_ALIGN;  // TMA sources
+  CUtensorMap tm_w, tm_x;
+  if (!encode_tmap_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.k_in / 2, w.n_out, w.k_in / 2,
+                      128u, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
+      !encode_tmap_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, w.k_in, m, w.k_in * 2, 64u,
+                      static_cast<uint32_t>(pl.ntok), CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+    return FITQ_ERR_CUDA;
   TcParams p;
   p.w = w;
-  p.x = static_cast<const __nv_bfloat16*>(x);
   p.M = static_cast<int>(m);
   p.tiles = static_cast<int>(w.n_out / kTcRows);
   p.slices = pl.slices;
   p.bps = pl.bps;
   p.items = pl.items;
   p.nst = pl.nst;
-  p.stage_bytes = pl.stage_bytes;
+  p.xbytes = pl.xbytes;
   p.partial = partial;
   p.status = status;
   const bool nested = w.absmax_f32 == nullptr;
@@ -492,10 +493,12 @@ int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partia
       if (e != cudaSuccess) return FITQ_ERR_CUDA;                                               \
       attr[nested] = true;                                                                      \
     }                                                                                           \
-    e = launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(kTcThreads), kTcSmem, st, p); \
+    e = launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(kTcThreads), kTcSmem, st,     \
+                   tm_w, tm_x, p);                                                              \
   }
   FITQ_TC_CASE(16)
   FITQ_TC_CASE(32)
+  FITQ_TC_CASE(48)
   FITQ_TC_CASE(64)
 #undef FITQ_TC_CASE
   note_launch();

@@ -140,10 +140,16 @@ int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEp
 int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
                                cudaStream_t st, int num_sms);
 
+// 2-D tiled tensor map [outer rows][inner elements], row pitch row_bytes; elements
+// outside the tensor read as zero (gemm_sm100.cu).
+bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2);
+
 // NF4 skinny GEMM on tcgen05 with the decoded weights in tensor memory
 // (gemv_tc.cu), 8 < M <= 64 (FITQ_GEMV_TC=1: also M <= 8, =0: never);
-// N % 128 == 0, K % 128 == 0.  Writes fp32 split-K partials [slices, M, N]
-// for launch_nf4_gemv_dec_finish.
+// N % 128 == 0, K % 256 == 0, packed weights and x 16-byte aligned.  Writes
+// fp32 split-K partials [slices, M, N] for launch_nf4_gemv_dec_finish.
 bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slices);
 int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
                        cudaStream_t st, int num_sms);

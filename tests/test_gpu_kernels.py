@@ -165,7 +165,8 @@ def test_gemv_paths(cuda_dev, m, n, k, r):
                                             (8, 3072, 1024, 16, False), (5, 1024, 5120, 0, False),
                                             (1, 128, 256, 0, True), (16, 2048, 5120, 16, True),
                                             (40, 1024, 5120, 16, True), (64, 512, 1024, 0, False),
-                                            (33, 384, 27648, 0, True)])
+                                            (33, 384, 27648, 0, True), (48, 640, 5120, 16, False),
+                                            (24, 1152, 1024, 0, True), (47, 256, 2048, 16, True)])
 def test_gemv_decode_kernels(cuda_dev, monkeypatch, variant, m, n, k, r, nested):
     """The M <= 8 decode kernel, the tcgen05 skinny GEMM with the decoded
     weights in tensor memory (M <= 64; forced for M <= 8 by "tc") and the
