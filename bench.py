@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--cpu-seq", type=int, default=2048)
+    ap.add_argument("--gemv-case", default=None,
+                    help="N,K,M[,R]: run one NF4 GEMV shape and exit (a profiling target)")
     ap.add_argument("--full-step", choices=["auto", "on", "off"], default="auto",
                     help="also time a full 64-layer step with shards streamed from pinned host "
                          "memory (auto: on one GPU only; every rank builds the 64-layer host store)")
@@ -318,6 +320,35 @@ def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, st
     return out
 
 
+def gemv_case(dev, spec):
+    """One NF4 GEMV shape on its own ("N,K,M[,R]"): three warm calls, then 20
+    timed ones on one weight (L2-resident when it fits: a profiling target, not
+    a bench number).  Used to capture the decode kernels under ncu."""
+    import torch
+    from fitllm_b200 import ops
+    from fitllm_b200.nf4 import Nf4WeightCRef, quantize_nf4
+    n, k, m, r = (list(map(int, spec.split(","))) + [0])[:4]
+    g = torch.Generator(device=dev).manual_seed(12)
+    w = torch.randn(n, k, generator=g, device=dev) * 0.02
+    wr = Nf4WeightCRef(*quantize_nf4(w))
+    del w
+    A = (torch.rand(r, k, generator=g, device=dev) - 0.5) * 0.02 if r else None
+    B = torch.randn(n, r, generator=g, device=dev) * 0.01 if r else None
+    x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+    for _ in range(3):
+        ops.qlora_forward(x, wr, A, B, 2.0, gemv=True)
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(20):
+        ops.qlora_forward(x, wr, A, B, 2.0, gemv=True)
+    e_ev.record()
+    torch.cuda.synchronize()
+    if ops.device_status() != 0:
+        raise RuntimeError("device status error in the GEMV case")
+    return {"gemv_case": spec, "us_per_call": round(s_ev.elapsed_time(e_ev) * 1000.0 / 20, 2)}
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -367,6 +398,10 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     L = _lib.load()
+    if a.gemv_case:
+        if rank == 0:
+            print(json.dumps(gemv_case(dev, a.gemv_case)), flush=True)
+        return
 
     cfg = LayerConfig.qwen25_32b()
     sched, store = build_synthetic_model(cfg, 1, dev, seed=0)
@@ -520,7 +555,7 @@ def main():
                               "the HBM budget, so their backward skips the recompute",
                       "value_recompute_every_layer": round(tokens / (ms_rc / 1000.0), 1),
                       "ms_per_step_recompute_every_layer": round(ms_rc, 3)},
-        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn_kernel (tcgen05)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn (tcgen05; the cta_group::2 kernel on these shapes)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if achieved else None,
                      "peak_source": peak_src, "traffic": None,
