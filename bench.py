@@ -265,7 +265,8 @@ def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, re
             "ms_per_pass": round(ms, 3), "tokens_per_s": round(batch * t / (ms / 1000.0), 1),
             "bytes_per_pass": int(wbytes + kv), "GB/s": round(gbs, 1),
             "frac_of_hbm": round(gbs / peak_gbs, 3), "m_per_projection": batch * t,
-            "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention torch SDPA"}
+            "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention on the "
+                    "split-KV verify kernel (fitq_verify_attention)"}
 
 
 def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, steps=2):

@@ -649,6 +649,43 @@ int fitq_rope(const void* t, void* out, const float* cos_half, const float* sin_
                                          backward, static_cast<cudaStream_t>(stream), sms), "rope");
 }
 
+size_t fitq_verify_attention_workspace(int64_t batch, int heads, int kv_heads, int t_new,
+                                       int prefix) {
+  (void)heads;
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms || batch <= 0 || kv_heads <= 0 || t_new <= 0 || prefix < 0) return 0;
+  return fitq::verify_attention_workspace(batch, kv_heads, prefix + t_new, sms);
+}
+
+int fitq_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                          int64_t batch, int heads, int kv_heads, int t_new, int prefix,
+                          int capacity, int head_dim, void* workspace, size_t workspace_bytes,
+                          fitq_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !out || !workspace)
+    return fail(FITQ_ERR_ARG, "verify_attention: NULL tensor or workspace");
+  if (batch <= 0 || batch > 65535 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 ||
+      kv_heads > 65535 || t_new <= 0 || prefix < 0 || prefix + t_new > capacity)
+    return fail(FITQ_ERR_SHAPE, "verify_attention: bad shape (B=%lld H=%d KVH=%d T=%d prefix=%d cap=%d)",
+                (long long)batch, heads, kv_heads, t_new, prefix, capacity);
+  if (head_dim != 128 || (heads / kv_heads) * t_new > 32)
+    return fail(FITQ_ERR_UNSUPPORTED,
+                "verify_attention: needs head_dim 128 and (H / KVH) * T <= 32 (D=%d G*T=%d)", head_dim,
+                (heads / kv_heads) * t_new);
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(out) || !al16(workspace))
+    return fail(FITQ_ERR_ALIGN, "verify_attention: 16-byte alignment");
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms) return rc;
+  const size_t need = fitq::verify_attention_workspace(batch, kv_heads, prefix + t_new, sms);
+  if (workspace_bytes < need)
+    return fail(FITQ_ERR_WORKSPACE, "verify_attention: workspace %zu < %zu bytes", workspace_bytes, need);
+  return launch_status(fitq::launch_verify_attention(q, k_cache, v_cache, out, batch, heads, kv_heads,
+                                                     t_new, prefix, capacity, workspace,
+                                                     static_cast<cudaStream_t>(stream), sms),
+                       "verify_attention");
+}
+
 int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n, fitq_stream_t stream) {
   if (!gate || !up || !act) return fail(FITQ_ERR_ARG, "swiglu: NULL tensor");
   if (n <= 0 || n % 8 != 0) return fail(FITQ_ERR_SHAPE, "swiglu: need n %% 8 == 0");

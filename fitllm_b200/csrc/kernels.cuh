@@ -154,6 +154,13 @@ bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slic
 int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
                        cudaStream_t st, int num_sms);
 
+// Speculative-verify attention over a KV cache (attn.cu): q, out [B, T, H, 128],
+// caches [B, KVH, cap, 128] bf16, (H / KVH) * T <= 32, prefix + T <= cap.
+size_t verify_attention_workspace(int64_t batch, int kv_heads, int len, int num_sms);
+int launch_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                            int64_t batch, int heads, int kv_heads, int t_new, int prefix, int cap,
+                            void* workspace, cudaStream_t st, int num_sms);
+
 // NF4 GEMV / skinny GEMM for M <= 64 (gemv.cu): split-K partial products
 // [splits, M, N] fp32, then a finishing pass adding LoRA / y_add -> bf16.
 size_t gemv_partial_bytes(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* splits_out);

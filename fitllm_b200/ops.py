@@ -101,6 +101,31 @@ def qlora_backward(x2: Optional[torch.Tensor], dy2: torch.Tensor, w: Nf4WeightCR
     return (dx if need_dx else None), grad_a, grad_b
 
 
+def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     prefix: int) -> torch.Tensor:
+    """Attention of T new tokens over a KV cache (fitq_verify_attention).
+
+    q: [B, T, H, D] bf16 (post-RoPE); k_cache, v_cache: [B, KVH, cap, D] bf16 with
+    the new tokens' keys/values at [prefix, prefix + T).  Returns [B, T, H, D]
+    bf16; token i attends to positions <= prefix + i."""
+    L = _lib.load()
+    b, t, h, d = q.shape
+    kvh, cap = int(k_cache.shape[1]), int(k_cache.shape[2])
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("verify_attention: caches must be contiguous [B, KVH, cap, D]")
+    q = q.contiguous()
+    out = torch.empty_like(q)
+    dev = q.device
+    with torch.cuda.device(dev):
+        nbytes = L.fitq_verify_attention_workspace(b, h, kvh, t, prefix)
+        ws = _workspace(nbytes, dev)
+        _lib.check(L.fitq_verify_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                           out.data_ptr(), b, h, kvh, t, prefix, cap, d,
+                                           ws.data_ptr(), nbytes, _stream(dev)),
+                   "fitq_verify_attention")
+    return out
+
+
 def gemm_bf16_tn(a: torch.Tensor, b: torch.Tensor, c_add: Optional[torch.Tensor] = None) -> torch.Tensor:
     """c = a.b^T (+ c_add) on the tcgen05 tensor cores (bf16 in/out, fp32 accumulate)."""
     L = _lib.load()

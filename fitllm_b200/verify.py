@@ -12,6 +12,11 @@ The layer arithmetic is DecoderLayer's (fitllm_b200/layer.py): RMSNorm, q/k/v
 with bias, rotary embedding at the tokens' absolute positions, grouped-query
 attention (causal within the new tokens, full over the prefix), o_proj with
 the residual fused, RMSNorm, SwiGLU MLP with the residual fused.
+
+Attention runs on the library's split-KV kernel (fitq_verify_attention) when
+head_dim is 128 and (heads / kv_heads) * T <= 32 -- every verify step of the
+Qwen2.5 shapes; other shapes (e.g. filling a cache with a long prompt) use
+torch's scaled_dot_product_attention with the prefix + causal mask.
 """
 from __future__ import annotations
 
@@ -20,6 +25,7 @@ from typing import List, Tuple
 import torch
 import torch.nn.functional as F
 
+from . import ops
 from .layer import DecoderLayer, rotary_tables
 from .layer_ops import rope, swiglu
 
@@ -54,6 +60,11 @@ def verify_mask(prefix: int, t: int, device) -> torch.Tensor:
     return cols[None, :] <= (prefix + rows)[:, None]
 
 
+def kernel_attention_ok(cfg, t: int) -> bool:
+    """Shapes fitq_verify_attention covers: head_dim 128, (heads / kv_heads) * t <= 32."""
+    return cfg.head_dim == 128 and (cfg.heads // cfg.kv_heads) * t <= 32
+
+
 def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Tensor,
                          v_cache: torch.Tensor, prefix: int, tables: Tuple[torch.Tensor, torch.Tensor],
                          mask: torch.Tensor) -> torch.Tensor:
@@ -65,14 +76,18 @@ def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Te
     attn = layer.self_attn
     cos, sin = tables
     x = layer.input_layernorm(h)
-    q = rope(attn.q_proj(x), cos, sin, cfg.heads).view(b, t, cfg.heads, cfg.head_dim).transpose(1, 2)
+    q = rope(attn.q_proj(x), cos, sin, cfg.heads).view(b, t, cfg.heads, cfg.head_dim)
     k = rope(attn.k_proj(x), cos, sin, cfg.kv_heads).view(b, t, cfg.kv_heads, cfg.head_dim)
     v = attn.v_proj(x).view(b, t, cfg.kv_heads, cfg.head_dim)
     k_cache[:, :, prefix:prefix + t].copy_(k.transpose(1, 2))
     v_cache[:, :, prefix:prefix + t].copy_(v.transpose(1, 2))
-    o = F.scaled_dot_product_attention(q, k_cache[:, :, :prefix + t], v_cache[:, :, :prefix + t],
-                                       attn_mask=mask, enable_gqa=True)
-    o = o.transpose(1, 2).reshape(b, t, cfg.heads * cfg.head_dim)
+    if kernel_attention_ok(cfg, t):
+        o = ops.verify_attention(q, k_cache, v_cache, prefix)
+    else:
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k_cache[:, :, :prefix + t],
+                                           v_cache[:, :, :prefix + t], attn_mask=mask,
+                                           enable_gqa=True).transpose(1, 2)
+    o = o.reshape(b, t, cfg.heads * cfg.head_dim)
     h1 = attn.o_proj(o, residual=h)
     mlp = layer.mlp
     x2 = layer.post_attention_layernorm(h1)
@@ -86,7 +101,7 @@ def verify_pass(layers: List[DecoderLayer], h: torch.Tensor, cache: KVCache, pre
     t = h.shape[1]
     pos = torch.arange(prefix, prefix + t, device=h.device)
     tables = rotary_tables(t, cfg.head_dim, cfg.rope_theta, h.device, position_ids=pos)
-    mask = verify_mask(prefix, t, h.device)
+    mask = None if kernel_attention_ok(cfg, t) else verify_mask(prefix, t, h.device)
     for i, layer in enumerate(layers):
         h = verify_layer_forward(layer, h, cache.k[i], cache.v[i], prefix, tables, mask)
     return h

@@ -204,6 +204,22 @@ FITQ_API int fitq_rope(const void* t, void* out, const float* cos_half, const fl
                        fitq_stream_t stream);
 FITQ_API int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n,
                              fitq_stream_t stream);
+
+/* Speculative-verify attention over a key/value cache.  Replaces the
+ * re-run of the whole prefix that verifies draft tokens (fitllm/inference.py:
+ * 380-397, attention inside fitllm/forward.py's layer forward): the T new
+ * tokens of each sequence attend to prefix + T cached positions, token i to
+ * positions <= prefix + i.  q, out: [B, T, H, head_dim] bf16 (post-RoPE q_proj
+ * output / o_proj input); k_cache, v_cache: [B, KVH, capacity, head_dim] bf16
+ * with the new tokens' keys/values already at [prefix, prefix + T).  Scale
+ * 1/sqrt(head_dim), fp32 softmax and accumulation.  Needs head_dim == 128 and
+ * (H / KVH) * T <= 32 (FITQ_ERR_UNSUPPORTED otherwise). */
+FITQ_API size_t fitq_verify_attention_workspace(int64_t batch, int heads, int kv_heads, int t_new,
+                                                int prefix);
+FITQ_API int fitq_verify_attention(const void* q, const void* k_cache, const void* v_cache,
+                                   void* out, int64_t batch, int heads, int kv_heads, int t_new,
+                                   int prefix, int capacity, int head_dim, void* workspace,
+                                   size_t workspace_bytes, fitq_stream_t stream);
 FITQ_API int fitq_swiglu_bwd(const void* d_act, const void* gate, const void* up, void* d_gate,
                              void* d_up, int64_t n, fitq_stream_t stream);
 

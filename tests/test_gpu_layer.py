@@ -290,14 +290,17 @@ def test_fused_layer_kernels_vs_torch(cuda_dev):
     assert onf4.rel_err(up.grad.float().cpu().numpy(), ur.grad.cpu().numpy()) < REL
 
 
-def test_verify_pass_matches_full_forward(cuda_dev):
+@pytest.mark.parametrize("head_dim,heads,kv_heads,p", [(64, 4, 2, 16), (128, 8, 2, 100)])
+def test_verify_pass_matches_full_forward(cuda_dev, head_dim, heads, kv_heads, p):
     """KV-cached verify (fitllm_b200/verify.py): filling the cache with the
     prefix, then running only the T new tokens of each sequence, gives the
     same last-T hidden states as the full causal forward over prefix + new
-    tokens (the reference's re-prefill), within 1e-2."""
+    tokens (the reference's re-prefill), within 1e-2.  head_dim 128 runs the
+    verify step on fitq_verify_attention, head_dim 64 on torch SDPA."""
     from fitllm_b200.layer import DecoderLayer, LayerConfig, add_lora_, quantize_layer_
     from fitllm_b200.verify import KVCache, verify_pass
-    cfg = LayerConfig(hidden=256, heads=4, kv_heads=2, head_dim=64, intermediate=512)
+    cfg = LayerConfig(hidden=heads * head_dim, heads=heads, kv_heads=kv_heads, head_dim=head_dim,
+                      intermediate=512)
     layers = []
     for i in range(2):
         layer = DecoderLayer(cfg, device=cuda_dev)
@@ -305,7 +308,7 @@ def test_verify_pass_matches_full_forward(cuda_dev):
         add_lora_(layer, 16, 32.0, ("q_proj", "v_proj"), seed=i, b_std=0.01)
         layer.eval()
         layers.append(layer)
-    b, p, t = 2, 16, 5
+    b, t = 2, 5
     g = torch.Generator(device=cuda_dev).manual_seed(9)
     h = torch.randn(b, p + t, cfg.hidden, generator=g, device=cuda_dev).bfloat16()
     with torch.no_grad():
