@@ -18,23 +18,24 @@
 // not grow with M.
 //
 // A stage is four 64-column blocks (256 K values) of one 128-row tile: its
-// packed bytes (16 KB) and the four matching x tiles.  One CTA per SM, 19 warps:
+// packed bytes (16 KB) and the four matching x tiles.  One CTA per SM, 21 warps:
 //   warp 0      producer: per stage one TMA load of the packed bytes (128 rows
 //               x 128 B, 128-byte swizzle: conflict-free 16-byte reads by row)
 //               and four of the x tiles (tokens >= M read as zeros), issued
 //               together on one barrier.  Loads leave the TMA unit in order,
 //               so x issued later than its weights would wait behind every
 //               weight load queued in between;
-//   warps 1, 2  MMA issuers: one lane each issues the MMAs of blocks 0-1
-//               (warp 1) or 2-3 (warp 2) of every stage into its own fp32
-//               accumulator.  One thread waits about 50 cycles on each
-//               M=128, K=16 MMA whatever N <= 64 is; two issuing threads keep
-//               the tensor core about twice as busy.  Warp 1 also allocates
-//               TMEM (three 128-column A buffers + two accumulators);
-//   warps 3-18  decoders: warp w decodes block (w - 3) / 4 of every stage for
+//   warps 1-4   MMA issuers: one lane of warp 1 + b issues the four MMAs of
+//               block b of every stage into its own fp32 accumulator.  One
+//               thread waits about 50 cycles on each M=128, K=16 MMA whatever
+//               N <= 64 is; four issuers (one per SM sub-partition) bring a
+//               stage's 16 MMAs to the tensor core's own rate.  Warp 1 also
+//               allocates TMEM: A buffers of 128 columns (three for NTOK <= 32,
+//               two above) and the four accumulators;
+//   warps 5-20  decoders: warp w decodes block (w - 5) / 4 of every stage for
 //               the 32 rows of TMEM sub-partition w % 4; at the end of an item
-//               each drains NTOK / 4 columns of both accumulators and writes
-//               their sum as the fp32 partials.
+//               each drains NTOK / 4 columns of the four accumulators and
+//               writes their sum as the fp32 partials.
 // Work items are (128-row tile, K slice) pairs, walked by the CTAs with a grid
 // stride.  Every mbarrier wait is bounded (common.cuh); no multicast.
 #include "common.cuh"
@@ -43,17 +44,20 @@
 namespace fitq {
 namespace {
 
-constexpr int kTcWarps = 19;
+constexpr int kTcWarps = 21;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr int kTcDecWarp0 = 3;          // first decoder warp
+constexpr int kTcDecWarp0 = 5;          // first decoder warp (issuers are warps 1-4)
 constexpr int kTcRows = 128;            // weight rows per tile (UMMA M)
 constexpr int kTcWStage = kTcRows * 128;  // packed bytes of one stage (four blocks per row)
 constexpr int kTcTbl = 256 * 256;       // code-pair table, 64 KB aligned
 constexpr int kTcMaxSt = 8;
 constexpr int kTcSmem = 232448 - 2048;  // dynamic shared memory (static part holds barriers)
 constexpr int kTcTmemCols = 512;
-constexpr int kTcABufs = 3;             // A buffers (128 columns each), then the accumulators
-constexpr int kTcAcc = kTcABufs * 128;  // accumulator of issuer i at kTcAcc + 64 i
+constexpr int kTcMaxABufs = 3;          // A buffers (128 columns each), then the accumulators
+// TMEM plan per token padding: A buffers, first accumulator column, column
+// stride of the four accumulators (3 x 128 + 4 x 32 or 2 x 128 + 4 x 64 = 512).
+__host__ __device__ constexpr int tc_abufs(int ntok) { return ntok <= 32 ? 3 : 2; }
+__host__ __device__ constexpr int tc_acc_stride(int ntok) { return ntok <= 32 ? 32 : 64; }
 
 struct TcParams {
   Nf4Args w;
@@ -138,18 +142,20 @@ template <int NTOK, bool NESTED>
 __global__ void __launch_bounds__(kTcThreads, 1)
     nf4_gemv_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_x, const TcParams p) {
-  __shared__ uint64_t bars[3 * kTcMaxSt + 2 * kTcABufs + 3];
+  __shared__ uint64_t bars[3 * kTcMaxSt + 2 * kTcMaxABufs + 3];
   __shared__ uint32_t slot_s[2 * kTcMaxSt];  // W slot of stage s at [s], x slot at [kTcMaxSt + s]
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_s, never_s, layout_ok_s;
   uint64_t* full = bars;                  // producer -> decoders + MMA (TMA bytes, W and x)
   uint64_t* wfree = full + kTcMaxSt;      // decoders read the W slot (count 16)
-  uint64_t* xfree = wfree + kTcMaxSt;     // MMAs done with the x slot (2 commits)
-  uint64_t* afull = xfree + kTcMaxSt;     // [kTcABufs] decoders wrote A buffer (count 16)
-  uint64_t* aempty = afull + kTcABufs;    // [kTcABufs] MMAs done with A buffer (2 commits)
-  uint64_t* accfull = aempty + kTcABufs;  // item's MMAs done (2 commits)
+  constexpr int kABufs = tc_abufs(NTOK), kAccStride = tc_acc_stride(NTOK);
+  constexpr int kAcc = kABufs * 128;      // accumulator of issuer b at kAcc + b kAccStride
+  uint64_t* xfree = wfree + kTcMaxSt;     // MMAs done with the x slot (4 commits)
+  uint64_t* afull = xfree + kTcMaxSt;     // [kABufs] decoders wrote A buffer (count 16)
+  uint64_t* aempty = afull + kTcMaxABufs; // [kABufs] MMAs done with A buffer (4 commits)
+  uint64_t* accfull = aempty + kTcMaxABufs;  // item's MMAs done (4 commits)
   uint64_t* accempty = accfull + 1;       // accumulators drained (count 16)
-  uint64_t* done = accfull + 2;           // every issued MMA retired (2 commits)
+  uint64_t* done = accfull + 2;           // every issued MMA retired (4 commits)
   volatile int* abort_flag = &abort_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -176,15 +182,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int s = 0; s < kTcMaxSt; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&wfree[s], 16);
-      mbar_init(&xfree[s], 2);
+      mbar_init(&xfree[s], 4);
     }
-    for (int a = 0; a < kTcABufs; ++a) {
+    for (int a = 0; a < kABufs; ++a) {
       mbar_init(&afull[a], 16);
-      mbar_init(&aempty[a], 2);
+      mbar_init(&aempty[a], 4);
     }
-    mbar_init(accfull, 2);
+    mbar_init(accfull, 4);
     mbar_init(accempty, 16);
-    mbar_init(done, 2);
+    mbar_init(done, 4);
     abort_s = 0;
     never_s = 0;
     fence_mbar_init();
@@ -256,14 +262,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never_s, p.status);
     }
     __syncwarp();
-  } else if (warp == 1 || warp == 2) {
+  } else if (warp < kTcDecWarp0) {
     // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
-      const int half = warp - 1;  // blocks 2 half and 2 half + 1 of every stage
+      const int blk = warp - 1;  // block of every stage this thread multiplies
       int xs = 0, a = 0;
       uint32_t xph = 0, aph = 0, accph = 0;  // x slot = ring stage
       bool ok = true;
-      const uint32_t acc = tmem_base + kTcAcc + 64 * half;
+      const uint32_t acc = tmem_base + kAcc + kAccStride * blk;
       for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
         if (!mbar_wait(accempty, accph ^ 1, abort_flag, p.status)) break;
         tc_fence_after();
@@ -276,18 +282,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();
           // Keep the per-MMA work to two adds: both offsets stay inside the
           // 14-bit start-address field (shared addresses < 256 KB).
-          const uint64_t xd = umma_smem_desc_sw128(slot_s[kTcMaxSt + xs] + 2 * half * kXTile);
-          const uint32_t ad = tmem_base + a * 128 + 64 * half;
+          const uint64_t xd = umma_smem_desc_sw128(slot_s[kTcMaxSt + xs] + blk * kXTile);
+          const uint32_t ad = tmem_base + a * 128 + 32 * blk;
           umma_bf16_ts(acc, ad, xd, idesc, ks > 0 ? 1u : 0u);
 #pragma unroll
-          for (int i = 1; i < 8; ++i) {
-            const int b = i >> 2, kk = i & 3;
-            umma_bf16_ts(acc, ad + b * 32 + kk * 8, xd + static_cast<uint64_t>((b * kXTile + kk * 32) >> 4),
-                         idesc, 1u);
-          }
+          for (int kk = 1; kk < 4; ++kk)
+            umma_bf16_ts(acc, ad + kk * 8, xd + static_cast<uint64_t>((kk * 32) >> 4), idesc, 1u);
           umma_commit(&aempty[a]);
           umma_commit(&xfree[xs]);
-          if (++a == kTcABufs) { a = 0; aph ^= 1; }
+          if (++a == kABufs) { a = 0; aph ^= 1; }
           if (++xs == nst) { xs = 0; xph ^= 1; }
         }
         if (!ok) break;
@@ -372,22 +375,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[a]);
-        if (++a == kTcABufs) { a = 0; aph ^= 1; }
+        if (++a == kABufs) { a = 0; aph ^= 1; }
       }
       if (!ok) break;
-      // drain this warp's quarter of the columns of both accumulators
+      // drain this warp's quarter of the columns of the four accumulators
       if (!mbar_wait(accfull, accph, abort_flag, p.status)) break;
       tc_fence_after();
       constexpr int kQ = NTOK / 4;
       float v[kQ];
 #pragma unroll
       for (int q = 0; q < kQ; q += 4) {
-        uint32_t v0[4], v1[4];
-        tmem_ld_32x32b_x4(tmem_base + lane_off + kTcAcc + d * kQ + q, v0);
-        tmem_ld_32x32b_x4(tmem_base + lane_off + kTcAcc + 64 + d * kQ + q, v1);
+        uint32_t v0[4], v1[4], v2[4], v3[4];
+        const uint32_t col = tmem_base + lane_off + kAcc + d * kQ + q;
+        tmem_ld_32x32b_x4(col, v0);
+        tmem_ld_32x32b_x4(col + kAccStride, v1);
+        tmem_ld_32x32b_x4(col + 2 * kAccStride, v2);
+        tmem_ld_32x32b_x4(col + 3 * kAccStride, v3);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[q + j] = __uint_as_float(v0[j]) + __uint_as_float(v1[j]);
+        for (int j = 0; j < 4; ++j)
+          v[q + j] = (__uint_as_float(v0[j]) + __uint_as_float(v1[j])) +
+                     (__uint_as_float(v2[j]) + __uint_as_float(v3[j]));
       }
       tc_fence_before();
       __syncwarp();
