@@ -222,23 +222,14 @@ class ShardStationaryEngine:
         return self.backward(acts, grad_out)
 
 
-def build_synthetic_model(cfg: LayerConfig, num_layers: int, device, seed: int = 0,
-                          ring_slots: int = 2, pin_memory: bool = True, lora_b_std: float = 0.01):
-    """Random-init NF4 layers (quantised on the device, per-layer seeds) loaded
-    into a pinned host store, plus a LoRAStore with PEFT-initialised adapters
-    (B ~ N(0, lora_b_std) so that dA is non-zero).  Returns (scheduler, store)."""
-    dev = torch.device(device)
-    sched = ShardScheduler(num_layers, dev, ring_slots=ring_slots, pin_memory=pin_memory)
-    proto = DecoderLayer(cfg, device=dev)
+def _lora_store(cfg: LayerConfig, num_layers: int, dev, seed: int, lora_b_std: float) -> LoRAStore:
+    """LoRAStore with PEFT-initialised adapters per layer: A ~ U(-1/sqrt(K),
+    1/sqrt(K)) (Kaiming-uniform, a=sqrt(5)); B zeros, or N(0, lora_b_std)."""
+    proto = DecoderLayer(cfg, device="meta")
     add_lora_(proto, cfg.lora_rank, cfg.lora_alpha, cfg.lora_targets, seed=0)
     entries = lora_entries(proto)
     store = LoRAStore(num_layers, entries, dev)
-    from .layer import quantize_layer_
     for l in range(num_layers):
-        quantize_layer_(proto, seed=seed * 1000 + l)
-        sched.add_layer(l, layer_shard(proto))
-        # PEFT init per layer: A ~ U(-1/sqrt(K), 1/sqrt(K)) (Kaiming-uniform,
-        # a=sqrt(5)); B zeros, or N(0, lora_b_std) when lora_b_std > 0.
         g = torch.Generator(device=dev).manual_seed(seed * 7919 + l)
         vals = {}
         for name, shape in entries:
@@ -250,6 +241,46 @@ def build_synthetic_model(cfg: LayerConfig, num_layers: int, device, seed: int =
             else:
                 vals[name] = torch.zeros(shape, device=dev)
         store.init_layer_(l, vals)
+    return store
+
+
+def synthetic_layer_shards(cfg: LayerConfig, num_layers: int, device, seed: int = 0):
+    """Yields the flat shard key set of each random-init NF4 layer (quantised
+    on the device with per-layer seeds seed * 1000 + l)."""
+    from .layer import quantize_layer_
+    proto = DecoderLayer(cfg, device=torch.device(device))
+    for l in range(num_layers):
+        quantize_layer_(proto, seed=seed * 1000 + l)
+        yield layer_shard(proto)
     del proto
+
+
+def build_synthetic_model(cfg: LayerConfig, num_layers: int, device, seed: int = 0,
+                          ring_slots: int = 2, pin_memory: bool = True, lora_b_std: float = 0.01):
+    """Random-init NF4 layers (quantised on the device, per-layer seeds) loaded
+    into a pinned host store, plus a LoRAStore with PEFT-initialised adapters
+    (B ~ N(0, lora_b_std) so that dA is non-zero).  Returns (scheduler, store)."""
+    dev = torch.device(device)
+    sched = ShardScheduler(num_layers, dev, ring_slots=ring_slots, pin_memory=pin_memory)
+    for l, shard in enumerate(synthetic_layer_shards(cfg, num_layers, dev, seed)):
+        sched.add_layer(l, shard)
+    store = _lora_store(cfg, num_layers, dev, seed, lora_b_std)
     torch.cuda.empty_cache()
     return sched, store
+
+
+def build_model_from_shards(cfg: LayerConfig, shard_dir, num_layers: int, device,
+                            group_size: int = 1, verify_checksums: bool = True, seed: int = 0,
+                            ring_slots: int = 2, pin_memory: bool = True,
+                            lora_b_std: float = 0.01):
+    """The same (scheduler, store) pair from FitLLM-format shard files
+    (``layer_{i:03d}_weights.safetensors`` + ``.sha256``): each file is
+    checksummed and read once into the pinned host store; LoRA keys in the
+    files are dropped as the reference does (fitllm/forward.py:733-734) and the
+    adapters get the PEFT initialisation."""
+    from .shards import load_shards_into
+    dev = torch.device(device)
+    sched = ShardScheduler(num_layers, dev, ring_slots=ring_slots, pin_memory=pin_memory)
+    load_shards_into(sched, shard_dir, num_layers, group_size=group_size,
+                     verify_checksums=verify_checksums)
+    return sched, _lora_store(cfg, num_layers, dev, seed, lora_b_std)
