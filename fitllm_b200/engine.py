@@ -246,7 +246,8 @@ def _lora_store(cfg: LayerConfig, num_layers: int, dev, seed: int, lora_b_std: f
 
 def synthetic_layer_shards(cfg: LayerConfig, num_layers: int, device, seed: int = 0):
     """Yields the flat shard key set of each random-init NF4 layer (quantised
-    on the device with per-layer seeds seed * 1000 + l)."""
+    on the device with per-layer seeds seed * 1000 + l).  The tensors of one
+    yield are overwritten by the next: consume (copy) each before advancing."""
     from .layer import quantize_layer_
     proto = DecoderLayer(cfg, device=torch.device(device))
     for l in range(num_layers):

@@ -99,16 +99,29 @@ def write_layer_shards(layer_state_dicts: Iterable[Dict[str, torch.Tensor]], sha
                        group_size: int = 1) -> int:
     """Write per-layer state dicts as shard files (fitllm/model.py:25-83 layout).
     Returns the number of layers written."""
+    if group_size < 1:
+        raise ValueError("group_size must be >= 1")
     shard_dir = Path(shard_dir)
     shard_dir.mkdir(parents=True, exist_ok=True)
-    sds = list(layer_state_dicts)
-    for first, last in shard_groups(len(sds), group_size):
-        group: Dict[str, torch.Tensor] = {}
-        for off, i in enumerate(range(first, last + 1)):
-            for k, v in sds[i].items():
-                group[k if group_size == 1 else f"{off}.{k}"] = v
+    group: Dict[str, torch.Tensor] = {}
+    first = count = 0
+
+    def flush(last: int) -> None:
         save_shard_with_checksum(group, shard_dir / shard_file_name(first, last if group_size > 1 else None))
-    return len(sds)
+        group.clear()
+
+    # one group at a time, copied out: a producer may reuse its tensors for the next layer
+    for n, sd in enumerate(layer_state_dicts):
+        count = n + 1
+        off = n - first
+        for k, v in sd.items():
+            group[k if group_size == 1 else f"{off}.{k}"] = v.detach().to("cpu", copy=True)
+        if off == group_size - 1:
+            flush(n)
+            first = n + 1
+    if group:
+        flush(count - 1)
+    return count
 
 
 def split_group(tensors: Dict[str, torch.Tensor], count: int) -> List[Dict[str, torch.Tensor]]:

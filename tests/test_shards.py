@@ -94,3 +94,19 @@ def test_missing_or_corrupt_shard_fails_before_loading(tmp_path):
     with pytest.raises(RuntimeError, match="Checksum mismatch"):
         shards.load_shards_into(sched, tmp_path, 3)
     assert sched.num_layers == 3 and not sched._host  # nothing stored
+
+
+def test_writer_copies_each_layer_before_the_next(tmp_path):
+    """A producer that reuses one buffer for every layer (as the synthetic
+    model generator does) still gets one file per layer with its own values."""
+    buf = torch.zeros(8)
+
+    def layers():
+        for i in range(3):
+            buf.fill_(float(i))
+            yield {"w": buf}
+
+    assert shards.write_layer_shards(layers(), tmp_path) == 3
+    for i in range(3):
+        t = shards.load_shard_with_checksum(tmp_path / shards.shard_file_name(i))
+        assert torch.equal(t["w"], torch.full((8,), float(i)))
