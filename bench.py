@@ -273,13 +273,17 @@ def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, st
     """One full synthetic training step over 64 random-init
     NF4 Qwen2.5-32B-shaped layers whose shards live in pinned host memory and
     stream through the device ring (sharded upload + NCCL all-gather when
-    world > 1), 16 micro-batches of 1024 tokens split over the ranks, the
-    per-layer LoRA-gradient all-reduce, then clip + AdamW on the q/v adapters.
-    Device time per step (CUDA events, max over ranks)."""
+    world > 1), 16 micro-batches of 1024 tokens split over the ranks, the loss
+    of every micro-batch from the final norm + bf16 lm_head (vocab 152,064) +
+    cross-entropy on the device, the per-layer LoRA-gradient all-reduce, then
+    clip + AdamW on the q/v adapters.  Seeded token ids uniform over the
+    vocabulary, embedded with a random bf16 table; labels are the ids shifted
+    by one.  Device time per step (CUDA events, max over ranks)."""
     import torch
     from fitllm_b200.distributed import LoRAGradComm, barrier, max_over_ranks, microbatch_range
     from fitllm_b200.engine import ShardStationaryEngine, build_synthetic_model
     from fitllm_b200.layer import LayerConfig
+    from fitllm_b200.lm_head import random_lm_head
     from fitllm_b200.optimizer import ShardOptimizer
     cfg = LayerConfig.qwen25_32b()
     sched, store = build_synthetic_model(cfg, layers_n, dev, seed=7)
@@ -288,12 +292,17 @@ def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, st
     opt = ShardOptimizer(store)
     mb0, mb1 = microbatch_range(microbatches, rank, world)
     g = torch.Generator(device=dev).manual_seed(8)
-    h0 = (torch.randn(mb1 - mb0, seq, cfg.hidden, generator=g, device=dev) * 0.02).bfloat16()
-    gout = torch.randn(mb1 - mb0, seq, cfg.hidden, generator=g, device=dev).bfloat16()
+    ids = torch.randint(0, cfg.vocab, (microbatches, seq + 1), generator=g, device=dev)[mb0:mb1]
+    emb = (torch.randn(cfg.vocab, cfg.hidden, generator=g, device=dev) * 0.02).bfloat16()
+    h0 = emb[ids[:, :seq]].contiguous()
+    labels = ids[:, 1:].contiguous()
+    del emb
+    head = random_lm_head(cfg.hidden, cfg.vocab, dev, seed=9)
+    losses = []
 
     def step():
         store.zero_grad()
-        eng.step(h0, gout)
+        losses[:] = eng.step_with_loss(h0, labels, head, microbatches)[0]
         opt.step()
 
     step()
@@ -312,11 +321,17 @@ def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, st
            "value": round(microbatches * seq / (ms / 1000.0), 1), "unit": "tokens/s",
            "ms_per_step": round(ms, 1), "layers": layers_n,
            "model_tflops": round(microbatches * seq * layers_n * flops_per_token(seq) / (ms / 1000.0) / 1e12, 1),
+           "model_tflops_incl_lm_head": round(microbatches * seq * (layers_n * flops_per_token(seq) +
+                                                                    4 * cfg.hidden * cfg.vocab)
+                                              / (ms / 1000.0) / 1e12, 1),
+           "loss": {"mean_ce_rank0_last_step": round(float(torch.stack(losses).mean()), 4),
+                    "note": "random-init model: about ln(152064) = 11.93"},
            "layers_kept_without_recompute": eng.last_kept,
            "h2d_shard_bytes_per_layer_pass_per_rank": int(h2d // layers_n),
            "note": "each layer's shard is uploaded in the forward and again in the backward "
-                   "(two-slot ring)"}
-    del eng, sched, store, opt, h0, gout
+                   "(two-slot ring); model_tflops counts the 64 layers (2.085 PFLOP per step), "
+                   "the lm_head adds 2 GEMMs of 2 x 5120 x 152064 FLOP per token"}
+    del eng, sched, store, opt, h0, labels, head
     torch.cuda.empty_cache()
     return out
 

@@ -60,6 +60,8 @@ SIGNATURES = {
     "fitq_rope": (I32, [P, P, P, P, I64, I32, I32, I64, I32, P]),
     "fitq_swiglu_fwd": (I32, [P, P, P, I64, P]),
     "fitq_swiglu_bwd": (I32, [P, P, P, P, P, I64, P]),
+    "fitq_cross_entropy_workspace": (SZ, [I64]),
+    "fitq_cross_entropy": (I32, [P, P, I64, I64, I64, F32, P, P, SZ, P]),
     "fitq_verify_attention_workspace": (SZ, [I64, I32, I32, I32, I32]),
     "fitq_verify_attention": (I32, [P, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, SZ, P]),
 }

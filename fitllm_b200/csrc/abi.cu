@@ -649,6 +649,30 @@ int fitq_rope(const void* t, void* out, const float* cos_half, const float* sin_
                                          backward, static_cast<cudaStream_t>(stream), sms), "rope");
 }
 
+size_t fitq_cross_entropy_workspace(int64_t rows) {
+  return rows > 0 ? fitq::cross_entropy_workspace(rows) : 0;
+}
+
+int fitq_cross_entropy(void* logits, const int64_t* labels, int64_t rows, int64_t vocab,
+                       int64_t ignore_index, float loss_scale, float* loss_out, void* workspace,
+                       size_t workspace_bytes, fitq_stream_t stream) {
+  if (!logits || !labels || !loss_out || !workspace)
+    return fail(FITQ_ERR_ARG, "cross_entropy: NULL tensor or workspace");
+  if (rows <= 0 || rows >= (1ll << 31) || vocab <= 0 || vocab % 8 != 0)
+    return fail(FITQ_ERR_SHAPE, "cross_entropy: need rows > 0 and vocab %% 8 == 0 (rows=%lld V=%lld)",
+                (long long)rows, (long long)vocab);
+  if (!al16(logits) || (reinterpret_cast<uintptr_t>(labels) & 7) != 0 || !al16(workspace))
+    return fail(FITQ_ERR_ALIGN, "cross_entropy: alignment");
+  if (workspace_bytes < fitq::cross_entropy_workspace(rows))
+    return fail(FITQ_ERR_WORKSPACE, "cross_entropy: workspace %zu < %zu bytes", workspace_bytes,
+                fitq::cross_entropy_workspace(rows));
+  int rc;
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_cross_entropy(logits, labels, rows, vocab, ignore_index, loss_scale,
+                                                  loss_out, workspace, static_cast<cudaStream_t>(stream)),
+                       "cross_entropy");
+}
+
 size_t fitq_verify_attention_workspace(int64_t batch, int heads, int kv_heads, int t_new,
                                        int prefix) {
   (void)heads;

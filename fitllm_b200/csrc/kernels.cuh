@@ -154,6 +154,13 @@ bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slic
 int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
                        cudaStream_t st, int num_sms);
 
+// Cross-entropy of [T, V] bf16 logits, mean over labels != ignore_index; the
+// logits are overwritten with d(loss_scale * loss)/dlogits (ce.cu).
+size_t cross_entropy_workspace(int64_t rows);
+int launch_cross_entropy(void* logits, const int64_t* labels, int64_t T, int64_t V,
+                         int64_t ignore_index, float loss_scale, float* loss_out, void* workspace,
+                         cudaStream_t st);
+
 // Speculative-verify attention over a KV cache (attn.cu): q, out [B, T, H, 128],
 // caches [B, KVH, cap, 128] bf16, (H / KVH) * T <= 32, prefix + T <= cap.
 size_t verify_attention_workspace(int64_t batch, int kv_heads, int len, int num_sms);

@@ -221,6 +221,16 @@ class ShardStationaryEngine:
         acts = self.forward(h)
         return self.backward(acts, grad_out)
 
+    def step_with_loss(self, h: torch.Tensor, labels: torch.Tensor, head, grad_accum: int):
+        """The reference's step (fitllm/trainer.py:495-535): forward over all
+        layers, per micro-batch CE loss of the final norm + lm_head
+        (``head``: lm_head.LMHeadLoss) scaled by 1/grad_accum, backward.
+        Returns (per-micro-batch losses as device scalars, grad w.r.t. h)."""
+        acts = self.forward(h)
+        losses, grad_out = head.loss_and_grad_microbatches(acts[-1], labels, 1.0 / grad_accum)
+        acts[-1] = None  # the last layer's output is only needed by the head
+        return losses, self.backward(acts, grad_out)
+
 
 def _lora_store(cfg: LayerConfig, num_layers: int, dev, seed: int, lora_b_std: float) -> LoRAStore:
     """LoRAStore with PEFT-initialised adapters per layer: A ~ U(-1/sqrt(K),

@@ -205,6 +205,18 @@ FITQ_API int fitq_rope(const void* t, void* out, const float* cos_half, const fl
 FITQ_API int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n,
                              fitq_stream_t stream);
 
+/* Cross-entropy of lm_head logits, forward and backward: loss_out (device
+ * fp32 scalar) = mean over rows with label != ignore_index of
+ * logsumexp(logits[t]) - logits[t, label[t]] (torch CrossEntropyLoss, as
+ * FitLLM applies it per micro-batch: fitllm/backward.py:188-198), and logits
+ * [rows, vocab] bf16 are OVERWRITTEN with d(loss_scale * loss)/dlogits.
+ * labels: int64 [rows]; labels outside [0, vocab) other than ignore_index
+ * contribute nothing.  vocab % 8 == 0. */
+FITQ_API size_t fitq_cross_entropy_workspace(int64_t rows);
+FITQ_API int fitq_cross_entropy(void* logits, const int64_t* labels, int64_t rows, int64_t vocab,
+                                int64_t ignore_index, float loss_scale, float* loss_out,
+                                void* workspace, size_t workspace_bytes, fitq_stream_t stream);
+
 /* Speculative-verify attention over a key/value cache.  Replaces the
  * re-run of the whole prefix that verifies draft tokens (fitllm/inference.py:
  * 380-397, attention inside fitllm/forward.py's layer forward): the T new

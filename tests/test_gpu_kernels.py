@@ -266,3 +266,61 @@ def test_verify_attention(cuda_dev, b, h, kvh, t, prefix, cap):
     assert ops.device_status() == 0
     # deterministic: a second call gives the same bits
     assert torch.equal(out, ops.verify_attention(q, kc, vc, prefix))
+
+
+@pytest.mark.parametrize("rows,vocab,ignored", [(64, 4096, 0), (130, 152064, 7), (33, 1000, 33)])
+def test_cross_entropy(cuda_dev, rows, vocab, ignored):
+    """fitq_cross_entropy against torch's CrossEntropyLoss (mean over labels
+    != -100) on the same bf16 logits: the loss, and the in-place
+    d(scale * loss)/dlogits within 1e-2; a batch with every label ignored
+    gives loss 0 and zero gradient."""
+    from fitllm_b200 import _lib, ops
+    import torch.nn.functional as F
+    g = torch.Generator(device=cuda_dev).manual_seed(rows + vocab)
+    logits = (torch.randn(rows, vocab, generator=g, device=cuda_dev) * 2).bfloat16()
+    labels = torch.randint(0, vocab, (rows,), generator=g, device=cuda_dev)
+    labels[:ignored] = -100
+    ref = logits.float().requires_grad_(True)
+    scale = 0.25
+    L = _lib.load()
+    work = logits.clone()
+    loss = torch.empty((), dtype=torch.float32, device=cuda_dev)
+    nb = L.fitq_cross_entropy_workspace(rows)
+    ws = torch.empty(nb, dtype=torch.uint8, device=cuda_dev)
+    _lib.check(L.fitq_cross_entropy(work.data_ptr(), labels.data_ptr(), rows, vocab, -100, scale,
+                                    loss.data_ptr(), ws.data_ptr(), nb,
+                                    torch.cuda.current_stream().cuda_stream), "fitq_cross_entropy")
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    if ignored == rows:
+        assert float(loss) == 0.0 and not work.float().abs().sum().item()
+        return
+    lref = F.cross_entropy(ref, labels, ignore_index=-100)
+    (lref * scale).backward()
+    assert abs(float(loss) - float(lref.detach())) <= 1e-2 * abs(float(lref.detach()))
+    gref = ref.grad
+    assert float((work.float() - gref).norm() / gref.norm()) < 1e-2
+
+
+def test_lm_head_loss_and_grad(cuda_dev):
+    """Final RMSNorm + lm_head + CE (fitllm_b200/lm_head.py) against an fp32
+    autograd restatement of fitllm/backward.py:188-198: the mean loss of each
+    micro-batch and grad of loss * (1 / grad_accum) w.r.t. h_last, within 1e-2."""
+    import torch.nn.functional as F
+    from fitllm_b200.lm_head import LMHeadLoss
+    g = torch.Generator(device=cuda_dev).manual_seed(77)
+    nmb, s, hid, vocab = 2, 64, 256, 4096
+    h = torch.randn(nmb, s, hid, generator=g, device=cuda_dev).bfloat16()
+    nw = (1 + 0.1 * torch.randn(hid, generator=g, device=cuda_dev)).bfloat16()
+    w = (torch.randn(vocab, hid, generator=g, device=cuda_dev) * 0.05).bfloat16()
+    labels = torch.randint(0, vocab, (nmb, s), generator=g, device=cuda_dev)
+    labels[0, :10] = -100
+    head = LMHeadLoss(nw, w, eps=1e-6)
+    losses, grad = head.loss_and_grad_microbatches(h, labels, loss_scale=1.0 / nmb)
+    for i in range(nmb):
+        x = h[i].float().requires_grad_(True)
+        y = nw.float() * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6))
+        loss = F.cross_entropy(y @ w.float().t(), labels[i], ignore_index=-100)
+        (loss / nmb).backward()
+        assert abs(float(losses[i]) - float(loss.detach())) <= 1e-2 * float(loss.detach())
+        assert float((grad[i].float() - x.grad).norm() / x.grad.norm()) < 1e-2

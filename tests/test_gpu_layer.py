@@ -356,3 +356,63 @@ def test_engine_from_shard_files_matches_in_memory(cuda_dev, tmp_path, group_siz
     first.write_bytes(bytes(raw))
     with pytest.raises(RuntimeError, match="Checksum mismatch"):
         build_model_from_shards(cfg, tmp_path, 3, cuda_dev, group_size=group_size)
+
+
+def test_engine_step_with_lm_head_loss(cuda_dev):
+    """The reference's full step (fitllm/trainer.py:495-535 with
+    fitllm/backward.py:188-198): two layers streamed through the ring, the
+    final norm + lm_head + CE loss of each micro-batch scaled by 1/grad_accum,
+    backward.  Losses, input grad and LoRA grads against the fp32 CPU
+    restatement with autograd, within 1e-2."""
+    import torch.nn.functional as F
+    from fitllm_b200.engine import ShardStationaryEngine, lora_entries
+    from fitllm_b200.layer import DecoderLayer, add_lora_
+    from fitllm_b200.lm_head import LMHeadLoss
+    from fitllm_b200.optimizer import LoRAStore
+    from fitllm_b200.scheduler import ShardScheduler
+    cfg = _cfg()
+    shards, refs = [], []
+    for l in range(2):
+        s, r = _oracle_shard(50 + l)
+        shards.append(s)
+        refs.append(r)
+    sched = ShardScheduler(2, cuda_dev, ring_slots=2)
+    for l in range(2):
+        sched.add_layer(l, shards[l])
+    proto = DecoderLayer(cfg, device=cuda_dev)
+    add_lora_(proto, 16, 32.0, cfg.lora_targets, seed=0)
+    store = LoRAStore(2, lora_entries(proto), cuda_dev)
+    for l in range(2):
+        store.init_layer_(l, {f"self_attn.{n}.lora_{ab}.default.weight": refs[l][f"{n}.lora_{ab}"]
+                              for n in ("q_proj", "v_proj") for ab in ("A", "B")})
+    vocab, nmb, seq = 2048, 2, 64
+    g = torch.Generator().manual_seed(52)
+    h = torch.randn(nmb, seq, SMALL["hidden"], generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(SMALL["hidden"], generator=g)).bfloat16()
+    w = (torch.randn(vocab, SMALL["hidden"], generator=g) * 0.05).bfloat16()
+    labels = torch.randint(0, vocab, (nmb, seq), generator=g)
+    labels[1, -5:] = -100
+    head = LMHeadLoss(nw.to(cuda_dev), w.to(cuda_dev))
+    eng = ShardStationaryEngine(cfg, sched, store, cuda_dev, keep_activations=1)
+    store.zero_grad()
+    losses, gin = eng.step_with_loss(h.to(cuda_dev), labels.to(cuda_dev), head, grad_accum=nmb)
+    params = {l: {k: refs[l][k].clone().requires_grad_(True) for k in refs[l] if "lora_" in k}
+              for l in range(2)}
+    x = h.float().clone().requires_grad_(True)
+    y = x
+    for l in range(2):
+        ww = dict(refs[l])
+        ww.update(params[l])
+        y = layer_ref.layer_forward(ww, y)
+    z = nw.float() * (y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6))
+    ref_losses = [F.cross_entropy(z[i] @ w.float().t(), labels[i], ignore_index=-100) for i in range(nmb)]
+    (sum(ref_losses) / nmb).backward()
+    for i in range(nmb):
+        assert abs(float(losses[i]) - float(ref_losses[i].detach())) <= 1e-2 * float(ref_losses[i].detach())
+    assert onf4.rel_err(gin.float().cpu().numpy(), x.grad.numpy()) < REL
+    for l in range(2):
+        gv = store.views(store.grad, l)
+        for n in ("q_proj", "v_proj"):
+            for ab in ("A", "B"):
+                got = gv[f"self_attn.{n}.lora_{ab}.default.weight"].cpu().numpy()
+                assert onf4.rel_err(got, params[l][f"{n}.lora_{ab}"].grad.numpy()) < REL
