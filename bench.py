@@ -73,17 +73,24 @@ def flops_per_token(seq: int) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons around the timed region.
+
+    Started before the warm-up and awaited until it writes its first sample,
+    so that short timed regions (a few tens of ms at 8 GPUs) still see the
+    GPU; samples are selected by their timestamps: those inside the timed
+    window, else the last one before and the first one after it (the GPU is
+    under the same load in the warm-up just before)."""
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
-    def start(self):
+    def start(self, wait_s: float = 5.0):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
@@ -92,10 +99,29 @@ class ClockSampler:
                  "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t_end = time.time() + wait_s
+        while time.time() < t_end and os.path.getsize(self.path) == 0:
+            time.sleep(0.02)
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    @staticmethod
+    def _ts(field: str):
+        import datetime
+        try:
+            return datetime.datetime.strptime(field.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)  # one more sample after the window
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -104,20 +130,29 @@ class ClockSampler:
         rows = []
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) >= 9:
-                rows.append(f)
+            if len(f) >= 10:
+                rows.append((self._ts(f[0]), f[1:]))
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        inside = [r for t, r in rows if t is not None and self.t0 is not None and self.t0 <= t <= self.t1]
+        sel, where = inside, "inside the timed region"
+        if not sel:
+            before = [r for t, r in rows if t is not None and self.t0 is not None and t < self.t0]
+            after = [r for t, r in rows if t is not None and self.t1 is not None and t > self.t1]
+            sel = before[-1:] + after[:1]
+            where = "nearest before and after the timed region (shorter than the sampling period)"
+        if not sel:
+            sel, where = [r for _, r in rows], "whole run"
+        sm = [float(r[1]) for r in sel if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in sel if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in sel if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        load = [s for s, p in zip(sm, pw) if p > 200] or sm
+        reasons = sorted({names[i] for r in sel for i in range(4) if r[5 + i].lower() == "active"})
+        load = [v for v, w in zip(sm, pw) if w > 200] or sm
         return {"sm_mhz": statistics.median(load) if load else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(pw) if pw else None}
+                "samples": len(sel), "samples_from": where, "power_w_max": max(pw) if pw else None}
 
 
 def cpu_baseline(a, seq):
@@ -446,26 +481,28 @@ def main():
         eng.step(h0, gout)
         opt.step()
 
+    clocks = ClockSampler(local)
+    clocks.start()  # running through the warm-up, so a short timed region still has samples
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
     if _lib.load().fitq_get_device_status(1, None) != 0:
         raise RuntimeError("device status error after warm-up")
 
-    clocks = ClockSampler(local)
     L.fitq_timing_enable(4096)
     barrier()
     torch.cuda.synchronize()
-    clocks.start()
     launches0 = L.fitq_launch_count()
     s_ev = torch.cuda.Event(enable_timing=True)
     e_ev = torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
     s_ev.record()
     for _ in range(a.steps):
         step()
     e_ev.record()
     launches = L.fitq_launch_count() - launches0
     torch.cuda.synchronize()
+    clocks.mark_end()
     barrier()
     clk = clocks.stop()
     ms_local = s_ev.elapsed_time(e_ev) / a.steps
