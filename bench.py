@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--cpu-seq", type=int, default=2048)
     ap.add_argument("--gemv-case", default=None,
                     help="N,K,M[,R]: run one NF4 GEMV shape and exit (a profiling target)")
+    ap.add_argument("--attn-case", default=None,
+                    help="B,H,KVH,T,prefix: run the verify attention on one shape and exit")
+    ap.add_argument("--ce-case", default=None,
+                    help="rows,vocab: run the cross-entropy kernel on one shape and exit")
     ap.add_argument("--full-step", choices=["auto", "on", "off"], default="auto",
                     help="also time a full 64-layer step with shards streamed from pinned host "
                          "memory (auto: on one GPU only; every rank builds the 64-layer host store)")
@@ -400,6 +404,64 @@ def gemv_case(dev, spec):
     return {"gemv_case": spec, "us_per_call": round(s_ev.elapsed_time(e_ev) * 1000.0 / 20, 2)}
 
 
+def attn_case(dev, spec):
+    """One verify-attention shape on its own ("B,H,KVH,T,prefix"): caches of
+    prefix + T positions, three warm calls then 20 timed (a profiling target)."""
+    import torch
+    from fitllm_b200 import ops
+    b, h, kvh, t, prefix = map(int, spec.split(","))
+    g = torch.Generator(device=dev).manual_seed(13)
+    q = torch.randn(b, t, h, 128, generator=g, device=dev).bfloat16()
+    kc = torch.randn(b, kvh, prefix + t, 128, generator=g, device=dev).bfloat16()
+    vc = torch.randn(b, kvh, prefix + t, 128, generator=g, device=dev).bfloat16()
+    for _ in range(3):
+        ops.verify_attention(q, kc, vc, prefix)
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(20):
+        ops.verify_attention(q, kc, vc, prefix)
+    e_ev.record()
+    torch.cuda.synchronize()
+    us = s_ev.elapsed_time(e_ev) * 1000.0 / 20
+    kv = 2 * kc.numel() * 2
+    return {"attn_case": spec, "us_per_call": round(us, 2), "kv_bytes": kv,
+            "kv_GB/s": round(kv / us / 1e3, 1)}
+
+
+def ce_case(dev, spec):
+    """fitq_cross_entropy on its own ("rows,vocab"): bf16 logits, three warm
+    calls then 20 timed on fresh copies (a profiling target)."""
+    import torch
+    from fitllm_b200 import _lib, ops
+    rows, vocab = map(int, spec.split(","))
+    g = torch.Generator(device=dev).manual_seed(14)
+    logits = (torch.randn(rows, vocab, generator=g, device=dev) * 2).bfloat16()
+    labels = torch.randint(0, vocab, (rows,), generator=g, device=dev)
+    L = _lib.load()
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    nb = L.fitq_cross_entropy_workspace(rows)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    work = logits.clone()
+
+    def call():
+        _lib.check(L.fitq_cross_entropy(work.data_ptr(), labels.data_ptr(), rows, vocab, -100, 1.0,
+                                        loss.data_ptr(), ws.data_ptr(), nb, ops._stream(dev)),
+                   "fitq_cross_entropy")
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(20):
+        call()  # gradients of gradients after the first call: same traffic and work
+    e_ev.record()
+    torch.cuda.synchronize()
+    us = s_ev.elapsed_time(e_ev) * 1000.0 / 20
+    return {"ce_case": spec, "us_per_call": round(us, 2),
+            "GB/s_algorithmic": round(3 * logits.numel() * 2 / us / 1e3, 1)}
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -449,10 +511,11 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     L = _lib.load()
-    if a.gemv_case:
-        if rank == 0:
-            print(json.dumps(gemv_case(dev, a.gemv_case)), flush=True)
-        return
+    for case, fn in ((a.gemv_case, gemv_case), (a.attn_case, attn_case), (a.ce_case, ce_case)):
+        if case:
+            if rank == 0:
+                print(json.dumps(fn(dev, case)), flush=True)
+            return
 
     cfg = LayerConfig.qwen25_32b()
     sched, store = build_synthetic_model(cfg, 1, dev, seed=0)

@@ -318,13 +318,40 @@ __global__ void __launch_bounds__(kAttD)
       __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
 }
 
+// CTAs of verify_attn_kernel resident per SM (shared memory bound: 2 on B200).
+int att_ctas_per_sm() {
+  static int n = 0;
+  if (n == 0) {
+    int v = 0;
+    if (cudaFuncSetAttribute(verify_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kAttSmem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, verify_attn_kernel, kAttThreads, kAttSmem) !=
+            cudaSuccess ||
+        v < 1)
+      v = 1;
+    n = v;
+  }
+  return n;
+}
+
+// KV splits per (batch, KV head): minimise waves x (tiles per CTA + 1), the +1
+// standing for a CTA's fixed cost (Q load, partial write, its share of the
+// combine).  A split count whose last wave is nearly empty costs a whole wave.
 int att_splits(int64_t batch, int kv_heads, int len, int num_sms) {
   const int tiles = (len + kAttTile - 1) / kAttTile;
   const int64_t pairs = batch * kv_heads;
-  int64_t s = (2 * static_cast<int64_t>(num_sms) + pairs - 1) / pairs;
-  if (s > tiles) s = tiles;
-  if (s < 1) s = 1;
-  return static_cast<int>(s);
+  const int64_t slots = static_cast<int64_t>(num_sms) * att_ctas_per_sm();
+  int best = 1;
+  int64_t best_cost = -1;
+  for (int s = 1; s <= tiles; ++s) {
+    const int64_t waves = (pairs * s + slots - 1) / slots;
+    const int64_t cost = waves * ((tiles + s - 1) / s + 1);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 }  // namespace
