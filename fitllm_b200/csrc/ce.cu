@@ -24,7 +24,10 @@
 namespace fitq {
 namespace {
 
-constexpr int kCeThreads = 512;
+// 1024 threads: two CTAs (rows) per SM keep ~300 rows in flight, 90 MB at
+// V = 152,064, so the second read of a row still finds it in L2 (at four rows
+// per SM a third of the second reads went to DRAM).
+constexpr int kCeThreads = 1024;
 
 __device__ __forceinline__ void block_reduce_max_sum(float& m, float& s, float* sh_m, float* sh_s) {
   // warp: combine (m, s) pairs
