@@ -297,7 +297,8 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   if (m <= 0 || m >= (1ll << 31)) return fail(FITQ_ERR_SHAPE, "qlora_fwd: bad M=%lld", (long long)m);
   if (!valid_rank(rank)) return fail(FITQ_ERR_UNSUPPORTED, "qlora_fwd: rank %d not in {0,16,32,48,64}", rank);
   if (rank > 0 && (!lora_a || !lora_b)) return fail(FITQ_ERR_ARG, "qlora_fwd: lora_a/lora_b required for rank > 0");
-  if (rank > 0 && !al16(lora_b)) return fail(FITQ_ERR_ALIGN, "qlora_fwd: lora_b must be 16-byte aligned");
+  if (rank > 0 && (!al16(lora_a) || !al16(lora_b)))
+    return fail(FITQ_ERR_ALIGN, "qlora_fwd: lora_a / lora_b must be 16-byte aligned");
   if (a.n_out % 16 != 0) return fail(FITQ_ERR_SHAPE, "qlora_fwd: N=%lld not a multiple of 16", (long long)a.n_out);
   if (!al16(x) || !al16(y) || (y_add && !al16(y_add)) || (t_out && !al16(t_out)) ||
       (bias && !al16(bias)))
