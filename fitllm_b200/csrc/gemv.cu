@@ -342,8 +342,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
 
   // Shared layout: [slack below the 64 KB boundary][table 64 KB][rest].  Ring
-  // stages fill the slack first, then the rest; the reduction area, the
-  // per-warp scale areas and the round's tile flags follow.
+  // stages fill the slack first, then the rest; the reduction area and the
+  // per-warp scale areas follow.
   const uint32_t sbase = smem_u32(g_gemv_smem);
   const uint32_t tbl = (sbase + 0xFFFFu) & ~0xFFFFu;
   const int n_slack = static_cast<int>((tbl - sbase) / kDecStage);
@@ -354,35 +354,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   float4* const red = reinterpret_cast<float4*>(g_gemv_smem + (red_addr - sbase));
   const int red_warp = 8 * qn;  // float4 slots per warp and tile
   const uint32_t sc_addr = red_addr + static_cast<uint32_t>(R * kWarps * 8 * 4 * 16);  // 256 B per warp
-
-  // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g;
-  // two threads per entry, 16-byte stores
-  {
-    uint4* table = reinterpret_cast<uint4*>(g_gemv_smem + (tbl - sbase));
-    const int e = threadIdx.x >> 1, h = threadIdx.x & 1;
-    const uint32_t v = pack_bf16x2(__ldg(w.quant_map + (e >> 4)), __ldg(w.quant_map + (e & 15)));
-    const uint4 vv = make_uint4(v, v, v, v);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) table[e * 16 + h * 4 + i] = vv;
-    if (NESTED) {
-      const uint32_t nv = __float_as_uint(__ldg(w.nested_quant_map + e));
-      table[e * 16 + 8 + h] = make_uint4(nv, nv, nv, nv);
-    }
-  }
-
-  uint4 xr[kDecKB][2];
-#pragma unroll
-  for (int c = 0; c < kDecKB; ++c) {
-    if (g < M) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(g) * K +
-                                                        (b0 + c) * 64 + 16 * q);
-      xr[c][0] = __ldg(src);
-      xr[c][1] = __ldg(src + 1);
-    } else {
-      xr[c][0] = make_uint4(0, 0, 0, 0);
-      xr[c][1] = make_uint4(0, 0, 0, 0);
-    }
-  }
 
   // ring stages of this warp
   uint32_t stage[R];
@@ -416,8 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sc_w = sc_addr + static_cast<uint32_t>(warp) * 256u;
   const uint32_t sc_lane = sc_w + static_cast<uint32_t>(g * 16 + 4 * q);
   const uint64_t pol = evict_first_policy();
-  __syncthreads();  // table ready
 
+  // The first tiles' copies go out before the table fill and the x loads, so
+  // their latency overlaps that setup.
   ScaleBuf<NESTED> sb[R];
 #pragma unroll
   for (int d = 0; d < D; ++d) {
@@ -431,6 +403,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     f_next += fstep;
     src += src_step;
   }
+  // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g;
+  // two threads per entry, 16-byte stores
+  {
+    uint4* table = reinterpret_cast<uint4*>(g_gemv_smem + (tbl - sbase));
+    const int e = threadIdx.x >> 1, h = threadIdx.x & 1;
+    const uint32_t v = pack_bf16x2(__ldg(w.quant_map + (e >> 4)), __ldg(w.quant_map + (e & 15)));
+    const uint4 vv = make_uint4(v, v, v, v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) table[e * 16 + h * 4 + i] = vv;
+    if (NESTED) {
+      const uint32_t nv = __float_as_uint(__ldg(w.nested_quant_map + e));
+      table[e * 16 + 8 + h] = make_uint4(nv, nv, nv, nv);
+    }
+  }
+
+  uint4 xr[kDecKB][2];
+#pragma unroll
+  for (int c = 0; c < kDecKB; ++c) {
+    if (g < M) {
+      const uint4* xs = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(g) * K +
+                                                       (b0 + c) * 64 + 16 * q);
+      xr[c][0] = __ldg(xs);
+      xr[c][1] = __ldg(xs + 1);
+    } else {
+      xr[c][0] = make_uint4(0, 0, 0, 0);
+      xr[c][1] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  __syncthreads();  // table ready
+
   for (int rd = 0; rd < rounds; ++rd) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {

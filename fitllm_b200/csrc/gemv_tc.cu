@@ -220,9 +220,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  // The producer needs neither the table nor TMEM: it starts streaming now and
+  // the other warps wait for both on a named barrier of their own.
+  if (warp != 0) {
+    tc_fence_before();
+    asm volatile("bar.sync 1, %0;" ::"n"(kTcThreads - 32) : "memory");
+    tc_fence_after();
+  }
   const uint32_t tmem_base = tmem_slot;
   const uint32_t idesc = umma_idesc_bf16_f32(kTcRows, NTOK);
   constexpr int kXTile = NTOK * 128;  // one 64-column x tile, 128-byte swizzled
