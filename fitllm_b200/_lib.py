@@ -34,6 +34,17 @@ class Nf4WeightC(ctypes.Structure):
 
 WP = ctypes.POINTER(Nf4WeightC)
 
+
+class GemvJobC(ctypes.Structure):
+    """struct fitq_gemv_job"""
+    _fields_ = [
+        ("w", WP), ("lora_a", P), ("lora_b", P), ("rank", I32), ("scale", F32), ("bias", P),
+        ("y", P), ("y_add", P),
+    ]
+
+
+JP = ctypes.POINTER(GemvJobC)
+
 SIGNATURES = {
     "fitq_version": (ctypes.c_char_p, []),
     "fitq_last_error": (ctypes.c_char_p, []),
@@ -60,6 +71,8 @@ SIGNATURES = {
     "fitq_rope": (I32, [P, P, P, P, I64, I32, I32, I64, I32, P]),
     "fitq_swiglu_fwd": (I32, [P, P, P, I64, P]),
     "fitq_swiglu_bwd": (I32, [P, P, P, P, P, I64, P]),
+    "fitq_nf4_gemv_grouped_workspace": (SZ, [JP, I32, I64]),
+    "fitq_nf4_gemv_grouped": (I32, [JP, I32, P, I64, P, SZ, P]),
     "fitq_cross_entropy_workspace": (SZ, [I64]),
     "fitq_cross_entropy": (I32, [P, P, I64, I64, I64, F32, P, P, SZ, P]),
     "fitq_verify_attention_workspace": (SZ, [I64, I32, I32, I32, I32]),

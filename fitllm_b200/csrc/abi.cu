@@ -390,6 +390,104 @@ int fitq_nf4_gemv(const fitq_nf4_weight* w, const void* x, int64_t m, const floa
                         workspace_bytes, stream, 1);
 }
 
+// Grouped GEMV: the single tcgen05 launch applies when every job shares K and
+// the scale format, N % 128 == 0 and the tcgen05 plan takes M for the summed N.
+static bool grouped_tc(const fitq_gemv_job* jobs, int count, int64_t m, int sms, int* slices) {
+  if (count < 1 || count > 3) return false;
+  const fitq_nf4_weight* w0 = jobs[0].w;
+  if (!w0) return false;
+  const bool nested = w0->absmax_f32 == nullptr;
+  int64_t n_total = 0;
+  for (int g = 0; g < count; ++g) {
+    const fitq_nf4_weight* w = jobs[g].w;
+    if (!w || w->k_in != w0->k_in || (w->absmax_f32 == nullptr) != nested || w->n_out % 128 != 0)
+      return false;
+    n_total += w->n_out;
+  }
+  return fitq::gemv_tc_plan(m, n_total, w0->k_in, sms, slices);
+}
+
+static size_t grouped_bytes(const fitq_gemv_job* jobs, int count, int64_t m, int slices) {
+  Carve c{nullptr, 0};
+  for (int g = 0; g < count; ++g) {
+    c.take(static_cast<size_t>(slices) * m * jobs[g].w->n_out * sizeof(float));
+    if (jobs[g].rank > 0) c.take(fitq::lora_t_workspace(m, jobs[g].w->k_in, jobs[g].rank));
+  }
+  return c.used;
+}
+
+size_t fitq_nf4_gemv_grouped_workspace(const fitq_gemv_job* jobs, int count, int64_t m) {
+  if (!jobs || count < 1) return 0;
+  const int sms = sms_for_sizing();
+  int slices = 0;
+  if (grouped_tc(jobs, count, m, sms, &slices)) return grouped_bytes(jobs, count, m, slices);
+  size_t need = 0;
+  for (int g = 0; g < count; ++g) {
+    if (!jobs[g].w) return 0;
+    const size_t b = fitq_nf4_gemv_workspace(m, jobs[g].w->n_out, jobs[g].w->k_in, jobs[g].rank);
+    need = b > need ? b : need;
+  }
+  return need;
+}
+
+int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, int64_t m,
+                          void* workspace, size_t workspace_bytes, fitq_stream_t stream) {
+  if (!jobs || count < 1 || count > 3) return fail(FITQ_ERR_ARG, "nf4_gemv_grouped: 1 to 3 jobs");
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms) return rc;
+  int slices = 0;
+  if (!grouped_tc(jobs, count, m, sms, &slices)) {
+    for (int g = 0; g < count; ++g) {
+      const fitq_gemv_job& j = jobs[g];
+      rc = fitq_nf4_gemv(j.w, x, m, j.lora_a, j.lora_b, j.rank, j.scale, j.bias, j.y, j.y_add,
+                         workspace, workspace_bytes, stream);
+      if (rc) return rc;
+    }
+    return FITQ_OK;
+  }
+  // the checks of fitq_nf4_gemv, per job
+  fitq::Nf4Args a[3];
+  for (int g = 0; g < count; ++g) {
+    const fitq_gemv_job& j = jobs[g];
+    if ((rc = check_weight(j.w, &a[g]))) return rc;
+    if (!x || !j.y) return fail(FITQ_ERR_ARG, "nf4_gemv_grouped: x and y are required");
+    if (!valid_rank(j.rank)) return fail(FITQ_ERR_UNSUPPORTED, "nf4_gemv_grouped: rank %d", j.rank);
+    if (j.rank > 0 && (!j.lora_a || !j.lora_b || !al16(j.lora_a) || !al16(j.lora_b)))
+      return fail(FITQ_ERR_ALIGN, "nf4_gemv_grouped: lora_a / lora_b required, 16-byte aligned");
+    if (!al16(x) || !al16(j.y) || (j.y_add && !al16(j.y_add)) || (j.bias && !al16(j.bias)))
+      return fail(FITQ_ERR_ALIGN, "nf4_gemv_grouped: x/y/bias/y_add must be 16-byte aligned");
+  }
+  const size_t need = grouped_bytes(jobs, count, m, slices);
+  if (workspace_bytes < need || !workspace)
+    return fail(FITQ_ERR_WORKSPACE, "nf4_gemv_grouped: workspace %zu < %zu bytes", workspace_bytes, need);
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  float* partial[3] = {nullptr, nullptr, nullptr};
+  float* t_part[3] = {nullptr, nullptr, nullptr};
+  for (int g = 0; g < count; ++g) {
+    partial[g] = static_cast<float*>(c.take(static_cast<size_t>(slices) * m * a[g].n_out * sizeof(float)));
+    if (jobs[g].rank > 0)
+      t_part[g] = static_cast<float*>(c.take(fitq::lora_t_workspace(m, a[g].k_in, jobs[g].rank)));
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t K = a[0].k_in;
+  rc = fitq::launch_nf4_gemv_tc_grouped(a, count, x, m, partial, status_ptr(), st, sms);
+  if (rc) return launch_status(rc, "nf4_gemv_grouped tcgen05");
+  for (int g = 0; g < count; ++g) {
+    const fitq_gemv_job& j = jobs[g];
+    if (j.rank > 0 && (rc = fitq::launch_lora_t(x, m, K, j.lora_a, j.rank, t_part[g], st)))
+      return launch_status(rc, "lora T = x.A^T");
+  }
+  for (int g = 0; g < count; ++g) {
+    const fitq_gemv_job& j = jobs[g];
+    fitq::GemvEpilogue ep{j.y, j.y_add, j.bias, j.lora_b, t_part[g], fitq::lora_t_groups(K), nullptr,
+                          j.rank, j.scale, partial[g]};
+    rc = fitq::launch_nf4_gemv_dec_finish(m, a[g].n_out, slices, ep, st, sms);
+    if (rc) return launch_status(rc, "nf4_gemv_grouped finish");
+  }
+  return FITQ_OK;
+}
+
 size_t fitq_qlora_bwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank) {
   Carve c{nullptr, 0};
   BwdPlan p;

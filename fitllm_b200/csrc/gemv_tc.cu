@@ -37,7 +37,10 @@
 //               each drains NTOK / 4 columns of the four accumulators and
 //               writes their sum as the fp32 partials.
 // Work items are (128-row tile, K slice) pairs, walked by the CTAs with a grid
-// stride.  Every mbarrier wait is bounded (common.cuh); no multicast.
+// stride.  One launch may cover up to three weights that share K and x (q, k
+// and v, or gate and up): the tiles of all of them form one item list, each
+// with its own tensor map, scales and partial-sum buffer, so small weights
+// (k, v: 8 tiles each) share the SMs instead of each splitting K many ways.  Every mbarrier wait is bounded (common.cuh); no multicast.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -59,17 +62,29 @@ constexpr int kTcMaxABufs = 3;          // A buffers (128 columns each), then th
 __host__ __device__ constexpr int tc_abufs(int ntok) { return ntok <= 32 ? 3 : 2; }
 __host__ __device__ constexpr int tc_acc_stride(int ntok) { return ntok <= 32 ? 32 : 64; }
 
+constexpr int kTcMaxGroups = 3;
+
 struct TcParams {
-  Nf4Args w;
+  Nf4Args w[kTcMaxGroups];          // weights of the launch (same K, same scale format)
+  float* partial[kTcMaxGroups];     // [slices, M, N_g] each
+  int tile_end[kTcMaxGroups];       // exclusive prefix sums of the groups' tiles
+  int groups;
   int M;
-  int tiles;        // N / 128
+  int tiles;        // total tiles of all groups
   int slices, bps;  // K slices, 64-column blocks per slice (multiple of 4)
   int items;        // tiles * slices
   int nst;          // ring stages
   int xbytes;       // x bytes of one stage (4 * NTOK * 128)
-  float* partial;   // [slices, M, N]
   int* status;
 };
+
+// Group of a (global) tile index and its first tile.
+__device__ __forceinline__ int tc_group(const TcParams& p, int t) {
+  return t < p.tile_end[0] ? 0 : t < p.tile_end[1] ? 1 : 2;
+}
+__device__ __forceinline__ int tc_group_start(const TcParams& p, int g) {
+  return g == 0 ? 0 : g == 1 ? p.tile_end[0] : p.tile_end[1];
+}
 
 extern __shared__ __align__(1024) uint8_t g_tc_smem[];
 
@@ -140,7 +155,9 @@ __device__ __forceinline__ uint4 lds128u(uint32_t addr) {
 
 template <int NTOK, bool NESTED>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    nf4_gemv_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+    nf4_gemv_tc_kernel(const __grid_constant__ CUtensorMap tm_w0,
+                       const __grid_constant__ CUtensorMap tm_w1,
+                       const __grid_constant__ CUtensorMap tm_w2,
                        const __grid_constant__ CUtensorMap tm_x, const TcParams p) {
   __shared__ uint64_t bars[3 * kTcMaxSt + 2 * kTcMaxABufs + 3];
   __shared__ uint32_t slot_s[2 * kTcMaxSt];  // W slot of stage s at [s], x slot at [kTcMaxSt + s]
@@ -159,7 +176,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   volatile int* abort_flag = &abort_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int K = static_cast<int>(p.w.k_in), N = static_cast<int>(p.w.n_out);
+  const int K = static_cast<int>(p.w[0].k_in);
   const int nblk = K / 64;
   const int nst = p.nst, kst = p.bps / 4;
 
@@ -210,14 +227,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int kFill = kTcThreads - 32 * kTcDecWarp0;
     for (int i = threadIdx.x - 32 * kTcDecWarp0; i < 512; i += kFill) {
       const int e = i >> 1, h = i & 1;
-      const uint32_t v = pack_bf16x2(__ldg(p.w.quant_map + (e >> 4)), __ldg(p.w.quant_map + (e & 15)));
+      const float qa = __ldg(p.w[0].quant_map + (e >> 4)), qb = __ldg(p.w[0].quant_map + (e & 15));
+      const uint32_t v = pack_bf16x2(qa, qb);
       const uint4 vv = make_uint4(v, v, v, v);
 #pragma unroll
       for (int j = 0; j < 4; ++j) table[e * 16 + h * 4 + j] = vv;
       if (NESTED) {
-        const uint32_t nv = __float_as_uint(__ldg(p.w.nested_quant_map + e));
+        const uint32_t nv = __float_as_uint(__ldg(p.w[0].nested_quant_map + e));
         table[e * 16 + 8 + h] = make_uint4(nv, nv, nv, nv);
       }
+    }
+    // One code table serves every group: the groups' maps must hold the same values.
+    const int i = threadIdx.x - 32 * kTcDecWarp0;
+    for (int g = 1; g < p.groups; ++g) {
+      bool same = true;
+      if (i < 16) same = __ldg(p.w[g].quant_map + i) == __ldg(p.w[0].quant_map + i);
+      if (NESTED && i < 256)
+        same = same && __ldg(p.w[g].nested_quant_map + i) == __ldg(p.w[0].nested_quant_map + i);
+      if (!same) report_device_error(p.status, FITQ_ERR_UNSUPPORTED);
     }
   }
   // The producer needs neither the table nor TMEM: it starts streaming now and
@@ -234,14 +261,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tm_w);
+      tma_prefetch_desc(&tm_w0);
+      if (p.groups > 1) tma_prefetch_desc(&tm_w1);
+      if (p.groups > 2) tma_prefetch_desc(&tm_w2);
       tma_prefetch_desc(&tm_x);
       int st = 0;
       uint32_t ph = 0;
       uint32_t armed = 0, armed_parity = 0;  // per-stage bit: armed / parity of the last arm
       bool ok = true;
       for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
-        const int t = it / p.slices, sl = it % p.slices;
+        const int tg = it / p.slices, sl = it % p.slices;
+        const int g = tc_group(p, tg), t = tg - tc_group_start(p, g);
+        const CUtensorMap* tm_w = g == 0 ? &tm_w0 : g == 1 ? &tm_w1 : &tm_w2;
         const int kb0 = sl * p.bps;
         for (int ks = 0; ks < kst; ++ks) {
           if (!mbar_wait(&wfree[st], ph ^ 1, abort_flag, p.status) ||
@@ -254,7 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           armed_parity = (armed_parity & ~(1u << st)) | (ph << st);
           const int kb = kb0 + 4 * ks;
           // packed bytes: x = byte column kb * 32 (a multiple of 128), y = first row of the tile
-          tma_load_2d(g_tc_smem + (slot_s[st] - sbase), &tm_w, &full[st], kb * 32, t * kTcRows);
+          tma_load_2d(g_tc_smem + (slot_s[st] - sbase), tm_w, &full[st], kb * 32, t * kTcRows);
           uint8_t* xd = g_tc_smem + (slot_s[kTcMaxSt + st] - sbase);
 #pragma unroll
           for (int b = 0; b < 4; ++b) tma_load_2d(xd + b * kXTile, &tm_x, &full[st], (kb + b) * 64, 0);
@@ -322,8 +353,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t wph = 0, aph = 0, accph = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < p.items && ok; it += gridDim.x) {
-      const int t = it / p.slices, sl = it % p.slices;
+      const int tg = it / p.slices, sl = it % p.slices;
+      const int g = tc_group(p, tg), t = tg - tc_group_start(p, g);
       const int row = t * kTcRows + r;
+      const int N = static_cast<int>(g == 0 ? p.w[0].n_out : g == 1 ? p.w[1].n_out : p.w[2].n_out);
+      const uint8_t* acode = g == 0 ? p.w[0].absmax_code : g == 1 ? p.w[1].absmax_code : p.w[2].absmax_code;
+      const float* nabs = g == 0 ? p.w[0].nested_absmax : g == 1 ? p.w[1].nested_absmax : p.w[2].nested_absmax;
+      const float* af32 = g == 0 ? p.w[0].absmax_f32 : g == 1 ? p.w[1].absmax_f32 : p.w[2].absmax_f32;
+      const float offset = g == 0 ? p.w[0].offset : g == 1 ? p.w[1].offset : p.w[2].offset;
+      float* const part = g == 0 ? p.partial[0] : g == 1 ? p.partial[1] : p.partial[2];
       // Scales, fetched three stages ahead: the 32-bit word j of absmax codes
       // covers blocks 4j..4j+3 of the slice (stage j; one 256-block nested
       // group since 4 | 256), this warp's block is byte d.
@@ -333,10 +371,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       auto fetch = [&](int j, uint32_t& c, float& n) {
         if (j >= kst) return;
         if (NESTED) {
-          c = __ldg(reinterpret_cast<const uint32_t*>(p.w.absmax_code + rb) + j);
-          n = __ldg(p.w.nested_absmax + ((rb + 4 * j) >> 8));
+          c = __ldg(reinterpret_cast<const uint32_t*>(acode + rb) + j);
+          n = __ldg(nabs + ((rb + 4 * j) >> 8));
         } else {
-          n = __ldg(p.w.absmax_f32 + rb + 4 * j + d);
+          n = __ldg(af32 + rb + 4 * j + d);
         }
       };
       fetch(0, c0, n0);
@@ -348,7 +386,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           uint32_t ca, nv;
           asm("prmt.b32 %0, %1, %2, %3;" : "=r"(ca) : "r"(c0), "r"(nq), "r"(csel));
           asm volatile("ld.shared.u32 %0, [%1];" : "=r"(nv) : "r"(ca));
-          am = __fadd_rn(__fmul_rn(__uint_as_float(nv), n0), p.w.offset);
+          am = __fadd_rn(__fmul_rn(__uint_as_float(nv), n0), offset);
         } else {
           am = n0;
         }
@@ -405,7 +443,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty);
       accph ^= 1;
-      float* out = p.partial + static_cast<int64_t>(sl) * p.M * N + row;
+      float* out = part + static_cast<int64_t>(sl) * p.M * N + row;
 #pragma unroll
       for (int j = 0; j < kQ; ++j) {
         const int tk = d * kQ + j;
@@ -469,32 +507,50 @@ bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slic
   return true;
 }
 
-int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
-                       cudaStream_t st, int num_sms) {
-  const TcPlan pl = make_tc_plan(m, w.n_out, w.k_in, num_sms);
+int launch_nf4_gemv_tc_grouped(const Nf4Args* w, int groups, const void* x, int64_t m,
+                               float* const* partial, int* status, cudaStream_t st, int num_sms) {
+  if (groups < 1 || groups > kTcMaxGroups) return FITQ_ERR_UNSUPPORTED;
+  const bool nested = w[0].absmax_f32 == nullptr;
+  int64_t n_total = 0;
+  for (int g = 0; g < groups; ++g) {
+    if (w[g].k_in != w[0].k_in || w[g].n_out % kTcRows != 0 || (w[g].absmax_f32 == nullptr) != nested)
+      return FITQ_ERR_UNSUPPORTED;
+    if (nested && (reinterpret_cast<uintptr_t>(w[g].absmax_code) & 3) != 0) return FITQ_ERR_ALIGN;
+    if ((reinterpret_cast<uintptr_t>(w[g].packed) & 15) != 0) return FITQ_ERR_ALIGN;  // TMA source
+    n_total += w[g].n_out;
+  }
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return FITQ_ERR_ALIGN;  // TMA source
+  const int64_t K = w[0].k_in;
+  const TcPlan pl = make_tc_plan(m, n_total, K, num_sms);
   if (pl.slices == 0) return FITQ_ERR_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(w.absmax_code) & 3) != 0) return FITQ_ERR_ALIGN;  // word reads
-  if (((reinterpret_cast<uintptr_t>(w.packed) | reinterpret_cast<uintptr_t>(x)) & 15) != 0)
-    return FITQ_ERR_ALIGN;  // TMA sources
-  CUtensorMap tm_w, tm_x;
-  if (!encode_tmap_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.k_in / 2, w.n_out, w.k_in / 2,
-                      128u, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
-      !encode_tmap_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, w.k_in, m, w.k_in * 2, 64u,
+  CUtensorMap tm_w[kTcMaxGroups], tm_x;
+  for (int g = 0; g < groups; ++g)
+    if (!encode_tmap_2d(&tm_w[g], CU_TENSOR_MAP_DATA_TYPE_UINT8, w[g].packed, K / 2, w[g].n_out, K / 2,
+                        128u, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+      return FITQ_ERR_CUDA;
+  for (int g = groups; g < kTcMaxGroups; ++g) tm_w[g] = tm_w[0];
+  if (!encode_tmap_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, m, K * 2, 64u,
                       static_cast<uint32_t>(pl.ntok), CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
     return FITQ_ERR_CUDA;
   TcParams p;
-  p.w = w;
+  int end = 0;
+  for (int g = 0; g < kTcMaxGroups; ++g) {
+    const int gg = g < groups ? g : 0;
+    p.w[g] = w[gg];
+    p.partial[g] = partial[gg];
+    if (g < groups) end += static_cast<int>(w[g].n_out / kTcRows);
+    p.tile_end[g] = end;
+  }
+  p.groups = groups;
   p.M = static_cast<int>(m);
-  p.tiles = static_cast<int>(w.n_out / kTcRows);
+  p.tiles = end;
   p.slices = pl.slices;
   p.bps = pl.bps;
   p.items = pl.items;
   p.nst = pl.nst;
   p.xbytes = pl.xbytes;
-  p.partial = partial;
   p.status = status;
-  const bool nested = w.absmax_f32 == nullptr;
   cudaError_t e = cudaSuccess;
 #define FITQ_TC_CASE(NT)                                                                        \
   if (pl.ntok == NT) {                                                                          \
@@ -506,7 +562,7 @@ int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partia
       attr[nested] = true;                                                                      \
     }                                                                                           \
     e = launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(kTcThreads), kTcSmem, st,     \
-                   tm_w, tm_x, p);                                                              \
+                   tm_w[0], tm_w[1], tm_w[2], tm_x, p);                                         \
   }
   FITQ_TC_CASE(16)
   FITQ_TC_CASE(32)
@@ -515,6 +571,11 @@ int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partia
 #undef FITQ_TC_CASE
   note_launch();
   return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
+                       cudaStream_t st, int num_sms) {
+  return launch_nf4_gemv_tc_grouped(&w, 1, x, m, &partial, status, st, num_sms);
 }
 
 }  // namespace fitq

@@ -153,6 +153,11 @@ bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base,
 bool gemv_tc_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slices);
 int launch_nf4_gemv_tc(const Nf4Args& w, const void* x, int64_t m, float* partial, int* status,
                        cudaStream_t st, int num_sms);
+// One launch over up to three weights sharing K, x and the scale format (q/k/v,
+// gate/up): partial[g] = [slices, M, N_g] with the slices gemv_tc_plan gives for
+// N = the sum of the N_g.
+int launch_nf4_gemv_tc_grouped(const Nf4Args* w, int groups, const void* x, int64_t m,
+                               float* const* partial, int* status, cudaStream_t st, int num_sms);
 
 // Cross-entropy of [T, V] bf16 logits, mean over labels != ignore_index; the
 // logits are overwritten with d(loss_scale * loss)/dlogits (ce.cu).

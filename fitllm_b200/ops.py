@@ -4,7 +4,8 @@ device tensors out; every call is asynchronous on the current CUDA stream.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+import ctypes
+from typing import List, Optional, Tuple
 
 import torch
 
@@ -99,6 +100,38 @@ def qlora_backward(x2: Optional[torch.Tensor], dy2: torch.Tensor, w: Nf4WeightCR
                                     _lib.ptr(grad_a), _lib.ptr(grad_b), int(grad_accumulate),
                                     ws.data_ptr(), nbytes, _stream(dev)), "fitq_qlora_bwd")
     return (dx if need_dx else None), grad_a, grad_b
+
+
+def nf4_gemv_grouped(x2: torch.Tensor, jobs) -> List[torch.Tensor]:
+    """Up to three projections of the same x2 [M, K] bf16 in one call
+    (fitq_nf4_gemv_grouped).  jobs: (wref, lora_a, lora_b, scale, bias,
+    y_add) per projection (None for absent parts).  Returns the bf16 [M, N]
+    outputs, each fitq_nf4_gemv's result."""
+    L = _lib.load()
+    m = x2.shape[0]
+    dev = x2.device
+    arr = (_lib.GemvJobC * len(jobs))()
+    keep, outs = [], []
+    for i, (wref, lora_a, lora_b, scale, bias, y_add) in enumerate(jobs):
+        n = wref.c.n_out
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        a = None if lora_a is None else lora_a.detach().to(torch.float32).contiguous()
+        b = None if lora_b is None else lora_b.detach().to(torch.float32).contiguous()
+        bb = None if bias is None else bias.detach().to(torch.bfloat16).contiguous()
+        ya = None if y_add is None else _bf16_2d(y_add, n)
+        keep += [a, b, bb, ya]
+        arr[i].w = ctypes.pointer(wref.c)
+        arr[i].lora_a, arr[i].lora_b = _lib.ptr(a), _lib.ptr(b)
+        arr[i].rank = 0 if a is None else int(a.shape[0])
+        arr[i].scale = float(scale)
+        arr[i].bias, arr[i].y, arr[i].y_add = _lib.ptr(bb), y.data_ptr(), _lib.ptr(ya)
+        outs.append(y)
+    with torch.cuda.device(dev):
+        nbytes = L.fitq_nf4_gemv_grouped_workspace(arr, len(jobs), m)
+        ws = _workspace(nbytes, dev)
+        _lib.check(L.fitq_nf4_gemv_grouped(arr, len(jobs), x2.data_ptr(), m, ws.data_ptr(), nbytes,
+                                           _stream(dev)), "fitq_nf4_gemv_grouped")
+    return outs
 
 
 def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

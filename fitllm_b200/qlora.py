@@ -267,6 +267,29 @@ class QLoRALinear4bit(nn.Module):
         return f"r={self.r[a]}, alpha={self.lora_alpha[a]}, scaling={self.scaling[a]}"
 
 
+def projection_job(mod: nn.Module, y_add: Optional[torch.Tensor] = None):
+    """The fitq_gemv_job arguments (wref, lora_a, lora_b, scale, bias, y_add)
+    of a Linear4bit or QLoRALinear4bit, for inference."""
+    if isinstance(mod, QLoRALinear4bit):
+        a = mod.active_adapter
+        return (mod.base_layer.wref(), mod.lora_A[a].weight, mod.lora_B[a].weight,
+                float(mod.scaling[a]), mod.base_layer.bias, y_add)
+    if isinstance(mod, Linear4bit):
+        return (mod.wref(), None, None, 1.0, mod.bias, y_add)
+    raise TypeError(f"projection_job: not an NF4 projection: {type(mod).__name__}")
+
+
+@torch.no_grad()
+def grouped_forward(mods: Sequence[nn.Module], x: torch.Tensor) -> List[torch.Tensor]:
+    """The outputs of up to three projections of the same x in one
+    fitq_nf4_gemv_grouped call (no autograd; x.shape[:-1] flattens to M <= 64).
+    Same results as calling each module, which the HF layer does one by one
+    (fitllm/forward.py:680-686)."""
+    lead, k = x.shape[:-1], x.shape[-1]
+    ys = ops.nf4_gemv_grouped(ops._bf16_2d(x, k), [projection_job(m) for m in mods])
+    return [y.view(*lead, y.shape[-1]) for y in ys]
+
+
 def inject_qlora(model: nn.Module, r: int, alpha: float, targets: Sequence[str]) -> List[str]:
     """Wrap every Linear4bit whose name matches a target suffix (PEFT
     target_modules semantics: exact child name or dotted suffix)."""

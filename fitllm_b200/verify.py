@@ -28,6 +28,7 @@ import torch.nn.functional as F
 from . import ops
 from .layer import DecoderLayer, rotary_tables
 from .layer_ops import rope, swiglu
+from .qlora import grouped_forward
 
 
 class KVCache:
@@ -76,9 +77,14 @@ def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Te
     attn = layer.self_attn
     cos, sin = tables
     x = layer.input_layernorm(h)
-    q = rope(attn.q_proj(x), cos, sin, cfg.heads).view(b, t, cfg.heads, cfg.head_dim)
-    k = rope(attn.k_proj(x), cos, sin, cfg.kv_heads).view(b, t, cfg.kv_heads, cfg.head_dim)
-    v = attn.v_proj(x).view(b, t, cfg.kv_heads, cfg.head_dim)
+    grouped = b * t <= 64  # the skinny GEMM path: q/k/v (and gate/up) as one launch each
+    if grouped:
+        q_raw, k_raw, v_raw = grouped_forward([attn.q_proj, attn.k_proj, attn.v_proj], x)
+    else:
+        q_raw, k_raw, v_raw = attn.q_proj(x), attn.k_proj(x), attn.v_proj(x)
+    q = rope(q_raw, cos, sin, cfg.heads).view(b, t, cfg.heads, cfg.head_dim)
+    k = rope(k_raw, cos, sin, cfg.kv_heads).view(b, t, cfg.kv_heads, cfg.head_dim)
+    v = v_raw.view(b, t, cfg.kv_heads, cfg.head_dim)
     k_cache[:, :, prefix:prefix + t].copy_(k.transpose(1, 2))
     v_cache[:, :, prefix:prefix + t].copy_(v.transpose(1, 2))
     if kernel_attention_ok(cfg, t):
@@ -91,7 +97,9 @@ def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Te
     h1 = attn.o_proj(o, residual=h)
     mlp = layer.mlp
     x2 = layer.post_attention_layernorm(h1)
-    return mlp.down_proj(swiglu(mlp.gate_proj(x2), mlp.up_proj(x2)), residual=h1)
+    gate, up = grouped_forward([mlp.gate_proj, mlp.up_proj], x2) if grouped else (
+        mlp.gate_proj(x2), mlp.up_proj(x2))
+    return mlp.down_proj(swiglu(gate, up), residual=h1)
 
 
 @torch.no_grad()

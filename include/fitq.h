@@ -154,6 +154,29 @@ FITQ_API int fitq_nf4_gemv(const fitq_nf4_weight* w, const void* x, int64_t m, c
                   const void* y_add, void* workspace, size_t workspace_bytes,
                   fitq_stream_t stream);
 
+/* One projection of a grouped GEMV: y[M, N] = x.W^T + scale.(x.A^T).B^T
+ * (+ bias) (+ y_add), the fitq_nf4_gemv arguments of one weight. */
+typedef struct fitq_gemv_job {
+  const fitq_nf4_weight* w;
+  const float* lora_a; /* fp32 [rank, K] or NULL */
+  const float* lora_b; /* fp32 [N, rank] or NULL */
+  int rank;
+  float scale;
+  const void* bias;    /* bf16 [N] or NULL */
+  void* y;             /* bf16 [M, N] */
+  const void* y_add;   /* bf16 [M, N] or NULL */
+} fitq_gemv_job;
+
+/* Up to three projections of the same x (q/k/v, gate/up of a decoder layer:
+ * the HF layer runs them as separate Linear4bit calls, fitllm/forward.py:
+ * 680-686), each with fitq_nf4_gemv's result.  For 8 < M <= 64 with a shared
+ * K and scale format they run as ONE tcgen05 launch over all their tiles
+ * (small projections such as k/v no longer split K many ways on their own);
+ * otherwise one fitq_nf4_gemv per job, in order. */
+FITQ_API size_t fitq_nf4_gemv_grouped_workspace(const fitq_gemv_job* jobs, int count, int64_t m);
+FITQ_API int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, int64_t m,
+                                   void* workspace, size_t workspace_bytes, fitq_stream_t stream);
+
 /* c[M,N] (bf16) = a[M,K].b[N,K]^T (+ c_add) on the tcgen05 tensor cores,
  * fp32 accumulation.  K % 64 == 0, N % 16 == 0, rows 16-byte aligned. */
 FITQ_API int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, int64_t m,
