@@ -71,6 +71,7 @@ SIGNATURES = {
     "fitq_rope": (I32, [P, P, P, P, I64, I32, I32, I64, I32, P]),
     "fitq_swiglu_fwd": (I32, [P, P, P, I64, P]),
     "fitq_swiglu_bwd": (I32, [P, P, P, P, P, I64, P]),
+    "fitq_rope_append": (I32, [P, P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
     "fitq_nf4_gemv_grouped_workspace": (SZ, [JP, I32, I64]),
     "fitq_nf4_gemv_grouped": (I32, [JP, I32, P, I64, P, SZ, P]),
     "fitq_cross_entropy_workspace": (SZ, [I64]),

@@ -809,6 +809,27 @@ int fitq_verify_attention(const void* q, const void* k_cache, const void* v_cach
                        "verify_attention");
 }
 
+int fitq_rope_append(const void* q, const void* k, const void* v, void* q_out, void* k_cache,
+                     void* v_cache, const float* cos_half, const float* sin_half, int64_t batch,
+                     int t_new, int heads, int kv_heads, int head_dim, int prefix, int capacity,
+                     fitq_stream_t stream) {
+  if (!q || !k || !v || !q_out || !k_cache || !v_cache || !cos_half || !sin_half)
+    return fail(FITQ_ERR_ARG, "rope_append: NULL tensor");
+  if (batch <= 0 || t_new <= 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 16 != 0 ||
+      prefix < 0 || prefix + t_new > capacity)
+    return fail(FITQ_ERR_SHAPE, "rope_append: bad shape (head_dim %% 16 == 0, prefix + T <= capacity)");
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(q_out) || !al16(k_cache) || !al16(v_cache) ||
+      !al16(cos_half) || !al16(sin_half))
+    return fail(FITQ_ERR_ALIGN, "rope_append: 16-byte alignment");
+  int rc;
+  const int sms = current_sms(&rc);
+  if (!sms) return rc;
+  return launch_status(fitq::launch_rope_append(q, k, v, q_out, k_cache, v_cache, cos_half, sin_half,
+                                                batch, t_new, heads, kv_heads, head_dim, prefix,
+                                                capacity, static_cast<cudaStream_t>(stream), sms),
+                       "rope_append");
+}
+
 int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n, fitq_stream_t stream) {
   if (!gate || !up || !act) return fail(FITQ_ERR_ARG, "swiglu: NULL tensor");
   if (n <= 0 || n % 8 != 0) return fail(FITQ_ERR_SHAPE, "swiglu: need n %% 8 == 0");

@@ -197,6 +197,10 @@ int launch_rmsnorm_fwd(const void* x, const void* w, void* y, int64_t rows, int6
                        float eps, cudaStream_t st);
 int launch_rmsnorm_bwd(const void* dy, const void* x, const void* w, void* dx, int64_t rows,
                        int64_t cols, float eps, cudaStream_t st);
+int launch_rope_append(const void* q, const void* k, const void* v, void* q_out, void* k_cache,
+                       void* v_cache, const float* cs, const float* sn, int64_t batch, int t_new,
+                       int heads, int kv_heads, int dim, int prefix, int cap, cudaStream_t st,
+                       int num_sms);
 int launch_rope(const void* t, void* out, const float* cs, const float* sn, int64_t rows,
                 int heads, int dim, int64_t seq, int backward, cudaStream_t st, int num_sms);
 int launch_swiglu_fwd(const void* g, const void* u, void* act, int64_t n, cudaStream_t st,

@@ -161,6 +161,62 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ t, __nv_bfloat16* 
   }
 }
 
+// Verify step: rotary embedding of the new tokens' q and k plus the append of
+// k (rotated) and v to the KV cache, one launch.  Row b * T + t of q/k/v is
+// token t of sequence b at position prefix + t (cos/sin row t); work item =
+// (row, head slot, 8-element group of a half), head slots: H of q, KVH of k,
+// KVH of v (copied unrotated).  Same arithmetic as rope_kernel<false>.
+__global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                                   const __nv_bfloat16* __restrict__ v, __nv_bfloat16* __restrict__ q_out,
+                                   __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
+                                   const float* __restrict__ cs, const float* __restrict__ sn, int64_t rows,
+                                   int T, int H, int KVH, int dim, int prefix, int cap) {
+  const int half = dim / 2;
+  const int groups = half / 8;
+  const int slots = H + 2 * KVH;
+  const int64_t total = rows * slots * groups;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int gi = static_cast<int>(e % groups);
+    const int64_t rs = e / groups;
+    const int slot = static_cast<int>(rs % slots);
+    const int64_t row = rs / slots;
+    const int t = static_cast<int>(row % T);
+    const int64_t b = row / T;
+    const __nv_bfloat16* src;
+    __nv_bfloat16* dst;
+    if (slot < H) {
+      src = q + (row * H + slot) * dim;
+      dst = q_out + (row * H + slot) * dim;
+    } else {
+      const int kh = slot < H + KVH ? slot - H : slot - H - KVH;
+      src = (slot < H + KVH ? k : v) + (row * KVH + kh) * dim;
+      dst = (slot < H + KVH ? kc : vc) + ((b * KVH + kh) * cap + prefix + t) * static_cast<int64_t>(dim);
+    }
+    float a[8], bb[8];
+    load8(src + gi * 8, a);
+    load8(src + half + gi * 8, bb);
+    if (slot < H + KVH) {
+      const float4* cp = reinterpret_cast<const float4*>(cs + static_cast<int64_t>(t) * half + gi * 8);
+      const float4* sp = reinterpret_cast<const float4*>(sn + static_cast<int64_t>(t) * half + gi * 8);
+      const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      float oa[8], ob[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        oa[i] = a[i] * c[i] - bb[i] * s[i];
+        ob[i] = bb[i] * c[i] + a[i] * s[i];
+      }
+      store8(dst + gi * 8, oa);
+      store8(dst + half + gi * 8, ob);
+    } else {
+      store8(dst + gi * 8, a);
+      store8(dst + half + gi * 8, bb);
+    }
+  }
+}
+
 __device__ __forceinline__ float sigmoidf_(float g) { return 1.0f / (1.0f + __expf(-g)); }
 
 // act = silu(g) * u
@@ -238,6 +294,21 @@ int launch_rope(const void* t, void* out, const float* cs, const float* sn, int6
     rope_kernel<false><<<grid_1d(work, num_sms), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(t), static_cast<__nv_bfloat16*>(out), cs, sn, rows,
         heads, dim, seq);
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_rope_append(const void* q, const void* k, const void* v, void* q_out, void* k_cache,
+                       void* v_cache, const float* cs, const float* sn, int64_t batch, int t_new,
+                       int heads, int kv_heads, int dim, int prefix, int cap, cudaStream_t st,
+                       int num_sms) {
+  const int64_t rows = batch * t_new;
+  const int64_t work = rows * (heads + 2 * kv_heads) * (dim / 16);
+  rope_append_kernel<<<grid_1d(work, num_sms), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+      static_cast<const __nv_bfloat16*>(v), static_cast<__nv_bfloat16*>(q_out),
+      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), cs, sn, rows, t_new,
+      heads, kv_heads, dim, prefix, cap);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }

@@ -112,5 +112,25 @@ def rope(t, cos_half, sin_half, heads):
     return RoPEFn.apply(t, cos_half, sin_half, heads)
 
 
+def rope_kv_append(q, k, v, cos_half, sin_half, k_cache, v_cache, prefix: int, heads: int,
+                   kv_heads: int):
+    """Verify step (no autograd): q [B, T, heads*D], k/v [B, T, kv_heads*D]
+    bf16 -> rotated q [B, T, heads, D]; rotated k and v written into the
+    caches [B, kv_heads, cap, D] at positions [prefix, prefix + T)."""
+    b, t = q.shape[0], q.shape[1]
+    d = q.shape[-1] // heads
+    q, k, v = _c(q), _c(k), _c(v)
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("rope_kv_append: caches must be contiguous")
+    out = torch.empty_like(q)
+    L = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(L.fitq_rope_append(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                      k_cache.data_ptr(), v_cache.data_ptr(), _c(cos_half).data_ptr(),
+                                      _c(sin_half).data_ptr(), b, t, heads, kv_heads, d, prefix,
+                                      int(k_cache.shape[2]), _st(q)), "fitq_rope_append")
+    return out.view(b, t, heads, d)
+
+
 def swiglu(gate, up):
     return SwiGLUFn.apply(gate, up)

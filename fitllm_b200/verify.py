@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .layer import DecoderLayer, rotary_tables
-from .layer_ops import rope, swiglu
+from .layer_ops import rope_kv_append, swiglu
 from .qlora import grouped_forward
 
 
@@ -82,11 +82,9 @@ def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Te
         q_raw, k_raw, v_raw = grouped_forward([attn.q_proj, attn.k_proj, attn.v_proj], x)
     else:
         q_raw, k_raw, v_raw = attn.q_proj(x), attn.k_proj(x), attn.v_proj(x)
-    q = rope(q_raw, cos, sin, cfg.heads).view(b, t, cfg.heads, cfg.head_dim)
-    k = rope(k_raw, cos, sin, cfg.kv_heads).view(b, t, cfg.kv_heads, cfg.head_dim)
-    v = v_raw.view(b, t, cfg.kv_heads, cfg.head_dim)
-    k_cache[:, :, prefix:prefix + t].copy_(k.transpose(1, 2))
-    v_cache[:, :, prefix:prefix + t].copy_(v.transpose(1, 2))
+    # rotary embedding of q and k and the append of k, v to the caches: one launch
+    q = rope_kv_append(q_raw, k_raw, v_raw, cos, sin, k_cache, v_cache, prefix, cfg.heads,
+                       cfg.kv_heads)
     if kernel_attention_ok(cfg, t):
         o = ops.verify_attention(q, k_cache, v_cache, prefix)
     else:

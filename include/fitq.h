@@ -228,6 +228,17 @@ FITQ_API int fitq_rope(const void* t, void* out, const float* cos_half, const fl
 FITQ_API int fitq_swiglu_fwd(const void* gate, const void* up, void* act, int64_t n,
                              fitq_stream_t stream);
 
+/* Verify step with a KV cache: rotary embedding of the T new tokens' q and k
+ * (positions prefix + t, fp32 half tables cos/sin [T, head_dim/2], the
+ * fitq_rope arithmetic) and the append of rotated k and of v to the caches
+ * [B, KVH, capacity, head_dim] at [prefix, prefix + T), one launch.
+ * q, q_out: [B*T, heads*head_dim]; k, v: [B*T, kv_heads*head_dim] bf16. */
+FITQ_API int fitq_rope_append(const void* q, const void* k, const void* v, void* q_out,
+                              void* k_cache, void* v_cache, const float* cos_half,
+                              const float* sin_half, int64_t batch, int t_new, int heads,
+                              int kv_heads, int head_dim, int prefix, int capacity,
+                              fitq_stream_t stream);
+
 /* Cross-entropy of lm_head logits, forward and backward: loss_out (device
  * fp32 scalar) = mean over rows with label != ignore_index of
  * logsumexp(logits[t]) - logits[t, label[t]] (torch CrossEntropyLoss, as

@@ -416,3 +416,29 @@ def test_engine_step_with_lm_head_loss(cuda_dev):
             for ab in ("A", "B"):
                 got = gv[f"self_attn.{n}.lora_{ab}.default.weight"].cpu().numpy()
                 assert onf4.rel_err(got, params[l][f"{n}.lora_{ab}"].grad.numpy()) < REL
+
+
+def test_rope_kv_append_matches_rope_and_copy(cuda_dev):
+    """fitq_rope_append (one launch) gives the rotated q of the rope kernel and
+    writes the rotated k and the v of the new tokens into the caches exactly
+    where the unfused rope + cache copies put them, leaving the rest untouched."""
+    from fitllm_b200.layer import rotary_tables
+    from fitllm_b200.layer_ops import rope, rope_kv_append
+    b, t, h, kvh, d, prefix, cap = 3, 5, 8, 2, 128, 37, 50
+    g = torch.Generator(device=cuda_dev).manual_seed(61)
+    q = torch.randn(b, t, h * d, generator=g, device=cuda_dev).bfloat16()
+    k = torch.randn(b, t, kvh * d, generator=g, device=cuda_dev).bfloat16()
+    v = torch.randn(b, t, kvh * d, generator=g, device=cuda_dev).bfloat16()
+    cos, sin = rotary_tables(t, d, 1e6, cuda_dev, position_ids=torch.arange(prefix, prefix + t, device=cuda_dev))
+    kc = torch.randn(b, kvh, cap, d, generator=g, device=cuda_dev).bfloat16()
+    vc = torch.randn(b, kvh, cap, d, generator=g, device=cuda_dev).bfloat16()
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    with torch.no_grad():
+        q_ref = rope(q, cos, sin, h).view(b, t, h, d)
+        k_rot = rope(k, cos, sin, kvh).view(b, t, kvh, d)
+    kc_ref[:, :, prefix:prefix + t] = k_rot.transpose(1, 2)
+    vc_ref[:, :, prefix:prefix + t] = v.view(b, t, kvh, d).transpose(1, 2)
+    q_out = rope_kv_append(q, k, v, cos, sin, kc, vc, prefix, h, kvh)
+    torch.cuda.synchronize()
+    assert torch.equal(q_out, q_ref)
+    assert torch.equal(kc, kc_ref) and torch.equal(vc, vc_ref)
