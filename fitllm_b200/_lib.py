@@ -74,6 +74,8 @@ SIGNATURES = {
     "fitq_rope_append": (I32, [P, P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
     "fitq_nf4_gemv_grouped_workspace": (SZ, [JP, I32, I64]),
     "fitq_nf4_gemv_grouped": (I32, [JP, I32, P, I64, P, SZ, P]),
+    "fitq_nf4_gemv_swiglu_workspace": (SZ, [JP, I64]),
+    "fitq_nf4_gemv_swiglu": (I32, [JP, P, I64, P, P, SZ, P]),
     "fitq_cross_entropy_workspace": (SZ, [I64]),
     "fitq_cross_entropy": (I32, [P, P, I64, I64, I64, F32, P, P, SZ, P]),
     "fitq_verify_attention_workspace": (SZ, [I64, I32, I32, I32, I32]),

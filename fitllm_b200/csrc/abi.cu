@@ -416,34 +416,67 @@ static size_t grouped_bytes(const fitq_gemv_job* jobs, int count, int64_t m, int
   return c.used;
 }
 
-size_t fitq_nf4_gemv_grouped_workspace(const fitq_gemv_job* jobs, int count, int64_t m) {
-  if (!jobs || count < 1) return 0;
+// Bytes of the fallback of the SwiGLU entry: gate and up outputs (bf16) ahead
+// of the per-projection GEMV workspace.
+static size_t swiglu_scratch_bytes(const fitq_gemv_job* jobs, int64_t m) {
+  return 2 * ((static_cast<size_t>(m) * jobs[0].w->n_out * 2 + 255) / 256 * 256);
+}
+
+static size_t grouped_workspace(const fitq_gemv_job* jobs, int count, int64_t m, bool swiglu) {
+  if (!jobs || count < 1 || count > 3) return 0;
+  for (int g = 0; g < count; ++g)
+    if (!jobs[g].w) return 0;
   const int sms = sms_for_sizing();
   int slices = 0;
   if (grouped_tc(jobs, count, m, sms, &slices)) return grouped_bytes(jobs, count, m, slices);
   size_t need = 0;
   for (int g = 0; g < count; ++g) {
-    if (!jobs[g].w) return 0;
     const size_t b = fitq_nf4_gemv_workspace(m, jobs[g].w->n_out, jobs[g].w->k_in, jobs[g].rank);
     need = b > need ? b : need;
   }
-  return need;
+  return need + (swiglu ? swiglu_scratch_bytes(jobs, m) : 0);
 }
 
-int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, int64_t m,
-                          void* workspace, size_t workspace_bytes, fitq_stream_t stream) {
-  if (!jobs || count < 1 || count > 3) return fail(FITQ_ERR_ARG, "nf4_gemv_grouped: 1 to 3 jobs");
+size_t fitq_nf4_gemv_grouped_workspace(const fitq_gemv_job* jobs, int count, int64_t m) {
+  return grouped_workspace(jobs, count, m, false);
+}
+
+size_t fitq_nf4_gemv_swiglu_workspace(const fitq_gemv_job* jobs, int64_t m) {
+  return grouped_workspace(jobs, 2, m, true);
+}
+
+// One grouped launch of 1-3 projections of x; with act set (the SwiGLU entry)
+// the two results are combined in the finishing pass and only act is stored.
+static int grouped_impl(const fitq_gemv_job* jobs, int count, const void* x, int64_t m, void* act,
+                        void* workspace, size_t workspace_bytes, fitq_stream_t stream) {
+  const char* what = act ? "nf4_gemv_swiglu" : "nf4_gemv_grouped";
   int rc;
   const int sms = current_sms(&rc);
   if (!sms) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   int slices = 0;
   if (!grouped_tc(jobs, count, m, sms, &slices)) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    size_t left = workspace_bytes;
+    void* y[3] = {nullptr, nullptr, nullptr};
+    if (act) {  // gate and up into the workspace, then the elementwise kernel
+      const size_t scratch = swiglu_scratch_bytes(jobs, m);
+      if (!ws || left < scratch)
+        return fail(FITQ_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", what, left, scratch);
+      y[0] = ws;
+      y[1] = ws + scratch / 2;
+      ws += scratch;
+      left -= scratch;
+    }
     for (int g = 0; g < count; ++g) {
       const fitq_gemv_job& j = jobs[g];
-      rc = fitq_nf4_gemv(j.w, x, m, j.lora_a, j.lora_b, j.rank, j.scale, j.bias, j.y, j.y_add,
-                         workspace, workspace_bytes, stream);
+      rc = fitq_nf4_gemv(j.w, x, m, j.lora_a, j.lora_b, j.rank, j.scale, j.bias, act ? y[g] : j.y,
+                         j.y_add, ws, left, stream);
       if (rc) return rc;
     }
+    if (act)
+      return launch_status(fitq::launch_swiglu_fwd(y[0], y[1], act, m * jobs[0].w->n_out, st, sms),
+                           "swiglu_fwd");
     return FITQ_OK;
   }
   // the checks of fitq_nf4_gemv, per job
@@ -451,16 +484,16 @@ int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, i
   for (int g = 0; g < count; ++g) {
     const fitq_gemv_job& j = jobs[g];
     if ((rc = check_weight(j.w, &a[g]))) return rc;
-    if (!x || !j.y) return fail(FITQ_ERR_ARG, "nf4_gemv_grouped: x and y are required");
-    if (!valid_rank(j.rank)) return fail(FITQ_ERR_UNSUPPORTED, "nf4_gemv_grouped: rank %d", j.rank);
+    if (!x || (!act && !j.y)) return fail(FITQ_ERR_ARG, "%s: x and y are required", what);
+    if (!valid_rank(j.rank)) return fail(FITQ_ERR_UNSUPPORTED, "%s: rank %d", what, j.rank);
     if (j.rank > 0 && (!j.lora_a || !j.lora_b || !al16(j.lora_a) || !al16(j.lora_b)))
-      return fail(FITQ_ERR_ALIGN, "nf4_gemv_grouped: lora_a / lora_b required, 16-byte aligned");
-    if (!al16(x) || !al16(j.y) || (j.y_add && !al16(j.y_add)) || (j.bias && !al16(j.bias)))
-      return fail(FITQ_ERR_ALIGN, "nf4_gemv_grouped: x/y/bias/y_add must be 16-byte aligned");
+      return fail(FITQ_ERR_ALIGN, "%s: lora_a / lora_b required, 16-byte aligned", what);
+    if (!al16(x) || (j.y && !al16(j.y)) || (j.y_add && !al16(j.y_add)) || (j.bias && !al16(j.bias)))
+      return fail(FITQ_ERR_ALIGN, "%s: x/y/bias/y_add must be 16-byte aligned", what);
   }
   const size_t need = grouped_bytes(jobs, count, m, slices);
   if (workspace_bytes < need || !workspace)
-    return fail(FITQ_ERR_WORKSPACE, "nf4_gemv_grouped: workspace %zu < %zu bytes", workspace_bytes, need);
+    return fail(FITQ_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", what, workspace_bytes, need);
   Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
   float* partial[3] = {nullptr, nullptr, nullptr};
   float* t_part[3] = {nullptr, nullptr, nullptr};
@@ -469,23 +502,41 @@ int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, i
     if (jobs[g].rank > 0)
       t_part[g] = static_cast<float*>(c.take(fitq::lora_t_workspace(m, a[g].k_in, jobs[g].rank)));
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t K = a[0].k_in;
   rc = fitq::launch_nf4_gemv_tc_grouped(a, count, x, m, partial, status_ptr(), st, sms);
   if (rc) return launch_status(rc, "nf4_gemv_grouped tcgen05");
+  fitq::GemvEpilogue ep[3];
+  int64_t n_out[3];
   for (int g = 0; g < count; ++g) {
     const fitq_gemv_job& j = jobs[g];
     if (j.rank > 0 && (rc = fitq::launch_lora_t(x, m, K, j.lora_a, j.rank, t_part[g], st)))
       return launch_status(rc, "lora T = x.A^T");
+    ep[g] = fitq::GemvEpilogue{j.y, j.y_add, j.bias, j.lora_b, t_part[g], fitq::lora_t_groups(K), nullptr,
+                               j.rank, j.scale, partial[g]};
+    n_out[g] = a[g].n_out;
   }
-  for (int g = 0; g < count; ++g) {
-    const fitq_gemv_job& j = jobs[g];
-    fitq::GemvEpilogue ep{j.y, j.y_add, j.bias, j.lora_b, t_part[g], fitq::lora_t_groups(K), nullptr,
-                          j.rank, j.scale, partial[g]};
-    rc = fitq::launch_nf4_gemv_dec_finish(m, a[g].n_out, slices, ep, st, sms);
-    if (rc) return launch_status(rc, "nf4_gemv_grouped finish");
-  }
-  return FITQ_OK;
+  return launch_status(fitq::launch_nf4_gemv_group_finish(m, n_out, count, slices, ep, act, st),
+                       "nf4_gemv_grouped finish");
+}
+
+int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, int64_t m,
+                          void* workspace, size_t workspace_bytes, fitq_stream_t stream) {
+  if (!jobs || count < 1 || count > 3) return fail(FITQ_ERR_ARG, "nf4_gemv_grouped: 1 to 3 jobs");
+  return grouped_impl(jobs, count, x, m, nullptr, workspace, workspace_bytes, stream);
+}
+
+int fitq_nf4_gemv_swiglu(const fitq_gemv_job* jobs, const void* x, int64_t m, void* act,
+                         void* workspace, size_t workspace_bytes, fitq_stream_t stream) {
+  if (!jobs || !jobs[0].w || !jobs[1].w || !act)
+    return fail(FITQ_ERR_ARG, "nf4_gemv_swiglu: gate, up and act are required");
+  if (jobs[0].w->n_out != jobs[1].w->n_out || jobs[0].w->k_in != jobs[1].w->k_in)
+    return fail(FITQ_ERR_SHAPE, "nf4_gemv_swiglu: gate and up must have the same shape");
+  if (jobs[0].rank != 0 || jobs[1].rank != 0)
+    return fail(FITQ_ERR_UNSUPPORTED, "nf4_gemv_swiglu: gate/up with LoRA are not fused");
+  if (m <= 0 || (m * jobs[0].w->n_out) % 8 != 0)
+    return fail(FITQ_ERR_SHAPE, "nf4_gemv_swiglu: need m * n_out %% 8 == 0");
+  if (!al16(act)) return fail(FITQ_ERR_ALIGN, "nf4_gemv_swiglu: act must be 16-byte aligned");
+  return grouped_impl(jobs, 2, x, m, act, workspace, workspace_bytes, stream);
 }
 
 size_t fitq_qlora_bwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank) {

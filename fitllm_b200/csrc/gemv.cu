@@ -291,8 +291,8 @@ __device__ __forceinline__ void tile_scales(const ScaleBuf<NESTED>& b, uint32_t 
 
 // y[tk, n] = bf16(s + scale * T[tk].B[n] + bias[n] + y_add[tk, n]); tl: row tk of
 // T as fp32 (bf16-rounded values), null when rank == 0.
-__device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* tl, int N, int tk,
-                                          int n, float s) {
+__device__ __forceinline__ float dec_value(const GemvEpilogue& o, const float* tl, int N, int tk,
+                                           int n, float s) {
   if (o.rank > 0) {
     const float4* bl = reinterpret_cast<const float4*>(o.lora_b + static_cast<int64_t>(n) * o.rank);
     float l = 0.f;
@@ -308,7 +308,13 @@ __device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* tl
   const int64_t e = static_cast<int64_t>(tk) * N + n;
   if (o.bias) s += __bfloat162float(static_cast<const __nv_bfloat16*>(o.bias)[n]);
   if (o.y_add) s += __bfloat162float(static_cast<const __nv_bfloat16*>(o.y_add)[e]);
-  static_cast<__nv_bfloat16*>(o.y)[e] = __float2bfloat16_rn(s);
+  return s;
+}
+
+__device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* tl, int N, int tk,
+                                          int n, float s) {
+  static_cast<__nv_bfloat16*>(o.y)[static_cast<int64_t>(tk) * N + n] =
+      __float2bfloat16_rn(dec_value(o, tl, N, tk, n, s));
 }
 
 template <bool NESTED>
@@ -535,6 +541,84 @@ __global__ void __launch_bounds__(256)
     float v = 0.f;
     for (int sl = 0; sl < slices; ++sl) v += __ldcg(out.partial + sl * total + e);
     dec_store(out, out.rank > 0 ? s_t : nullptr, N, tk, n, v);
+  }
+}
+
+// T[tk] of one epilogue into s_t (bf16-rounded, as fp32); all threads of the
+// block take part.  Shared by the finishing kernels.
+__device__ __forceinline__ void finish_t_row(const GemvEpilogue& out, int M, int tk, float* s_t,
+                                             float* s_stg, bool write_dense) {
+  const int r = out.rank, G = out.t_groups;
+  const int gc = kFinStage / r;
+  const float* src = out.t_part + static_cast<int64_t>(tk) * r;
+  float acc = 0.f;
+  for (int g0 = 0; g0 < G; g0 += gc) {
+    const int ng = G - g0 < gc ? G - g0 : gc, items = ng * r;
+    for (int b = threadIdx.x; b < items; b += 8 * 256) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = b + u * 256;
+        v[u] = i < items ? __ldcg(src + static_cast<int64_t>(g0 + i / r) * M * r + i % r) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (b + u * 256 < items) s_stg[b + u * 256] = v[u];
+    }
+    __syncthreads();
+    if (threadIdx.x < r)
+      for (int g = 0; g < ng; ++g) acc += s_stg[g * r + threadIdx.x];
+    __syncthreads();
+  }
+  if (threadIdx.x < r) {
+    const __nv_bfloat16 tb = __float2bfloat16_rn(acc);
+    s_t[threadIdx.x] = __bfloat162float(tb);
+    if (write_dense && out.t_dense)
+      static_cast<__nv_bfloat16*>(out.t_dense)[static_cast<int64_t>(tk) * r + threadIdx.x] = tb;
+  }
+  __syncthreads();
+}
+
+// Finishing pass of a grouped launch: the split-K sums and epilogues of up to
+// three projections in one grid, blockIdx.x ranges [nb_end[j-1], nb_end[j])
+// for projection j.  With act set (two projections of equal N, no LoRA), the
+// two results are not stored: act = SwiGLU(first, second) is, with the
+// arithmetic of swiglu_fwd_kernel on the bf16-rounded results.
+struct GroupFinish {
+  GemvEpilogue ep[3];
+  int n[3];
+  int nb_end[3];
+  __nv_bfloat16* act;
+};
+
+__global__ void __launch_bounds__(256)
+    gemv_group_finish_kernel(int M, int slices, GroupFinish gf) {
+  __shared__ float s_t[64];
+  extern __shared__ float s_stg[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tk = blockIdx.y;
+  const int j = blockIdx.x < gf.nb_end[0] ? 0 : blockIdx.x < gf.nb_end[1] ? 1 : 2;
+  const int b0 = j == 0 ? 0 : j == 1 ? gf.nb_end[0] : gf.nb_end[1];
+  const int nbj = (j == 0 ? gf.nb_end[0] : j == 1 ? gf.nb_end[1] : gf.nb_end[2]) - b0;
+  const GemvEpilogue out = j == 0 ? gf.ep[0] : j == 1 ? gf.ep[1] : gf.ep[2];
+  const int N = j == 0 ? gf.n[0] : j == 1 ? gf.n[1] : gf.n[2];
+  if (out.rank > 0) finish_t_row(out, M, tk, s_t, s_stg, blockIdx.x == b0);
+  const int64_t total = static_cast<int64_t>(M) * N;
+  for (int n = (blockIdx.x - b0) * blockDim.x + threadIdx.x; n < N; n += nbj * blockDim.x) {
+    const int64_t e = static_cast<int64_t>(tk) * N + n;
+    float v = 0.f;
+    for (int sl = 0; sl < slices; ++sl) v += __ldcg(out.partial + sl * total + e);
+    if (gf.act == nullptr) {
+      dec_store(out, out.rank > 0 ? s_t : nullptr, N, tk, n, v);
+    } else {
+      const GemvEpilogue& o2 = gf.ep[1];
+      float u = 0.f;
+      for (int sl = 0; sl < slices; ++sl) u += __ldcg(o2.partial + sl * total + e);
+      const float a = __bfloat162float(__float2bfloat16_rn(dec_value(out, nullptr, N, tk, n, v)));
+      const float b = __bfloat162float(__float2bfloat16_rn(dec_value(o2, nullptr, N, tk, n, u)));
+      gf.act[e] = __float2bfloat16_rn(a * (1.0f / (1.0f + __expf(-a))) * b);
+    }
   }
 }
 
@@ -872,6 +956,34 @@ int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvE
   const cudaError_t e = launch_pdl(gemv_dec_finish_kernel,
                                    dim3(static_cast<unsigned>(nb), static_cast<unsigned>(m)), dim3(256),
                                    smem, st, static_cast<int>(m), static_cast<int>(n_out), slices, out);
+  note_launch();
+  return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_nf4_gemv_group_finish(int64_t m, const int64_t* n_out, int jobs, int slices,
+                                 const GemvEpilogue* eps, void* swiglu_act, cudaStream_t st) {
+  if (jobs < 1 || jobs > 3 || (swiglu_act && (jobs != 2 || n_out[0] != n_out[1]))) return FITQ_ERR_UNSUPPORTED;
+  GroupFinish gf{};
+  int end = 0, rank_any = 0;
+  const int used = swiglu_act ? 1 : jobs;  // SwiGLU: one column range covers both
+  for (int j = 0; j < 3; ++j) {
+    const int jj = j < jobs ? j : 0;
+    gf.ep[j] = eps[jj];
+    gf.n[j] = static_cast<int>(n_out[jj]);
+    if (eps[jj].rank > 64 || (swiglu_act && eps[jj].rank > 0)) return FITQ_ERR_UNSUPPORTED;
+    if (j < used) {
+      int64_t nb = (n_out[j] + 511) / 512;
+      if (nb > 64) nb = 64;
+      end += static_cast<int>(nb);
+      rank_any |= eps[j].rank;
+    }
+    gf.nb_end[j] = end;
+  }
+  gf.act = static_cast<__nv_bfloat16*>(swiglu_act);
+  const size_t smem = rank_any ? kFinStage * sizeof(float) : 0;
+  const cudaError_t e = launch_pdl(gemv_group_finish_kernel,
+                                   dim3(static_cast<unsigned>(end), static_cast<unsigned>(m)), dim3(256),
+                                   smem, st, static_cast<int>(m), slices, gf);
   note_launch();
   return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }

@@ -139,6 +139,11 @@ int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEp
                         cudaStream_t st, int num_sms);
 int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
                                cudaStream_t st, int num_sms);
+// The finishing pass of a grouped launch (up to three epilogues, one grid);
+// with swiglu_act (two projections of equal N, rank 0) only
+// act = SwiGLU(first, second) is stored, bf16 [M, N].
+int launch_nf4_gemv_group_finish(int64_t m, const int64_t* n_out, int jobs, int slices,
+                                 const GemvEpilogue* eps, void* swiglu_act, cudaStream_t st);
 
 // 2-D tiled tensor map [outer rows][inner elements], row pitch row_bytes; elements
 // outside the tensor read as zero (gemm_sm100.cu).

@@ -102,19 +102,17 @@ def qlora_backward(x2: Optional[torch.Tensor], dy2: torch.Tensor, w: Nf4WeightCR
     return (dx if need_dx else None), grad_a, grad_b
 
 
-def nf4_gemv_grouped(x2: torch.Tensor, jobs) -> List[torch.Tensor]:
-    """Up to three projections of the same x2 [M, K] bf16 in one call
-    (fitq_nf4_gemv_grouped).  jobs: (wref, lora_a, lora_b, scale, bias,
-    y_add) per projection (None for absent parts).  Returns the bf16 [M, N]
-    outputs, each fitq_nf4_gemv's result."""
-    L = _lib.load()
+def _gemv_jobs(x2: torch.Tensor, jobs, with_y: bool):
+    """The fitq_gemv_job array of (wref, lora_a, lora_b, scale, bias, y_add)
+    tuples, the tensors it points at (kept alive by the caller) and, with
+    with_y, the bf16 [M, N] outputs it writes."""
     m = x2.shape[0]
     dev = x2.device
     arr = (_lib.GemvJobC * len(jobs))()
     keep, outs = [], []
     for i, (wref, lora_a, lora_b, scale, bias, y_add) in enumerate(jobs):
         n = wref.c.n_out
-        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev) if with_y else None
         a = None if lora_a is None else lora_a.detach().to(torch.float32).contiguous()
         b = None if lora_b is None else lora_b.detach().to(torch.float32).contiguous()
         bb = None if bias is None else bias.detach().to(torch.bfloat16).contiguous()
@@ -124,14 +122,44 @@ def nf4_gemv_grouped(x2: torch.Tensor, jobs) -> List[torch.Tensor]:
         arr[i].lora_a, arr[i].lora_b = _lib.ptr(a), _lib.ptr(b)
         arr[i].rank = 0 if a is None else int(a.shape[0])
         arr[i].scale = float(scale)
-        arr[i].bias, arr[i].y, arr[i].y_add = _lib.ptr(bb), y.data_ptr(), _lib.ptr(ya)
+        arr[i].bias, arr[i].y, arr[i].y_add = _lib.ptr(bb), _lib.ptr(y), _lib.ptr(ya)
         outs.append(y)
+    return arr, keep, outs
+
+
+def nf4_gemv_grouped(x2: torch.Tensor, jobs) -> List[torch.Tensor]:
+    """Up to three projections of the same x2 [M, K] bf16 in one call
+    (fitq_nf4_gemv_grouped).  jobs: (wref, lora_a, lora_b, scale, bias,
+    y_add) per projection (None for absent parts).  Returns the bf16 [M, N]
+    outputs, each fitq_nf4_gemv's result."""
+    L = _lib.load()
+    m = x2.shape[0]
+    dev = x2.device
+    arr, keep, outs = _gemv_jobs(x2, jobs, True)
     with torch.cuda.device(dev):
         nbytes = L.fitq_nf4_gemv_grouped_workspace(arr, len(jobs), m)
         ws = _workspace(nbytes, dev)
         _lib.check(L.fitq_nf4_gemv_grouped(arr, len(jobs), x2.data_ptr(), m, ws.data_ptr(), nbytes,
                                            _stream(dev)), "fitq_nf4_gemv_grouped")
+    del keep
     return outs
+
+
+def nf4_gemv_swiglu(x2: torch.Tensor, gate_job, up_job) -> torch.Tensor:
+    """SiLU(x2.Wg^T) * (x2.Wu^T) as bf16 [M, N] (fitq_nf4_gemv_swiglu): the
+    gate and up projections (rank 0) and the SwiGLU of their bf16 results."""
+    L = _lib.load()
+    m = x2.shape[0]
+    dev = x2.device
+    arr, keep, _ = _gemv_jobs(x2, [gate_job, up_job], False)
+    act = torch.empty(m, gate_job[0].c.n_out, dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        nbytes = L.fitq_nf4_gemv_swiglu_workspace(arr, m)
+        ws = _workspace(nbytes, dev)
+        _lib.check(L.fitq_nf4_gemv_swiglu(arr, x2.data_ptr(), m, act.data_ptr(), ws.data_ptr(), nbytes,
+                                          _stream(dev)), "fitq_nf4_gemv_swiglu")
+    del keep
+    return act
 
 
 def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

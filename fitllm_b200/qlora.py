@@ -290,6 +290,17 @@ def grouped_forward(mods: Sequence[nn.Module], x: torch.Tensor) -> List[torch.Te
     return [y.view(*lead, y.shape[-1]) for y in ys]
 
 
+@torch.no_grad()
+def swiglu_forward(gate: nn.Module, up: nn.Module, x: torch.Tensor) -> torch.Tensor:
+    """SiLU(gate(x)) * up(x) in one fitq_nf4_gemv_swiglu call (no autograd;
+    gate and up without LoRA, M <= 64): the HF MLP's act_fn(gate_proj(x)) *
+    up_proj(x) (fitllm/forward.py:680-686), bit-identical to the two modules
+    followed by the SwiGLU kernel."""
+    lead, k = x.shape[:-1], x.shape[-1]
+    act = ops.nf4_gemv_swiglu(ops._bf16_2d(x, k), projection_job(gate), projection_job(up))
+    return act.view(*lead, act.shape[-1])
+
+
 def inject_qlora(model: nn.Module, r: int, alpha: float, targets: Sequence[str]) -> List[str]:
     """Wrap every Linear4bit whose name matches a target suffix (PEFT
     target_modules semantics: exact child name or dotted suffix)."""

@@ -28,7 +28,7 @@ import torch.nn.functional as F
 from . import ops
 from .layer import DecoderLayer, rotary_tables
 from .layer_ops import rope_kv_append, swiglu
-from .qlora import grouped_forward
+from .qlora import QLoRALinear4bit, grouped_forward, swiglu_forward
 
 
 class KVCache:
@@ -95,9 +95,14 @@ def verify_layer_forward(layer: DecoderLayer, h: torch.Tensor, k_cache: torch.Te
     h1 = attn.o_proj(o, residual=h)
     mlp = layer.mlp
     x2 = layer.post_attention_layernorm(h1)
-    gate, up = grouped_forward([mlp.gate_proj, mlp.up_proj], x2) if grouped else (
-        mlp.gate_proj(x2), mlp.up_proj(x2))
-    return mlp.down_proj(swiglu(gate, up), residual=h1)
+    if grouped and not isinstance(mlp.gate_proj, QLoRALinear4bit) and not isinstance(mlp.up_proj,
+                                                                                       QLoRALinear4bit):
+        act = swiglu_forward(mlp.gate_proj, mlp.up_proj, x2)  # gate/up/SwiGLU, one GEMM + one finish
+    else:
+        gate, up = grouped_forward([mlp.gate_proj, mlp.up_proj], x2) if grouped else (
+            mlp.gate_proj(x2), mlp.up_proj(x2))
+        act = swiglu(gate, up)
+    return mlp.down_proj(act, residual=h1)
 
 
 @torch.no_grad()

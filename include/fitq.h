@@ -177,6 +177,17 @@ FITQ_API size_t fitq_nf4_gemv_grouped_workspace(const fitq_gemv_job* jobs, int c
 FITQ_API int fitq_nf4_gemv_grouped(const fitq_gemv_job* jobs, int count, const void* x, int64_t m,
                                    void* workspace, size_t workspace_bytes, fitq_stream_t stream);
 
+/* The MLP input of a decoder layer: act[M, N] = SiLU(gate) * up with
+ * gate = x.Wg^T, up = x.Wu^T (jobs[0], jobs[1]; rank 0, same shape; their y
+ * is not written), the HF Qwen2MLP's act_fn(gate_proj(x)) * up_proj(x) that
+ * fitllm/forward.py:680-686 runs per layer.  Bit-identical to
+ * fitq_nf4_gemv_grouped followed by fitq_swiglu_fwd; on the grouped tcgen05
+ * path the SwiGLU is applied in the finishing pass, so gate and up are never
+ * stored. */
+FITQ_API size_t fitq_nf4_gemv_swiglu_workspace(const fitq_gemv_job* jobs, int64_t m);
+FITQ_API int fitq_nf4_gemv_swiglu(const fitq_gemv_job* jobs, const void* x, int64_t m, void* act,
+                                  void* workspace, size_t workspace_bytes, fitq_stream_t stream);
+
 /* c[M,N] (bf16) = a[M,K].b[N,K]^T (+ c_add) on the tcgen05 tensor cores,
  * fp32 accumulation.  K % 64 == 0, N % 16 == 0, rows 16-byte aligned. */
 FITQ_API int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, int64_t m,

@@ -368,3 +368,34 @@ def test_gemv_grouped(cuda_dev, m, shapes, nested):
     for (wref, Ad, Bd, s, bias, y_add), y in zip(jobs, outs):
         y1, _ = ops.qlora_forward(x, wref, Ad, Bd, s, gemv=True, bias=bias, y_add=y_add)
         assert float((y.float() - y1.float()).norm() / y1.float().norm()) < 1e-3
+
+
+@pytest.mark.parametrize("m,n,k,bias", [(16, 1024, 2048, False), (40, 512, 1024, True), (64, 384, 512, False),
+                                        (4, 256, 512, True)])
+def test_gemv_swiglu(cuda_dev, m, n, k, bias):
+    """fitq_nf4_gemv_swiglu (gate/up + SwiGLU in one grouped launch and one
+    finishing pass for 8 < M <= 64, the per-projection calls + the SwiGLU
+    kernel otherwise) is bit-identical to fitq_nf4_gemv_grouped followed by
+    fitq_swiglu_fwd, and within 1e-2 of the oracle's SiLU(gate) * up."""
+    from fitllm_b200 import ops
+    from fitllm_b200.layer_ops import swiglu
+    g = torch.Generator(device=cuda_dev).manual_seed(m + n)
+    x = torch.randn(m, k, generator=g, device=cuda_dev).bfloat16()
+    jobs, refs = [], []
+    for i in range(2):
+        _, wref, w_deq, _, _, _, _ = _qlora_case(m, n, k, 0, 500 + i * 11 + m, cuda_dev)
+        b = (torch.randn(n, generator=g, device=cuda_dev) * 0.1).bfloat16() if bias else None
+        jobs.append((wref, None, None, 1.0, b, None))
+        ref = x.float().cpu().numpy() @ w_deq.T
+        if b is not None:
+            ref = ref + b.float().cpu().numpy()
+        refs.append(ref)
+    act = ops.nf4_gemv_swiglu(x, jobs[0], jobs[1])
+    gate, up = ops.nf4_gemv_grouped(x, jobs)
+    act2 = swiglu(gate, up)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert torch.equal(act, act2)
+    ga, ua = refs
+    ref = ga / (1.0 + np.exp(-ga)) * ua
+    assert onf4.rel_err(act.float().cpu().numpy(), ref) < REL_TOL
