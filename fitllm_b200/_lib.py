@@ -49,6 +49,7 @@ SIGNATURES = {
     "fitq_version": (ctypes.c_char_p, []),
     "fitq_last_error": (ctypes.c_char_p, []),
     "fitq_get_device_status": (I32, [I32, P]),
+    "fitq_selftest_wait_timeout": (I32, [ctypes.c_uint64, P, P]),
     "fitq_nf4_dequant": (I32, [WP, P, I32, I32, P]),
     "fitq_nf4_quantize_workspace": (SZ, [I64, I64]),
     "fitq_nf4_quantize": (I32, [P, I64, I64, P, P, P, P, P, P, P, SZ, P]),

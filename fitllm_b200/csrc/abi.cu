@@ -221,6 +221,19 @@ int fitq_get_device_status(int reset, fitq_stream_t stream) {
   return v;
 }
 
+int fitq_selftest_wait_timeout(uint64_t limit_ns, unsigned long long* elapsed_ns,
+                               fitq_stream_t stream) {
+  int code;
+  if (current_sms(&code) == 0) return code;
+  if (limit_ns < 1000ull || limit_ns > 1000000000ull)
+    return fail(FITQ_ERR_ARG, "selftest_wait_timeout: limit_ns must be in [1e3, 1e9]");
+  int* st = status_ptr();
+  if (!st) return fail(FITQ_ERR_CUDA, "selftest_wait_timeout: no status word");
+  return launch_status(fitq::launch_selftest_wait(limit_ns, elapsed_ns, st,
+                                                  static_cast<cudaStream_t>(stream)),
+                       "selftest_wait");
+}
+
 int fitq_nf4_dequant(const fitq_nf4_weight* w, void* out, int out_dtype, int transpose,
                      fitq_stream_t stream) {
   fitq::Nf4Args a;

@@ -74,10 +74,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed.  Returns false
-// (and records FITQ_ERR_TIMEOUT) after kWaitLimitNs, or at once when another
-// role of the kernel has already failed (*abort set).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* status) {
+// (and records FITQ_ERR_TIMEOUT) after limit_ns (kWaitLimitNs for mbar_wait),
+// or at once when another role of the kernel has already failed (*abort set).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, int* status,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   uint32_t it = 0;
@@ -85,13 +86,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((++it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         report_device_error(status, FITQ_ERR_TIMEOUT);
         *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag, int* status) {
+  return mbar_wait_for(bar, parity, abort_flag, status, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------- TMA

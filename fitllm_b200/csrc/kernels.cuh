@@ -193,6 +193,11 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
 int timing_begin(cudaStream_t st, double flops);
 // Counts kernel launches made by the library (read by fitq_launch_count).
 void note_launch();
+
+// One thread waits with mbar_wait_for on an mbarrier nothing completes; after
+// limit_ns it records FITQ_ERR_TIMEOUT in *status and returns (selftest.cu).
+int launch_selftest_wait(uint64_t limit_ns, unsigned long long* elapsed_ns, int* status,
+                         cudaStream_t st);
 // Sets the text returned by fitq_last_error() for the calling thread.
 void set_last_error(const char* msg);
 void timing_end(int slot, cudaStream_t st);

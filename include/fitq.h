@@ -100,6 +100,15 @@ FITQ_API const char* fitq_last_error(void);
  * clears it afterwards. */
 FITQ_API int fitq_get_device_status(int reset, fitq_stream_t stream);
 
+/* Self-test of the failure path of the device waits (no fault involved): one
+ * thread waits, with the bounded mbarrier wait every pipelined kernel uses,
+ * on a barrier that nothing completes; after limit_ns (1 us .. 1 s) it records
+ * FITQ_ERR_TIMEOUT in the device status word and the kernel returns, leaving
+ * the context usable.  elapsed_ns (device, optional) receives the time waited.
+ * Returns FITQ_OK once launched; read the outcome with fitq_get_device_status. */
+FITQ_API int fitq_selftest_wait_timeout(uint64_t limit_ns, unsigned long long* elapsed_ns,
+                                        fitq_stream_t stream);
+
 /* W -> out, bit-exact: absmax_b = fl(fl(nqm[code_b]*nabs[b/256]) + offset),
  * w = fl(qm[nibble]*absmax_b) rounded to nearest even into bf16 or fp16.
  * transpose = 0 writes out[N,K]; transpose = 1 writes out[K,N].

@@ -399,3 +399,28 @@ def test_gemv_swiglu(cuda_dev, m, n, k, bias):
     ga, ua = refs
     ref = ga / (1.0 + np.exp(-ga)) * ua
     assert onf4.rel_err(act.float().cpu().numpy(), ref) < REL_TOL
+
+
+def test_bounded_wait_timeout_leaves_context_usable(cuda_dev):
+    """The failure path of the device waits, without a fault: a wait on an
+    mbarrier that nothing completes runs out after its limit, records
+    FITQ_ERR_TIMEOUT in the status word and returns; the context keeps
+    working (a GEMM right after is correct) and the status clears."""
+    from fitllm_b200 import _lib, ops
+    L = _lib.load()
+    assert ops.device_status(reset=True) == 0
+    stream = torch.cuda.current_stream().cuda_stream
+    assert L.fitq_selftest_wait_timeout(0, None, stream) == 1  # FITQ_ERR_ARG: limit out of range
+    elapsed = torch.zeros(1, dtype=torch.int64, device=cuda_dev)
+    limit = 20_000_000  # 20 ms
+    assert L.fitq_selftest_wait_timeout(limit, elapsed.data_ptr(), stream) == 0
+    assert ops.device_status(reset=True) == 7  # FITQ_ERR_TIMEOUT
+    waited = int(elapsed.item())
+    assert limit <= waited < 1_000_000_000
+    assert ops.device_status() == 0
+    g = torch.Generator(device="cpu").manual_seed(3)
+    a = _bf16(torch.randn(256, 512, generator=g)).to(cuda_dev)
+    b = _bf16(torch.randn(128, 512, generator=g)).to(cuda_dev)
+    c = ops.gemm_bf16_tn(a, b)
+    assert onf4.rel_err(c.float().cpu().numpy(), (a.float() @ b.float().T).cpu().numpy()) < 4e-3
+    assert ops.device_status() == 0
