@@ -260,3 +260,58 @@ def test_shard_ranges_cover_arena():
                 assert a == min(i * chunk, total) and a == pos and a <= b <= total
                 pos = b
             assert pos == total
+
+
+def _rank_fail_main(rank, world, port, q, mode):
+    """Rank 1 fails (mode "raise": raises after joining, before the first
+    layer's all-reduce; "absent": never joins the group); rank 0 must end
+    with an error from the process group's short timeout instead of hanging."""
+    import time
+    from fitllm_b200.distributed import LoRAGradComm, init_from_env
+    from fitllm_b200.optimizer import LoRAStore
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    if rank == 1 and mode == "absent":
+        q.put((rank, "absent", 0.0))
+        return
+    t0 = time.time()
+    try:
+        init_from_env(backend="gloo", timeout_s=5.0)
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        store = LoRAStore(2, [("a", (4, 8))], "cpu")
+        comm = LoRAGradComm(store)
+        for layer in reversed(range(2)):
+            comm.allreduce_layer(layer)
+        comm.wait()
+        q.put((rank, "ok", time.time() - t0))
+    except Exception as e:  # the failure the test expects on rank 0
+        q.put((rank, type(e).__name__, time.time() - t0))
+        if rank == 1:
+            q.close()
+            q.join_thread()  # the report is sent before the abrupt exit
+            os._exit(3)  # leave without tearing the group down, like a crashed rank
+
+
+@pytest.mark.parametrize("mode", ["raise", "absent"])
+def test_failed_rank_ends_collectives_with_an_error(mode):
+    """Failure detection on the host: when one rank raises or never joins,
+    the surviving rank's group initialisation or per-layer all-reduce ends
+    with an exception within the process-group timeout (5 s here), so a
+    training job fails fast instead of hanging."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_fail_main, args=(r, 2, port, q, mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (status, t) for r, status, t in (q.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[0][0] != "ok", res
+    assert res[0][1] < 60.0, res
+    if mode == "raise":
+        assert res[1][0] == "RuntimeError"
