@@ -142,6 +142,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+      // Shared-memory descriptors of stage 0; a stage is A_BYTES / B_BYTES further
+      // (the 14-bit start-address field counts 16-byte units; shared addresses <
+      // 256 KB never carry out of it).  Built once: rebuilding two descriptors
+      // per MMA made this single issuing thread, not the tensor pipe, the
+      // bottleneck (~72% tensor activity per clock).
+      const uint64_t a_desc0 = umma_smem_desc_sw128(smem_u32(sA));
+      const uint64_t b_desc0 = umma_smem_desc_sw128(smem_u32(sB));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -154,14 +161,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+          const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage * (A_BYTES >> 4));
+          const uint64_t bd = b_desc0 + static_cast<uint64_t>(stage * (B_BYTES >> 4));
           const int nk = kb < num_kb ? BK / 16 : p.lora_k / 16;
-          for (int kk = 0; kk < nk; ++kk) {
-            umma_bf16_ss(d_tmem, umma_smem_desc_sw128(a_base + kk * 32),
-                         umma_smem_desc_sw128(b_base + kk * 32), idesc,
-                         (kb > 0 || kk > 0) ? 1u : 0u);
-          }
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes = +2 in the start-address field
+            if (kk < nk) umma_bf16_ss(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
