@@ -676,7 +676,7 @@ def main():
                               "the HBM budget, so their backward skips the recompute",
                       "value_recompute_every_layer": round(tokens / (ms_rc / 1000.0), 1),
                       "ms_per_step_recompute_every_layer": round(ms_rc, 3)},
-        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn (tcgen05; the cta_group::2 kernel on these shapes)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn (tcgen05: the cta_group::2 pair kernel, the one-CTA kernel for K >= 4N)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if achieved else None,
                      "peak_source": peak_src, "traffic": None,

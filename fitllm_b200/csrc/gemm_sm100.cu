@@ -27,7 +27,7 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
-constexpr int GROUP_M = 8;
+constexpr int GROUP_M = 16;  // M-tiles (128 rows) per raster group
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 256;
 
 struct Params {
@@ -358,9 +358,13 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms) {
   } else if (v && v[0] == '2') {
     pair = true;
   } else {
-    // pair tiles: enough of them for ~4 waves of 74 clusters
+    // Pair tiles need enough of them for ~4 waves of 74 clusters.  Shapes with
+    // K >= 4N (down_proj forward, gate/up dX: N = 5120, K = 27648) run faster
+    // on the one-CTA kernel under the 1 kW power cap (measured at M = 32,768:
+    // 1.23 vs 1.13 PFLOP/s), the others on the pair kernel (gate/up forward
+    // 1.25 vs 1.24, q 1.23 vs 1.19, k/v 1.21 vs 1.16).
     const int64_t tiles2 = ((g.m + 255) / 256) * ((g.n + 255) / 256);
-    pair = tiles2 >= 4 * static_cast<int64_t>(num_sms / 2);
+    pair = tiles2 >= 4 * static_cast<int64_t>(num_sms / 2) && g.k < 4 * g.n;
   }
   return pair ? launch_gemm_bf16_tn_2cta(g, st, num_sms) : launch_gemm_bf16_tn(g, st, num_sms);
 }
