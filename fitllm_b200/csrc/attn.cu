@@ -37,7 +37,11 @@ constexpr int kAttRowBytes = kAttD * 2;                 // 256 B per Q / K / V r
 constexpr int kAttKV = kAttTile * kAttRowBytes;         // 16 KB per K or V tile
 constexpr int kAttQ = kAttRows * kAttRowBytes;          // 8 KB
 constexpr int kAttP = kAttRows * kAttTile * 2;          // 4 KB
-constexpr int kAttSmem = kAttQ + 4 * kAttKV + kAttP + 2 * 4 * kAttRows * 4;  // 77 KB
+// P lives in the K tile it was computed from (every warp is past S = Q.K^T
+// when P is written, and the tile is reloaded only after P.V): 73 KB, so
+// three CTAs fit per SM.
+constexpr int kAttSmem = kAttQ + 4 * kAttKV + 2 * 4 * kAttRows * 4;  // 73 KB
+static_assert(kAttP <= kAttKV, "P must fit in a K tile");
 constexpr float kMaskedMax = -1.0e30f;
 
 extern __shared__ __align__(128) uint8_t g_att_smem[];
@@ -92,7 +96,7 @@ struct AttParams {
   float scale_log2;        // log2(e) / sqrt(D)
 };
 
-__global__ void __launch_bounds__(kAttThreads, 2)
+__global__ void __launch_bounds__(kAttThreads, 3)
     verify_attn_kernel(const AttParams p) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -100,8 +104,7 @@ __global__ void __launch_bounds__(kAttThreads, 2)
   const uint32_t s_q = smem_u32(g_att_smem);
   const uint32_t s_k = s_q + kAttQ;              // two K tiles, then two V tiles
   const uint32_t s_v = s_k + 2 * kAttKV;
-  const uint32_t s_p = s_v + 2 * kAttKV;
-  float* red_max = reinterpret_cast<float*>(g_att_smem + kAttQ + 4 * kAttKV + kAttP);
+  float* red_max = reinterpret_cast<float*>(g_att_smem + kAttQ + 4 * kAttKV);
   float* red_sum = red_max + 4 * kAttRows;
 
   const int tile0 = split * p.tiles_per_split;
@@ -157,6 +160,7 @@ __global__ void __launch_bounds__(kAttThreads, 2)
     if (t + 1 < tile1) load_tile(t + 1, buf ^ 1);
     cp_commit();
     const uint32_t kb = s_k + buf * kAttKV, vb = s_v + buf * kAttKV;
+    const uint32_t s_p = kb;  // P of this tile overwrites its K once S is done
     const int pos0 = t * kAttTile;
 
     // ---- S = Q.K^T for positions 16 warp .. + 15 (two n8 tiles), all rows
