@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(kAttThreads, 3)
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, qd = lane & 3;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the cache append come from the previous kernel
   const uint32_t s_q = smem_u32(g_att_smem);
   const uint32_t s_k = s_q + kAttQ;              // two K tiles, then two V tiles
   const uint32_t s_v = s_k + 2 * kAttKV;
@@ -307,6 +309,8 @@ __global__ void __launch_bounds__(kAttD)
                                __nv_bfloat16* __restrict__ out, int H, int KVH, int T, int G,
                                int splits) {
   const int row = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // the split partials
   const int64_t base = (static_cast<int64_t>(b) * KVH + kvh) * splits;
   float mx = kMaskedMax;
   for (int s = 0; s < splits; ++s) mx = fmaxf(mx, ml_part[((base + s) * kAttRows + row) * 2]);
@@ -395,13 +399,15 @@ int launch_verify_attention(const void* q, const void* k_cache, const void* v_ca
       return FITQ_ERR_CUDA;
     attr = true;
   }
-  verify_attn_kernel<<<dim3(splits, kv_heads, static_cast<unsigned>(batch)), kAttThreads, kAttSmem,
-                       st>>>(p);
+  cudaError_t e = launch_pdl(verify_attn_kernel, dim3(splits, kv_heads, static_cast<unsigned>(batch)),
+                             dim3(kAttThreads), kAttSmem, st, p);
   note_launch();
-  verify_attn_combine_kernel<<<dim3(p.rows, kv_heads, static_cast<unsigned>(batch)), kAttD, 0, st>>>(
-      p.o_part, p.ml_part, static_cast<__nv_bfloat16*>(out), heads, kv_heads, t_new, p.G, splits);
+  if (e != cudaSuccess) return FITQ_ERR_CUDA;
+  e = launch_pdl(verify_attn_combine_kernel, dim3(p.rows, kv_heads, static_cast<unsigned>(batch)), dim3(kAttD),
+                 0, st, static_cast<const float*>(p.o_part), static_cast<const float*>(p.ml_part),
+                 static_cast<__nv_bfloat16*>(out), heads, kv_heads, t_new, p.G, splits);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 }  // namespace fitq

@@ -61,6 +61,8 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_fwd_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     __nv_bfloat16* __restrict__ y, int64_t cols, float eps) {
   __shared__ float red[kRowThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait();  // x comes from the previous kernel
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * cols;
   float ss[1] = {0.f};
@@ -171,6 +173,8 @@ __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ q, const __
                                    __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                    const float* __restrict__ cs, const float* __restrict__ sn, int64_t rows,
                                    int T, int H, int KVH, int dim, int prefix, int cap) {
+  pdl_launch_dependents();
+  pdl_wait();  // q/k/v come from the previous kernel
   const int half = dim / 2;
   const int groups = half / 8;
   const int slots = H + 2 * KVH;
@@ -267,11 +271,12 @@ int grid_1d(int64_t work, int num_sms) {
 
 int launch_rmsnorm_fwd(const void* x, const void* w, void* y, int64_t rows, int64_t cols,
                        float eps, cudaStream_t st) {
-  rmsnorm_fwd_kernel<<<static_cast<unsigned>(rows), kRowThreads, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
-      static_cast<__nv_bfloat16*>(y), cols, eps);
+  const cudaError_t e = launch_pdl(rmsnorm_fwd_kernel, dim3(static_cast<unsigned>(rows)), dim3(kRowThreads), 0,
+                                   st, static_cast<const __nv_bfloat16*>(x),
+                                   static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
+                                   cols, eps);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 int launch_rmsnorm_bwd(const void* dy, const void* x, const void* w, void* dx, int64_t rows,
@@ -304,12 +309,13 @@ int launch_rope_append(const void* q, const void* k, const void* v, void* q_out,
                        int num_sms) {
   const int64_t rows = batch * t_new;
   const int64_t work = rows * (heads + 2 * kv_heads) * (dim / 16);
-  rope_append_kernel<<<grid_1d(work, num_sms), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-      static_cast<const __nv_bfloat16*>(v), static_cast<__nv_bfloat16*>(q_out),
-      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), cs, sn, rows, t_new,
-      heads, kv_heads, dim, prefix, cap);
+  const cudaError_t e = launch_pdl(
+      rope_append_kernel, dim3(grid_1d(work, num_sms)), dim3(256), 0, st, static_cast<const __nv_bfloat16*>(q),
+      static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
+      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+      static_cast<__nv_bfloat16*>(v_cache), cs, sn, rows, t_new, heads, kv_heads, dim, prefix, cap);
   note_launch();
+  if (e != cudaSuccess) return FITQ_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
