@@ -21,7 +21,7 @@ order (tested).
 """
 from __future__ import annotations
 
-from typing import Callable, List, Sequence
+from typing import Callable, List, Optional, Sequence
 
 import torch
 
@@ -40,7 +40,7 @@ class HostBatchPipeline:
         self.bufs = [[torch.empty(t.shape, dtype=t.dtype, device=self.device) for t in templates]
                      for _ in range(depth)]
         self.ready = [torch.cuda.Event() for _ in range(depth)]
-        self.free: List[torch.cuda.Event] = [None] * depth
+        self.free: List[Optional[torch.cuda.Event]] = [None] * depth
         self.h2d_bytes = 0
         self.d2h_bytes = 0
 
