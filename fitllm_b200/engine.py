@@ -86,10 +86,14 @@ def lora_entries(layer: DecoderLayer):
 class ShardStationaryEngine:
     def __init__(self, cfg: LayerConfig, scheduler: ShardScheduler, store: LoRAStore, device,
                  comm: Optional[LoRAGradComm] = None, mb_chunk: Optional[int] = None,
-                 keep_activations="auto", keep_budget_fraction: float = 0.6):
+                 keep_activations="auto", keep_budget_fraction: float = 0.75):
         """keep_activations: "auto" (as many trailing layers as fit in
         keep_budget_fraction of the free HBM), an int (that many trailing
-        layers) or 0 (recompute every layer, the reference behaviour)."""
+        layers) or 0 (recompute every layer, the reference behaviour).
+        The estimate per layer (saved_bytes_per_token) is ~8% below what
+        autograd keeps; at 0.78 the 64-layer, 16 x 1024-token step kept 56
+        layers and peaked at 163 GB of a 191.5 GB B200, so 0.75 leaves room
+        for the backward's temporaries."""
         self.keep_activations = keep_activations
         self.keep_budget_fraction = keep_budget_fraction
         self._graphs: Dict[int, tuple] = {}
