@@ -146,71 +146,106 @@ __global__ void lora_rowproj_finish_kernel(const float* __restrict__ partial, in
 }
 
 // Partial row reduction:  partial[chunk][j][d] = sum_{m in chunk} p[m][j0+j] * in[m][d]
-// for a 16-wide group of adapter columns j0 = 16*blockIdx.z.  CTA = 8 warps
-// over one 256-column tile of D (8 columns per lane); warps take rows
-// m = first + warp + 8i and are combined in shared memory in warp order.
-__global__ void __launch_bounds__(256) lora_colproj_kernel(
+// for a 16-wide group of adapter columns j0 = 16*blockIdx.z, one 256-column
+// tile of D per CTA, on the tensor cores: per 16-row step,
+// D[j][d] += P^T[j][m] . X[m][d] with mma.sync m16n8k16 (j = the 16 adapter
+// columns, m = the reduced rows, d = 8 columns per n-tile).  Both operands
+// are staged in shared memory 32 rows at a time (cp.async double buffer,
+// rows past the chunk zero-filled) and read with ldmatrix.trans, which hands
+// each thread the pairs along m the fragments need.  Warp w owns columns
+// [32w, 32w + 32) of the 256-column tile, so no cross-warp reduction: every
+// output is one warp's sum over the chunk's rows in order (deterministic).
+// x rows: 512 B, 16-byte chunk c of row r stored at c ^ (r & 7); p rows: 32 B,
+// half h of row r at h ^ ((r >> 2) & 1) -- both conflict-free for ldmatrix.
+__device__ __forceinline__ void cp16_zfill(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                            uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+constexpr int kCpRows = 32;  // rows per staged tile
+
+__global__ void __launch_bounds__(256) lora_colproj_mma_kernel(
     const __nv_bfloat16* __restrict__ p_pad, int64_t ld_p, const __nv_bfloat16* __restrict__ in,
     int64_t ld, int64_t M, int64_t D, int64_t rows_per_chunk, int R, float* __restrict__ partial) {
-  __shared__ float red[16][256];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t d0 = static_cast<int64_t>(blockIdx.x) * 256 + lane * 8;
+  __shared__ __align__(128) uint8_t xs[2][kCpRows * 512];
+  __shared__ __align__(128) uint8_t ps[2][kCpRows * 32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t dt0 = static_cast<int64_t>(blockIdx.x) * 256;
   const int64_t chunk = blockIdx.y;
   const int j0 = blockIdx.z * 16;
   const int64_t mb = chunk * rows_per_chunk;
   const int64_t me = mb + rows_per_chunk < M ? mb + rows_per_chunk : M;
-  float acc[16][8];
+
+  auto load_tile = [&](int64_t mt, int buf) {
+    const uint32_t xb = smem_u32(xs[buf]), pb = smem_u32(ps[buf]);
 #pragma unroll
-  for (int j = 0; j < 16; ++j)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[j][c] = 0.f;
-  const bool col_ok = d0 < D;
-  for (int64_t m = mb + warp; m < me; m += 8) {
-    float xv[8];
-    if (col_ok) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(in + m * ld + d0));
-      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = unpack_bf16x2(w4[i]);
-        xv[2 * i] = f.x;
-        xv[2 * i + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) xv[i] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const int c = tid + 256 * i, row = c >> 5, cc = c & 31;
+      const int64_t m = mt + row, d = dt0 + cc * 8;
+      const bool ok = m < me && d < D;
+      cp16_zfill(xb + row * 512 + ((cc ^ (row & 7)) << 4), ok ? in + m * ld + d : in, ok ? 16u : 0u);
     }
-    const uint4 pa = __ldg(reinterpret_cast<const uint4*>(p_pad + m * ld_p + j0));
-    const uint4 pb = __ldg(reinterpret_cast<const uint4*>(p_pad + m * ld_p + j0 + 8));
-    const uint32_t pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+    if (tid < 2 * kCpRows) {
+      const int row = tid >> 1, h = tid & 1;
+      const int64_t m = mt + row;
+      const bool ok = m < me;
+      cp16_zfill(pb + row * 32 + ((h ^ ((row >> 2) & 1)) << 4), ok ? p_pad + m * ld_p + j0 + 8 * h : p_pad,
+                 ok ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float acc[4][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float2 f = unpack_bf16x2(pw[i]);
+  for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        acc[2 * i][c] = fmaf(f.x, xv[c], acc[2 * i][c]);
-        acc[2 * i + 1][c] = fmaf(f.y, xv[c], acc[2 * i + 1][c]);
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+
+  const int mat = lane >> 3, r8 = lane & 7;
+  int buf = 0;
+  if (mb < me) load_tile(mb, 0);
+  for (int64_t mt = mb; mt < me; mt += kCpRows, buf ^= 1) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // tile mt visible; every warp is done with the other buffer
+    if (mt + kCpRows < me) load_tile(mt + kCpRows, buf ^ 1);
+    const uint32_t xb = smem_u32(xs[buf]), pb = smem_u32(ps[buf]);
+#pragma unroll
+    for (int ks = 0; ks < kCpRows / 16; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      {
+        // A = P^T: matrices (m 0-7 | 8-15 of the step) x (j 0-7 | 8-15)
+        const int row = ks * 16 + (mat >> 1) * 8 + r8, h = mat & 1;
+        ldsm4_trans(pb + row * 32 + ((h ^ ((row >> 2) & 1)) << 4), a0, a1, a2, a3);
       }
+      uint32_t b[4][2];
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        // B = X: matrices (m 0-7 | 8-15) x (n-tiles 2np, 2np + 1)
+        const int row = ks * 16 + (mat & 1) * 8 + r8;
+        const int cc = 4 * warp + 2 * np + (mat >> 1);
+        ldsm4_trans(xb + row * 512 + ((cc ^ (row & 7)) << 4), b[2 * np][0], b[2 * np][1],
+                    b[2 * np + 1][0], b[2 * np + 1][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_bf16_16816(acc[nt], a0, a1, a2, a3, b[nt][0], b[nt][1]);
     }
   }
-  // Fixed-order combination of the 8 warps.
-  for (int w = 0; w < 8; ++w) {
-    if (warp == w) {
+  // partial[chunk][j0 + j][d]: rows g / g + 8, columns 2q, 2q + 1 of each n-tile
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float& r = red[j][lane * 8 + c];
-          r = (w == 0) ? acc[j][c] : r + acc[j][c];
-        }
+  for (int nt = 0; nt < 4; ++nt) {
+    const int64_t d = dt0 + 32 * warp + 8 * nt + 2 * q;
+    if (d < D) {
+      *reinterpret_cast<float2*>(partial + (chunk * R + j0 + g) * D + d) = make_float2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<float2*>(partial + (chunk * R + j0 + g + 8) * D + d) =
+          make_float2(acc[nt][2], acc[nt][3]);
     }
-    __syncthreads();
-  }
-  // write partial[chunk][j0 + j][d]
-  for (int e = threadIdx.x; e < 16 * 256; e += 256) {
-    const int j = e / 256, c = e % 256;
-    const int64_t d = static_cast<int64_t>(blockIdx.x) * 256 + c;
-    if (d < D) partial[(chunk * R + j0 + j) * D + d] = red[j][c];
   }
 }
 
@@ -451,9 +486,9 @@ int launch_lora_colproj(const void* p_pad, int64_t ld_p, const void* in, int64_t
   colproj_geometry(M, D, num_sms, &rpc, &nch);
   dim3 grid(static_cast<unsigned>((D + 255) / 256), static_cast<unsigned>(nch),
             static_cast<unsigned>(r / 16));
-  lora_colproj_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p_pad), ld_p,
-                                            static_cast<const __nv_bfloat16*>(in), ld_in, M, D,
-                                            rpc, r, partial_ws);
+  lora_colproj_mma_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p_pad), ld_p,
+                                                static_cast<const __nv_bfloat16*>(in), ld_in, M, D,
+                                                rpc, r, partial_ws);
   note_launch();
   lora_colproj_finish_kernel<<<grid_for(static_cast<int64_t>(r) * D, 256, num_sms), 256, 0, st>>>(
       partial_ws, nch, r, D, scale, res, layout, accumulate);
