@@ -359,7 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       after + static_cast<uint32_t>(n_ring > n_slack ? n_ring - n_slack : 0) * kDecStage;
   float4* const red = reinterpret_cast<float4*>(g_gemv_smem + (red_addr - sbase));
   const int red_warp = 8 * qn;  // float4 slots per warp and tile
-  const uint32_t sc_addr = red_addr + static_cast<uint32_t>(R * kWarps * 8 * 4 * 16);  // 256 B per warp
+  // two rounds of reduction slots: the k-parts are summed every second round
+  const uint32_t sc_addr = red_addr + static_cast<uint32_t>(2 * R * kWarps * 8 * 4 * 16);  // 256 B per warp
 
   // ring stages of this warp
   uint32_t stage[R];
@@ -462,12 +463,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_scales(sb[r], nq_base, sel_q, w.offset, sc_w, sc_lane, g, am_a, am_b);
         o = compute_tile(stage[r], frag, am_a, am_b, xr, lb);
       }
-      if (q < qn) red[(r * kWarps + warp) * red_warp + (g << pl.lqn) + q] = o;
+      if (q < qn) red[((r + R * (rd & 1)) * kWarps + warp) * red_warp + (g << pl.lqn) + q] = o;
     }
+    if ((rd & 1) == 0 && rd + 1 < rounds) continue;  // CTA-uniform: reduce two rounds at once
     __syncthreads();
-    // sum the kw parts of each tile of the round in k order; slot f = (g*qn + q)*4 + component
+    // sum the kw parts of each tile of rounds rd0..rd in k order; slot f = (g*qn + q)*4 + component
+    const int rd0 = rd & ~1;
     const int fbits = 5 + pl.lqn;
-    const int outs = (R << pl.lrtg) << fbits;
+    const int outs = (((rd - rd0 + 1) * R) << pl.lrtg) << fbits;
     const float* rf = reinterpret_cast<const float*>(red);
     for (int e = threadIdx.x; e < outs; e += kThreads) {
       const int f = e & ((1 << fbits) - 1), hi = e >> fbits;
@@ -475,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ls = f >> 2, comp = f & 3;
       const int rr = (ls >> pl.lqn) + 8 * (comp >> 1);
       const int tk = 2 * (ls & (qn - 1)) + (comp & 1);
-      const int t = j + pl.cs * (rgo + ((rd * R + r) << pl.lrtg));
+      const int t = j + pl.cs * (rgo + ((rd0 * R + r) << pl.lrtg));
       if (tk >= M || t >= T) continue;
       const float* srcf = rf + (((r * kWarps + (rgo << pl.lkw)) * red_warp) << 2) + f;
       float s = 0.f;
@@ -483,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (out.partial == nullptr) dec_store(out, nullptr, N, tk, t * 16 + rr, s);
       else out.partial[(static_cast<int64_t>(slice) * M + tk) * N + t * 16 + rr] = s;
     }
-    __syncthreads();  // reduction area rewritten next round
+    __syncthreads();  // reduction area rewritten from the next round on
   }
   cp_async_wait<0>();
 }
