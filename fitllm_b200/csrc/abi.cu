@@ -298,6 +298,8 @@ size_t fitq_qlora_fwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank
   return plan_fwd(c, m, n_out, k_in, rank, sms_for_sizing(), &p);
 }
 
+}  // extern "C"
+
 static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
                           const float* lora_b, int rank, float scale, const void* bias, void* y,
                           const void* y_add,
@@ -382,6 +384,20 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   g.status = status_ptr();
   return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm");
 }
+
+namespace fitq {
+// fitq_nf4_gemv over a caller-chosen scratch (the no-allocation entry point
+// passes its fixed device array): same checks, plan and launches.
+int nf4_gemv_on_scratch(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                        const float* lora_b, int rank, float scale, const void* bias, void* y,
+                        const void* y_add, void* scratch, size_t scratch_bytes,
+                        fitq_stream_t stream) {
+  return qlora_fwd_impl(w, x, m, lora_a, lora_b, rank, scale, bias, y, y_add, nullptr, scratch,
+                        scratch_bytes, stream, 1);
+}
+}  // namespace fitq
+
+extern "C" {
 
 int fitq_qlora_fwd(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
                    const float* lora_b, int rank, float scale, const void* bias, void* y,

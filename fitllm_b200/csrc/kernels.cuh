@@ -5,6 +5,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "../../include/fitq.h"
+
 namespace fitq {
 
 constexpr int64_t kOffsetChunk = 4096;  // absmax mean: double sum per chunk, then chunks in order
@@ -200,6 +202,11 @@ int launch_selftest_wait(uint64_t limit_ns, unsigned long long* elapsed_ns, int*
                          cudaStream_t st);
 // Sets the text returned by fitq_last_error() for the calling thread.
 void set_last_error(const char* msg);
+// fitq_nf4_gemv with the given scratch in place of a caller workspace (abi.cu).
+int nf4_gemv_on_scratch(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
+                        const float* lora_b, int rank, float scale, const void* bias, void* y,
+                        const void* y_add, void* scratch, size_t scratch_bytes,
+                        fitq_stream_t stream);
 void timing_end(int slot, cudaStream_t st);
 
 // Decoder-layer row / elementwise kernels (layer_ops.cu).

@@ -299,10 +299,11 @@ FITQ_API long long fitq_launch_count(void);
  * device allocation up front: they pass the inputs and outputs they hold, and
  * the scratch comes from one fixed array of FITQ_GEMV_NOALLOC_SCRATCH_BYTES
  * (8 MiB) built into the library, which every GPU that loads the library
- * keeps until the process exits.  Same arguments and arithmetic as
- * fitq_nf4_gemv (M <= 64, N % 64 == 0, K % 256 == 0, rank 0/16/32/48/64);
- * shapes whose scratch exceeds the array return FITQ_ERR_WORKSPACE with the
- * needed size in fitq_last_error().  The first call on a device looks up the
+ * keeps until the process exits.  Same arguments, checks, kernels and
+ * arithmetic as fitq_nf4_gemv (M <= 64, N % 64 == 0, K % 256 == 0, rank
+ * 0/16/32/48/64; lora_a, lora_b 16-byte aligned), so the results are
+ * bit-identical to it; shapes whose scratch exceeds the array return
+ * FITQ_ERR_WORKSPACE with the needed size in fitq_last_error().  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) with that device current, so
  * make it before any stream capture.  All calls share the array and each one
  * overwrites what it uses; calls that overlap on the GPU (two streams, two
