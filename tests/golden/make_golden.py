@@ -1,6 +1,8 @@
 """Generate the committed golden fixtures under tests/golden/.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <FitLLM checkout>
+
+(or with the checkout in the FITLLM_REFERENCE_DIR environment variable)
 
 Two kinds of fixtures:
 
@@ -119,8 +121,11 @@ def make_nf4_vectors() -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("FITLLM_REFERENCE_DIR"),
+                    help="FitLLM checkout to import (default: $FITLLM_REFERENCE_DIR)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference or set FITLLM_REFERENCE_DIR")
     torch.save(make_reference_torch(a.reference), HERE / "reference_torch.pt")
     np.savez_compressed(HERE / "nf4_vectors.npz", **make_nf4_vectors())
     print("wrote", HERE / "reference_torch.pt", HERE / "nf4_vectors.npz")
