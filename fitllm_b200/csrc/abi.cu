@@ -123,8 +123,18 @@ int launch_status(int rc, const char* what) {
   return fail(rc, "%s: launch failed (%s)", what, cudaGetErrorString(e));
 }
 
+// NF4 dequant fused into the GEMM (gemm_nf4.cu) for the training-size
+// paths; FITQ_NF4_FUSED=0 in the environment selects the materialised
+// dequant + bf16 GEMM instead.
+bool use_fused_gemm(int64_t n_out, int64_t k_in, int trans) {
+  const char* e = getenv("FITQ_NF4_FUSED");
+  if (e != nullptr && e[0] == '0') return false;
+  return fitq::gemm_nf4_shape_ok(n_out, k_in, trans);
+}
+
 // Workspace layout of the forward (shared by the size query and the call).
 struct FwdPlan {
+  bool fused;      // NF4 decoded inside the GEMM (no wdeq)
   bool gemv;       // M <= 64 skinny path
   bool dec;        // M <= 8 single-launch decode kernel
   bool tc;         // M <= 64 tcgen05 skinny GEMM (weights decoded into TMEM)
@@ -156,13 +166,15 @@ size_t plan_fwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, int sms, Fw
     p->partial = static_cast<float*>(c.take(fitq::gemv_partial_bytes(m, n, k, sms, nullptr)));
     if (rank > 0) p->t_part = static_cast<float*>(c.take(fitq::lora_rowproj_small_workspace(m, k, rank)));
   } else {
-    p->wdeq = c.take(bf16_bytes(n * k));
+    p->fused = use_fused_gemm(n, k, 0);
+    if (!p->fused) p->wdeq = c.take(bf16_bytes(n * k));
     if (rank > 0) p->b_pad = c.take(bf16_bytes(n * 64));
   }
   return c.used;
 }
 
 struct BwdPlan {
+  bool fused;     // dX GEMM decodes W itself (no wt)
   void* wt;       // bf16 [K,N]  transposed dequant
   void* a_bf16;   // bf16 [r,K]  (T recompute)
   void* t_pad;    // bf16 [M,64] (T recompute)
@@ -175,7 +187,8 @@ struct BwdPlan {
 size_t plan_bwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, bool need_dx, bool need_t,
                 int sms, BwdPlan* p) {
   *p = BwdPlan{};
-  if (need_dx) p->wt = c.take(bf16_bytes(n * k));
+  p->fused = need_dx && use_fused_gemm(n, k, 1);
+  if (need_dx && !p->fused) p->wt = c.take(bf16_bytes(n * k));
   if (rank > 0) {
     if (need_t) {
       p->a_bf16 = c.take(bf16_bytes(static_cast<int64_t>(rank) * k));
@@ -366,12 +379,25 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
                                   y_add, y, st, sms);
     return launch_status(rc, "nf4_gemv finish");
   }
-  rc = fitq::launch_nf4_dequant(a, p.wdeq, FITQ_DTYPE_BF16, 0, st, sms);
-  if (rc) return launch_status(rc, "nf4_dequant");
   if (rank > 0) {
     rc = fitq::launch_pad_lora_weight(lora_b, N, rank, scale, 0, p.b_pad, st);
     if (rc) return launch_status(rc, "lora B pad");
   }
+  if (p.fused) {
+    fitq::Nf4GemmArgs g{};
+    g.w = a; g.trans = 0;
+    g.a = x; g.lda = K;
+    g.pa = p.t_pad; g.pb = p.b_pad;
+    g.c = y; g.ldc = N;
+    g.c_add = y_add; g.ldc_add = N;
+    g.bias = bias;
+    g.m = m;
+    g.lora_k = rank;
+    g.status = status_ptr();
+    return launch_status(fitq::launch_gemm_nf4(g, st, sms), "tcgen05 nf4 gemm");
+  }
+  rc = fitq::launch_nf4_dequant(a, p.wdeq, FITQ_DTYPE_BF16, 0, st, sms);
+  if (rc) return launch_status(rc, "nf4_dequant");
   fitq::GemmArgs g{};
   g.a = x; g.lda = K;
   g.b = p.wdeq; g.ldb = K;
@@ -629,13 +655,26 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
     if (rc) return launch_status(rc, "lora dA");
   }
   if (!need_dx) return FITQ_OK;
-  // dx[M, K] = dy[M, N].W[N, K] + U.(s.A): W^T materialised [K, N] bf16 (bit-exact dequant).
-  rc = fitq::launch_nf4_dequant(a, p.wt, FITQ_DTYPE_BF16, 1, st, sms);
-  if (rc) return launch_status(rc, "nf4_dequant (transposed)");
+  // dx[M, K] = dy[M, N].W[N, K] + U.(s.A), W decoded inside the GEMM, or
+  // W^T materialised [K, N] bf16 first (bit-exact dequant either way).
   if (rank > 0) {
     rc = fitq::launch_pad_lora_weight(lora_a, K, rank, scale, 1, p.at_pad, st);
     if (rc) return launch_status(rc, "lora A^T pad");
   }
+  if (p.fused) {
+    fitq::Nf4GemmArgs g{};
+    g.w = a; g.trans = 1;
+    g.a = dy; g.lda = N;
+    g.pa = p.u_pad; g.pb = p.at_pad;
+    g.c = dx; g.ldc = K;
+    g.c_add = dx_accumulate ? dx : nullptr; g.ldc_add = K;
+    g.m = m;
+    g.lora_k = rank;
+    g.status = status_ptr();
+    return launch_status(fitq::launch_gemm_nf4(g, st, sms), "tcgen05 nf4 gemm (dx)");
+  }
+  rc = fitq::launch_nf4_dequant(a, p.wt, FITQ_DTYPE_BF16, 1, st, sms);
+  if (rc) return launch_status(rc, "nf4_dequant (transposed)");
   fitq::GemmArgs g{};
   g.a = dy; g.lda = N;
   g.b = p.wt; g.ldb = N;

@@ -52,6 +52,33 @@ int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms);
 // (FITQ_GEMM_VARIANT=1cta|2cta in the environment forces one).
 int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms);
 
+// NF4 dequant fused into the tcgen05 GEMM (gemm_nf4.cu): the weight operand
+// is decoded bit-exactly from the packed codes into shared memory.
+//   trans = 0: C[m, N_w] = A[m, K_w] . W_deq^T   (A = x, forward)
+//   trans = 1: C[m, K_w] = A[m, N_w] . W_deq     (A = dy, input gradient)
+// plus the LoRA K-block pa[m, r] . pb[cols, r]^T (bf16, pitch 64) and the
+// bias / residual epilogue of GemmArgs.  Needs the GEMM's output columns % 128
+// == 0 and its reduction % 64 == 0 (gemm_nf4_shape_ok).
+struct Nf4GemmArgs {
+  Nf4Args w;
+  int trans;
+  const void* a; int64_t lda;
+  const void* pa;
+  const void* pb;
+  void* c; int64_t ldc;
+  const void* c_add; int64_t ldc_add;
+  const void* bias;
+  int64_t m;
+  int lora_k;
+  int* status;
+};
+inline bool gemm_nf4_shape_ok(int64_t n_out, int64_t k_in, int trans) {
+  const int64_t cols = trans ? k_in : n_out, red = trans ? n_out : k_in;
+  return cols % 128 == 0 && red % 64 == 0 && k_in % 64 == 0;
+}
+bool gemm_nf4_supported(const Nf4Args& w, int trans);
+int launch_gemm_nf4(const Nf4GemmArgs& g, cudaStream_t st, int num_sms);
+
 // LoRA building blocks (lora.cu).
 // out[M, r] = in[M, D] . wt[r, D]^T  (bf16 in, fp32 accumulate); written as
 // bf16 into out_pad (row pitch 64; columns r..63 are left untouched and never

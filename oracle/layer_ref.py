@@ -57,11 +57,13 @@ def _rms(x, eps=1e-6):
     return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
 
 
-def _rope(seq, head_dim, theta=1e6):
+def _rope(seq, head_dim, theta=1e6, device=None, dtype=torch.float32):
+    """HF rotary tables (cos, sin) [S, head_dim], computed in fp32 and cast to
+    the activations' dtype (as Qwen2RotaryEmbedding returns them)."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
     f = torch.outer(torch.arange(seq, dtype=torch.float32), inv)
     e = torch.cat([f, f], -1)
-    return e.cos(), e.sin()
+    return e.cos().to(device, dtype), e.sin().to(device, dtype)
 
 
 def _rot(x):
@@ -70,6 +72,9 @@ def _rot(x):
 
 
 def layer_forward(w, h):
+    """One decoder layer in the dtype and on the device of h and w (fp32 on
+    the host cores for the oracle; bf16 on a GPU restates the reference's own
+    precision: bf16 activations, fp32-accumulating matmuls)."""
     hidden, heads, kv_heads, head_dim, inter = [int(v) for v in w["cfg"]]
     s = float(w["scale"])
     b, S, _ = h.shape
@@ -86,7 +91,7 @@ def layer_forward(w, h):
     q = lin("q_proj", x).view(b, S, heads, head_dim).transpose(1, 2)
     k = lin("k_proj", x).view(b, S, kv_heads, head_dim).transpose(1, 2)
     v = lin("v_proj", x).view(b, S, kv_heads, head_dim).transpose(1, 2)
-    cos, sin = _rope(S, head_dim)
+    cos, sin = _rope(S, head_dim, device=h.device, dtype=h.dtype)
     q, k = q * cos + _rot(q) * sin, k * cos + _rot(k) * sin
     o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
     h1 = h + lin("o_proj", o.transpose(1, 2).reshape(b, S, heads * head_dim))

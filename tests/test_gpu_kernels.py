@@ -116,9 +116,16 @@ def _qlora_case(m, n, k, r, seed, dev):
 
 @pytest.mark.parametrize("m,n,k,r", [(512, 256, 512, 16), (200, 512, 256, 16), (130, 128, 128, 32),
                                      (384, 1024, 640, 64), (256, 320, 256, 0)])
-@pytest.mark.parametrize("variant", ["1cta", "2cta"])
+@pytest.mark.parametrize("variant", ["1cta", "2cta", "fused"])
 def test_qlora_forward_backward(cuda_dev, m, n, k, r, variant, monkeypatch):
-    monkeypatch.setenv("FITQ_GEMM_VARIANT", variant)
+    """QLoRA forward and backward on the dequant + bf16 GEMM paths (one-CTA
+    and pair kernels) and with the NF4 decode inside the GEMM ("fused"; shapes
+    it does not take fall back to the dequant path)."""
+    if variant == "fused":
+        monkeypatch.setenv("FITQ_NF4_FUSED", "1")
+    else:
+        monkeypatch.setenv("FITQ_NF4_FUSED", "0")
+        monkeypatch.setenv("FITQ_GEMM_VARIANT", variant)
     from fitllm_b200 import ops
     s = 2.0
     st, wref, w_deq, A, B, x, dy = _qlora_case(m, n, k, r, 7 + m, cuda_dev)

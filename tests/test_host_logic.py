@@ -44,7 +44,19 @@ def test_abi_rejects_bad_arguments_without_a_device():
     assert L.fitq_nf4_dequant(ctypes.byref(w2), 16, 0, 0, None) == 2  # K % 64 != 0
     assert L.fitq_gemm_bf16_tn(16, 16, 16, None, 128, 100, 64, None) == 2  # N % 16 != 0
     assert b"N % 16 == 0" in L.fitq_last_error()
-    assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) > 5120 * 5120 * 2
+    # NF4 decoded inside the GEMM: no dequantised copy of W in the workspace
+    assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) < 5120 * 5120 // 2
+    assert L.fitq_qlora_bwd_workspace(512, 5120, 5120, 16) < 5120 * 5120 // 2
+    # the dequant + bf16 GEMM path holds W (bf16) in the workspace
+    import os
+    os.environ["FITQ_NF4_FUSED"] = "0"
+    try:
+        assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) > 5120 * 5120 * 2
+        assert L.fitq_qlora_bwd_workspace(512, 5120, 5120, 16) > 5120 * 5120 * 2
+    finally:
+        del os.environ["FITQ_NF4_FUSED"]
+    # shapes the fused GEMM does not take (N % 128 != 0) keep the dequant path
+    assert L.fitq_qlora_fwd_workspace(512, 320, 256, 16) > 320 * 256 * 2
 
 
 # ---------------------------------------------------------------- reference API
