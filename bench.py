@@ -54,7 +54,7 @@ def parse():
                     help="rows,vocab: run the cross-entropy kernel on one shape and exit")
     ap.add_argument("--full-step", choices=["auto", "on", "off"], default="auto",
                     help="also time a full 64-layer step with shards streamed from pinned host "
-                         "memory (auto: on one GPU only; every rank builds the 64-layer host store)")
+                         "memory (each rank pins only its 1/N byte range of every layer)")
     return ap.parse_args()
 
 
@@ -367,6 +367,7 @@ def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, st
                     "note": "random-init model: about ln(152064) = 11.93"},
            "layers_kept_without_recompute": eng.last_kept,
            "h2d_shard_bytes_per_layer_pass_per_rank": int(h2d // layers_n),
+           "pinned_host_bytes_per_rank": sched.host_bytes(),
            "note": "each layer's shard is uploaded in the forward and again in the backward "
                    "(two-slot ring); model_tflops counts the 64 layers (2.085 PFLOP per step), "
                    "the lm_head adds 2 GEMMs of 2 x 5120 x 152064 FLOP per token"}
@@ -646,7 +647,7 @@ def main():
 
     # every rank takes part in the full-step measurement (it has collectives)
     full_step = None
-    if a.full_step == "on" or (a.full_step == "auto" and world == 1):
+    if a.full_step in ("on", "auto"):
         del eng, sched, store, opt, h0, gout
         if e2e is not None:
             del h_host, g_host, gin_host, lora_host, pipe

@@ -123,14 +123,26 @@ int launch_status(int rc, const char* what) {
   return fail(rc, "%s: launch failed (%s)", what, cudaGetErrorString(e));
 }
 
-// NF4 dequant fused into the GEMM (gemm_nf4.cu) for the training-size
-// paths; FITQ_NF4_FUSED=0 in the environment selects the materialised
-// dequant + bf16 GEMM instead.
-bool use_fused_gemm(int64_t n_out, int64_t k_in, int trans) {
+// NF4 dequant fused into the GEMM (gemm_nf4.cu, gemm_nf4_2cta.cu) or the
+// materialised dequant + bf16 GEMM, by measured throughput per shape;
+// FITQ_NF4_FUSED=1 / 0 in the environment forces one (shapes the fused
+// kernels do not take always use the dequant path).
+bool fused_faster(int64_t m, int64_t n_out, int64_t k_in, int trans) {
+  (void)m; (void)n_out; (void)k_in; (void)trans;
+  return false;
+}
+
+bool use_fused_gemm(int64_t m, int64_t n_out, int64_t k_in, int trans) {
+  if (!fitq::gemm_nf4_shape_ok(n_out, k_in, trans)) return false;
   const char* e = getenv("FITQ_NF4_FUSED");
   if (e != nullptr && e[0] == '0') return false;
-  return fitq::gemm_nf4_shape_ok(n_out, k_in, trans);
+  if (e != nullptr && e[0] == '1') return true;
+  return fused_faster(m, n_out, k_in, trans);
 }
+
+// The rank-r projections T = x.A^T and U = dy.B split the reduction over CTAs
+// when the rows alone (16 per CTA) would leave most SMs idle.
+bool rowproj_split(int64_t m, int sms) { return (m + 15) / 16 < 2 * static_cast<int64_t>(sms); }
 
 // Workspace layout of the forward (shared by the size query and the call).
 struct FwdPlan {
@@ -166,9 +178,11 @@ size_t plan_fwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, int sms, Fw
     p->partial = static_cast<float*>(c.take(fitq::gemv_partial_bytes(m, n, k, sms, nullptr)));
     if (rank > 0) p->t_part = static_cast<float*>(c.take(fitq::lora_rowproj_small_workspace(m, k, rank)));
   } else {
-    p->fused = use_fused_gemm(n, k, 0);
+    p->fused = use_fused_gemm(m, n, k, 0);
     if (!p->fused) p->wdeq = c.take(bf16_bytes(n * k));
     if (rank > 0) p->b_pad = c.take(bf16_bytes(n * 64));
+    if (rank > 0 && rowproj_split(m, sms))
+      p->t_part = static_cast<float*>(c.take(fitq::lora_rowproj_small_workspace(m, k, rank)));
   }
   return c.used;
 }
@@ -182,12 +196,13 @@ struct BwdPlan {
   void* u_pad;    // bf16 [M,64]
   void* at_pad;   // bf16 [K,64] = s.A^T
   float* partial; // colproj scratch
+  float* rp_part; // split row projection partials (few rows)
 };
 
 size_t plan_bwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, bool need_dx, bool need_t,
                 int sms, BwdPlan* p) {
   *p = BwdPlan{};
-  p->fused = need_dx && use_fused_gemm(n, k, 1);
+  p->fused = need_dx && use_fused_gemm(m, n, k, 1);
   if (need_dx && !p->fused) p->wt = c.take(bf16_bytes(n * k));
   if (rank > 0) {
     if (need_t) {
@@ -200,6 +215,11 @@ size_t plan_bwd(Carve& c, int64_t m, int64_t n, int64_t k, int rank, bool need_d
     size_t pa = fitq::lora_colproj_workspace(m, k, rank, sms);
     size_t pb = fitq::lora_colproj_workspace(m, n, rank, sms);
     p->partial = static_cast<float*>(c.take(pa > pb ? pa : pb));
+    if (rowproj_split(m, sms)) {
+      const size_t ra = need_t ? fitq::lora_rowproj_small_workspace(m, k, rank) : 0;
+      const size_t rb = fitq::lora_rowproj_small_workspace(m, n, rank);
+      p->rp_part = static_cast<float*>(c.take(ra > rb ? ra : rb));
+    }
   }
   return c.used;
 }
@@ -366,9 +386,9 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
   if (rank > 0) {
     rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
     if (rc) return launch_status(rc, "lora_a cast");
-    rc = p.gemv ? fitq::launch_lora_rowproj_small(x, K, m, K, p.a_bf16, rank, p.t_part, p.t_pad,
-                                                  t_out, st)
-                : fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
+    rc = p.t_part ? fitq::launch_lora_rowproj_small(x, K, m, K, p.a_bf16, rank, p.t_part, p.t_pad,
+                                                    t_out, st)
+                  : fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
     if (rc) return launch_status(rc, "lora T = x.A^T");
   }
   if (p.gemv) {
@@ -636,7 +656,9 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
     if (need_t) {
       rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
       if (rc) return launch_status(rc, "lora_a cast");
-      rc = fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, nullptr, st, sms);
+      rc = p.rp_part ? fitq::launch_lora_rowproj_small(x, K, m, K, p.a_bf16, rank, p.rp_part,
+                                                       p.t_pad, nullptr, st)
+                     : fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, nullptr, st, sms);
       if (rc) return launch_status(rc, "lora T recompute");
       t_ptr = p.t_pad;
       t_ld = 64;
@@ -644,7 +666,9 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
     // U = dy.B, with B^T cast to bf16 [r, N]
     rc = fitq::launch_f32_to_bf16_t(lora_b, N, rank, p.bt_bf16, st);
     if (rc) return launch_status(rc, "lora_b cast");
-    rc = fitq::launch_lora_rowproj(dy, N, m, N, p.bt_bf16, rank, p.u_pad, nullptr, st, sms);
+    rc = p.rp_part ? fitq::launch_lora_rowproj_small(dy, N, m, N, p.bt_bf16, rank, p.rp_part,
+                                                     p.u_pad, nullptr, st)
+                   : fitq::launch_lora_rowproj(dy, N, m, N, p.bt_bf16, rank, p.u_pad, nullptr, st, sms);
     if (rc) return launch_status(rc, "lora U = dy.B");
     // dB[N, r] = s.dy^T.T ; dA[r, K] = s.U^T.x
     rc = fitq::launch_lora_colproj(t_ptr, t_ld, dy, N, m, N, rank, scale, grad_b, 1,

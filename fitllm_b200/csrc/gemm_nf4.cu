@@ -11,19 +11,23 @@
 // (fitllm/forward.py:680-686) and MatMul4Bit.backward (fitllm/backward.py:234)
 // obtain it before their cuBLAS call.
 //
-// Persistent, warp-specialised CTA (448 threads, one per SM), tile 256 x 128:
-//   warp 0       TMA: the A tile (256 x 64 bf16, 128-byte swizzle) and the
-//                packed weight bytes of the stage (4 KB, unswizzled) into a
-//                4-stage ring.
+// Persistent, warp-specialised CTA (480 threads, one per SM), tile 256 x 128:
+//   warp 0       TMA of the A tile (256 x 64 bf16, 128-byte swizzle) into a
+//                4-stage ring that also holds the decoded B tiles.
+//   warp 6       TMA of the packed weight bytes (4 KB per stage, unswizzled)
+//                into their own 8-stage ring, so the codes are in shared
+//                memory long before their B slot frees up.
 //   warp 1       owns TMEM (512 columns: two buffers x two 128 x 128 fp32
 //                accumulators) and issues tcgen05.mma kind::f16 from one lane:
 //                two M = 128, N = 128 MMAs per K step share the decoded B tile,
 //                so every weight is decoded once per 256 rows of A.
 //   warps 2-5    epilogue (tcgen05.ld, bias / residual add, bf16 stores),
 //                overlapping the next tile's main loop (double-buffered TMEM).
-//   warps 6-13   decoders, two groups of four warps taking alternate stages.
-//                A thread decodes one 64-weight NF4 block of one W row per
-//                stage: it builds the block's 16-entry table of bf16 values
+//   warps 7-14   decoders, two groups of four warps taking alternate K
+//                steps; a thread decodes one 64-weight NF4 block of one W row
+//                once the slot's previous MMAs retired (its absmax inputs
+//                fetched two of its steps earlier): it builds the block's
+//                16-entry table of bf16 values
 //                bf16(fl(qm[i] * absmax)) as two byte planes of four registers,
 //                then looks up four weights per pair of prmt instructions and
 //                writes the 128-byte operand row in the 128-byte-swizzled
@@ -44,20 +48,23 @@ namespace {
 constexpr int BM = 256;  // A rows per tile: two 128-row UMMA sub-tiles
 constexpr int BN = 128;
 constexpr int BK = 64;
-constexpr int STAGES = 4;  // even: decoder group g takes the stages of parity g
+constexpr int STAGES = 4;   // A + decoded-B ring
+constexpr int PSTAGES = 8;  // packed-byte ring (runs ahead of the decoders)
 constexpr int A_BYTES = BM * BK * 2;  // 32 KB
 constexpr int B_BYTES = BN * BK * 2;  // 16 KB decoded (or the LoRA Q tile)
 constexpr int P_BYTES = BN * BK / 2;  // 4 KB packed NF4
-constexpr int NUM_DEC_WARPS = 8;
-constexpr int NUM_THREADS = (6 + NUM_DEC_WARPS) * 32;
+constexpr int NUM_DEC_WARPS = 8;      // 256 threads: half an NF4 block each per stage
+constexpr int DEC_WARP0 = 7;
+constexpr int NUM_THREADS = (DEC_WARP0 + NUM_DEC_WARPS) * 32;
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 8;  // M-tiles (256 rows) per raster group
 // MN-major operand (dX): 8 K-rows x 64 MN elements = one 1 KB swizzle atom;
 // the two MN atoms of a K group are adjacent, K groups follow each other.
 constexpr uint32_t MN_LBO = 1024;  // bytes between MN atoms
 constexpr uint32_t MN_SBO = 2048;  // bytes between 8-row K groups
-constexpr size_t SMEM_BYTES =
-    1024 /*align*/ + STAGES * (A_BYTES + B_BYTES + P_BYTES) + 256 * 4 /*nested map*/ + 256;
+constexpr size_t SMEM_BYTES = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + PSTAGES * P_BYTES +
+                               256 * 4 /*nested map*/ + 512 /*barriers*/;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Params {
   __nv_bfloat16* c;
@@ -124,6 +131,28 @@ __device__ __forceinline__ void lookup4(uint32_t h, const uint32_t (&L)[4], cons
   w23 = prmt(lo, hi, 0x6273u);  // e2 | e3 << 16
 }
 
+// Walks one decoder group's iterations (tile, kb) in order: the K steps of
+// the CTA's tiles whose running index has the group's parity, LoRA steps
+// excluded.  Used to fetch each block's absmax inputs two iterations early.
+struct DecCursor {
+  int tile, kb, it, nb;
+};
+
+__device__ __forceinline__ bool dec_next(DecCursor& c, int group, int num_tiles, int total_kb,
+                                         int num_kb, const Params& p) {
+  while (true) {
+    if (++c.kb == total_kb) {
+      c.kb = 0;
+      c.tile += gridDim.x;
+      if (c.tile >= num_tiles) return false;
+      int mb;
+      tile_coords(c.tile, p.num_m, p.num_n, p.group_m, mb, c.nb);
+    }
+    ++c.it;
+    if ((c.it & 1) == group && c.kb < num_kb) return true;
+  }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_nf4_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_p,
@@ -135,11 +164,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sP = sB + STAGES * B_BYTES;
-  float* s_nqm = reinterpret_cast<float*>(sP + STAGES * P_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_nqm + 256);
-  uint64_t* bfull = full + STAGES;
-  uint64_t* empty = bfull + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  float* s_nqm = reinterpret_cast<float*>(sP + PSTAGES * P_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_nqm + 256);  // A (or LoRA P+Q) landed
+  uint64_t* bfull = full + STAGES;                             // B decoded
+  uint64_t* empty = bfull + STAGES;                            // MMAs of the slot retired
+  uint64_t* pfull = empty + STAGES;                            // packed bytes landed
+  uint64_t* pempty = pfull + PSTAGES;                          // packed bytes read
+  uint64_t* tfull = pempty + PSTAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -152,8 +183,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bfull[s], 4);  // one arrive per warp of the stage's decoder group
+      mbar_init(&bfull[s], NUM_DEC_WARPS / 2);  // one arrive per warp of the stage's group
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&pfull[s], 1);
+      mbar_init(&pempty[s], NUM_DEC_WARPS / 2);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -187,6 +222,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int total_kb = num_kb + (p.lora_k ? 1 : 0);
 
   if (warp == 0) {
+    // ------------------------------------------------ A (and LoRA) producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -200,12 +236,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           if (kb < num_kb) {
-            mbar_arrive_expect_tx(&full[stage], A_BYTES + P_BYTES);
+            mbar_arrive_expect_tx(&full[stage], A_BYTES);
             tma_load_2d(sA + stage * A_BYTES, &tm_a, &full[stage], kb * BK, mb * BM);
-            if (p.trans)  // W rows kb*64.., bytes of W columns nb*128..
-              tma_load_2d(sP + stage * P_BYTES, &tm_p, &full[stage], nb * (BN / 2), kb * BK);
-            else  // W rows nb*128.., bytes of W columns kb*64..
-              tma_load_2d(sP + stage * P_BYTES, &tm_p, &full[stage], kb * (BK / 2), nb * BN);
           } else {
             mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
             tma_load_2d(sA + stage * A_BYTES, &tm_pa, &full[stage], 0, mb * BM);
@@ -217,6 +249,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       for (int s = 0; s < STAGES; ++s)
         if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, never, p.status);
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------ packed-byte producer
+    if (lane == 0) {
+      int ps = 0;
+      uint32_t pph = 0;
+      uint32_t armed = 0, armed_parity = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p.num_m, p.num_n, p.group_m, mb, nb);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&pempty[ps], pph ^ 1, abort_flag, p.status)) { ok = false; break; }
+          armed |= 1u << ps;
+          armed_parity = (armed_parity & ~(1u << ps)) | (pph << ps);
+          mbar_arrive_expect_tx(&pfull[ps], P_BYTES);
+          if (p.trans)  // W rows kb*64.., bytes of W columns nb*128..
+            tma_load_2d(sP + ps * P_BYTES, &tm_p, &pfull[ps], nb * (BN / 2), kb * BK);
+          else  // W rows nb*128.., bytes of W columns kb*64..
+            tma_load_2d(sP + ps * P_BYTES, &tm_p, &pfull[ps], kb * (BK / 2), nb * BN);
+          if (++ps == PSTAGES) { ps = 0; pph ^= 1; }
+        }
+        if (!ok) break;
+      }
+      for (int s = 0; s < PSTAGES; ++s)
+        if (armed & (1u << s)) mbar_wait(&pfull[s], (armed_parity >> s) & 1u, never, p.status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -235,7 +293,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t d0 = tmem_base + acc * 2 * BN;
         for (int kb = 0; kb < total_kb; ++kb) {
-          if (!mbar_wait(&bfull[stage], phase, abort_flag, p.status)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status) ||
+              !mbar_wait(&bfull[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
           const uint64_t ad = a_desc0 + static_cast<uint64_t>(stage * (A_BYTES >> 4));
           const bool lora = kb >= num_kb;
@@ -331,9 +390,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ decoders
-    const int dw = warp - 6;
-    const int group = dw >> 2;             // takes the stages of this parity
-    const int u = (dw & 3) * 32 + lane;    // unit: one 64-weight block of one W row
+    const int dw = warp - DEC_WARP0;
+    const int group = dw >> 2;           // takes the K steps of this parity
+    const int u = (dw & 3) * 32 + lane;  // unit: one 64-weight NF4 block of one W row
     float qm[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) qm[i] = __ldg(p.qm + i);
@@ -349,28 +408,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                                              (r_local & 7) * 128)
                                      : static_cast<uint32_t>(u * 128);
     const uint32_t swz = static_cast<uint32_t>(r_local & 7);
-    int it = 0;
+    const bool plain = p.absmax_f32 != nullptr;
+    // absmax inputs of this thread's block in K step (nb, kb)
+    auto block_of = [&](int nb, int kb) -> int64_t {
+      const int64_t wrow = p.trans ? (int64_t)kb * BK + r_local : (int64_t)nb * BN + u;
+      return wrow * p.w_kb + (p.trans ? nb * 2 + jb : kb);
+    };
+    auto fetch = [&](const DecCursor& c, uint32_t& code, float& scale) {
+      const int64_t b = block_of(c.nb, c.kb);
+      if (plain) {
+        code = 0;
+        scale = __ldg(p.absmax_f32 + b);
+      } else {
+        code = __ldg(p.codes + b);
+        scale = __ldg(p.nabs + (b >> 8));
+      }
+    };
+    // two-deep prefetch of the absmax inputs over this group's K steps
+    DecCursor la{static_cast<int>(blockIdx.x), -1, -1, 0};
+    {
+      int mb;
+      tile_coords(la.tile, p.num_m, p.num_n, p.group_m, mb, la.nb);
+    }
+    uint32_t code0 = 0, code1 = 0;
+    float sc0 = 0.f, sc1 = 0.f;
+    bool have0 = dec_next(la, group, num_tiles, total_kb, num_kb, p);
+    if (have0) fetch(la, code0, sc0);
+    bool have1 = have0 && dec_next(la, group, num_tiles, total_kb, num_kb, p);
+    if (have1) fetch(la, code1, sc1);
+
+    int it = 0, pit = 0;  // K steps (all), packed stages (LoRA steps excluded)
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, p.num_m, p.num_n, p.group_m, mb, nb);
       for (int kb = 0; kb < total_kb; ++kb, ++it) {
+        const bool lora = kb >= num_kb;
+        const int my_pit = pit;
+        if (!lora) ++pit;
         if ((it & 1) != group) continue;
         const int stage = it % STAGES;
         const uint32_t phase = static_cast<uint32_t>(it / STAGES) & 1u;
-        const bool lora = kb >= num_kb;
-        float am = 0.f;
+        // the B slot is free once the MMAs that read it last have retired
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
         if (!lora) {
-          const int64_t wrow = p.trans ? (int64_t)kb * BK + r_local : (int64_t)nb * BN + u;
-          const int64_t b = wrow * p.w_kb + (p.trans ? nb * 2 + jb : kb);
-          if (p.absmax_f32 != nullptr) {
-            am = __ldg(p.absmax_f32 + b);
-          } else {
-            am = __fadd_rn(__fmul_rn(s_nqm[__ldg(p.codes + b)], __ldg(p.nabs + (b >> 8))), p.offset);
+          const float am = plain ? sc0 : __fadd_rn(__fmul_rn(s_nqm[code0], sc0), p.offset);
+          code0 = code1;
+          sc0 = sc1;
+          if (have1) {
+            have1 = dec_next(la, group, num_tiles, total_kb, num_kb, p);
+            if (have1) fetch(la, code1, sc1);
           }
-        }
-        if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
-        if (!lora) {
+          const int ps = my_pit % PSTAGES;
+          const uint32_t pph = static_cast<uint32_t>(my_pit / PSTAGES) & 1u;
+          if (!mbar_wait(&pfull[ps], pph, abort_flag, p.status)) { ok = false; break; }
+          const uint8_t* src = sP + ps * P_BYTES + src_off;
+          const uint4 q0 = *reinterpret_cast<const uint4*>(src);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(src + 16);
           // the block's table: entry i = bf16(fl(qm[i] * am)), as byte planes
           uint32_t L[4], H[4];
 #pragma unroll
@@ -380,9 +472,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             L[i] = prmt(e01, e23, 0x6420u);
             H[i] = prmt(e01, e23, 0x7531u);
           }
-          const uint8_t* src = sP + stage * P_BYTES + src_off;
-          const uint4 q0 = *reinterpret_cast<const uint4*>(src);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(src + 16);
           const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
           uint8_t* dst = sB + stage * B_BYTES + dst_off;
 #pragma unroll
@@ -393,6 +482,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(c) ^ swz) << 4)) = o;
           }
           fence_proxy_async_smem();
+          // the packed slot is released only after its bytes were consumed
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[ps]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&bfull[stage]);
@@ -428,6 +520,9 @@ bool gemm_nf4_supported(const Nf4Args& w, int trans) {
 
 int launch_gemm_nf4(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
   const Nf4Args& w = g.w;
+  const char* v = getenv("FITQ_NF4_GEMM");
+  const bool one_cta = v != nullptr && v[0] == '1';
+  if (!one_cta && gemm_nf4_2cta_supported(w, g.trans)) return launch_gemm_nf4_2cta(g, st, num_sms);
   if (!gemm_nf4_supported(w, g.trans)) return FITQ_ERR_UNSUPPORTED;
   const int64_t n = g.trans ? w.k_in : w.n_out;
   const int64_t k = g.trans ? w.n_out : w.k_in;

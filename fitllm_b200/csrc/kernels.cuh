@@ -77,7 +77,12 @@ inline bool gemm_nf4_shape_ok(int64_t n_out, int64_t k_in, int trans) {
   return cols % 128 == 0 && red % 64 == 0 && k_in % 64 == 0;
 }
 bool gemm_nf4_supported(const Nf4Args& w, int trans);
+// Picks the CTA-pair kernel (256 x 256 tiles, gemm_nf4_2cta.cu) when the
+// output columns are a multiple of 256, else the one-CTA kernel (256 x 128
+// tiles); FITQ_NF4_GEMM=1cta in the environment forces the one-CTA kernel.
 int launch_gemm_nf4(const Nf4GemmArgs& g, cudaStream_t st, int num_sms);
+bool gemm_nf4_2cta_supported(const Nf4Args& w, int trans);
+int launch_gemm_nf4_2cta(const Nf4GemmArgs& g, cudaStream_t st, int num_sms);
 
 // LoRA building blocks (lora.cu).
 // out[M, r] = in[M, D] . wt[r, D]^T  (bf16 in, fp32 accumulate); written as

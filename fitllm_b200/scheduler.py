@@ -22,7 +22,9 @@ Data-parallel ranks (``group`` with more than one rank, NCCL): every rank
 needs the whole layer, but PCIe is per GPU while NVLink is shared by all, so
 by default each rank uploads only its 1/G byte range of the arena into its
 part of the slot and one in-place NCCL all-gather over NVLink fills in the
-rest (``shard_upload=False`` restores the replicated upload).
+rest (``shard_upload=False`` restores the replicated upload).  A rank then
+needs only that byte range in host memory, so it pins just its 1/G of every
+layer (``store_full=True`` keeps whole arenas, e.g. to compare against).
 """
 from __future__ import annotations
 
@@ -80,7 +82,7 @@ class ShardScheduler:
     """Pinned host store + device staging ring for layer shards."""
 
     def __init__(self, num_layers: int, device, ring_slots: int = 2, pin_memory: bool = True,
-                 group=None, shard_upload: bool = True):
+                 group=None, shard_upload: bool = True, store_full: bool = False):
         if ring_slots < 1:
             raise ValueError("ring_slots must be >= 1")
         self.group = group
@@ -92,7 +94,9 @@ class ShardScheduler:
         self.device = torch.device(device)
         self.ring_slots = ring_slots
         self.pin_memory = pin_memory
-        self._host: Dict[int, torch.Tensor] = {}
+        self.store_full = bool(store_full or not self.shard_upload)
+        self._host: Dict[int, torch.Tensor] = {}   # pinned arena, or this rank's byte range of it
+        self._total: Dict[int, int] = {}           # full arena bytes per layer
         self._layout: Dict[int, List[_Entry]] = {}
         self._meta: Dict[int, Dict[str, dict]] = {}
         self._slot_bytes = 0
@@ -113,18 +117,36 @@ class ShardScheduler:
                 meta[k[: -len(".quant_state.bitsandbytes__nf4")]] = json.loads(
                     bytes(base[k].cpu().tolist()).decode("utf-8"))
         entries, total = _layout(base)
-        arena = torch.empty(total, dtype=torch.uint8, pin_memory=self.pin_memory)
-        views = _views(arena, entries)
-        for k, t in base.items():
-            views[k].copy_(t.detach().cpu().view(views[k].dtype).view(views[k].shape))
+        if self.store_full:
+            arena = torch.zeros(total, dtype=torch.uint8, pin_memory=self.pin_memory)  # padding 0
+            views = _views(arena, entries)
+            for k, t in base.items():
+                views[k].copy_(t.detach().cpu().view(views[k].dtype).view(views[k].shape))
+        else:
+            # assemble the arena where the tensors live, keep only this rank's range
+            src_dev = next(iter(base.values())).device if base else torch.device("cpu")
+            full = torch.zeros(total, dtype=torch.uint8, device=src_dev)
+            views = _views(full, entries)
+            for k, t in base.items():
+                views[k].copy_(t.detach().view(views[k].dtype).view(views[k].shape))
+            _, ranges = shard_ranges(total, self.world)
+            a, b = ranges[self.rank]
+            arena = torch.empty(b - a, dtype=torch.uint8, pin_memory=self.pin_memory)
+            arena.copy_(full[a:b])
+            del full, views
         self._host[layer_idx] = arena
+        self._total[layer_idx] = total
         self._layout[layer_idx] = entries
         self._meta[layer_idx] = meta
         self._slot_bytes = max(self._slot_bytes, total)
         return total
 
     def layer_bytes(self, layer_idx: int) -> int:
-        return int(self._host[layer_idx].numel())
+        return int(self._total[layer_idx])
+
+    def host_bytes(self) -> int:
+        """Pinned host bytes this rank holds for all layers."""
+        return int(sum(t.numel() for t in self._host.values()))
 
     def upload_bytes(self, layer_idx: int) -> int:
         """Bytes this rank copies host -> device for one layer."""
@@ -136,6 +158,8 @@ class ShardScheduler:
         return b - a
 
     def host_tensors(self, layer_idx: int) -> Dict[str, torch.Tensor]:
+        if not self.store_full:
+            raise RuntimeError("this rank holds only its byte range of the layer (store_full=False)")
         return _views(self._host[layer_idx], self._layout[layer_idx])
 
     def quant_meta(self, layer_idx: int) -> Dict[str, dict]:
@@ -177,10 +201,11 @@ class ShardScheduler:
         src = self._host[layer_idx]
         with torch.cuda.stream(cs):
             if self.shard_upload:
-                chunk, ranges = shard_ranges(src.numel(), self.world)
+                chunk, ranges = shard_ranges(self._total[layer_idx], self.world)
                 a, b = ranges[self.rank]
                 if b > a:
-                    self._slots[s][a:b].copy_(src[a:b], non_blocking=True)
+                    part = src[a:b] if self.store_full else src
+                    self._slots[s][a:b].copy_(part, non_blocking=True)
                 mine = self._slots[s][self.rank * chunk:(self.rank + 1) * chunk]
                 # in place: this rank's chunk is already in position inside the output
                 dist.all_gather_into_tensor(self._slots[s][: chunk * self.world], mine,

@@ -1,6 +1,7 @@
 """Sharded weight upload on two GPUs: each rank copies its 1/G byte range of a
 layer arena from pinned host memory and one NCCL all-gather completes the
-device slot; the slot must equal the host arena byte for byte on every rank.
+device slot; the slot must equal the layer's tensors byte for byte on every
+rank, with each rank holding only its byte range in pinned host memory.
 Runs two NCCL ranks as child processes (skipped with fewer than two GPUs)."""
 import os
 import subprocess
@@ -24,14 +25,15 @@ _CHILD = textwrap.dedent("""
     layers = [{"w": torch.randint(0, 256, (1_000_003,), generator=g, dtype=torch.uint8),
                "b": torch.randn(777, generator=g)} for _ in range(3)]
     sched = ShardScheduler(3, torch.device("cuda", rank), ring_slots=2)
-    assert sched.shard_upload and sched.world == 2
+    assert sched.shard_upload and sched.world == 2 and not sched.store_full
     for l, t in enumerate(layers):
         sched.add_layer(l, t)
+    # each rank pins only its half of every arena
+    assert sched.host_bytes() <= sum(sched.layer_bytes(l) for l in range(3)) // 2 + 3 * 256
     for l in range(3):
         dev = sched.get_layer_tensors(l)
-        host = sched.host_tensors(l)
-        for k in host:
-            assert torch.equal(dev[k].cpu(), host[k]), (rank, l, k)
+        for k, v in layers[l].items():
+            assert torch.equal(dev[k].cpu(), v), (rank, l, k)
         sched.release(l)
     torch.cuda.synchronize()
     dist.barrier(device_ids=[rank])

@@ -5,8 +5,9 @@
   I . W_deq = W_deq; one product per output element, accumulated in fp32 and
   rounded to bf16, reproduces the decoded weight exactly.  So the outputs must
   equal the oracle's bitsandbytes dequant bit for bit -- for the K-major
-  (forward) and MN-major (dX) operand layouts, double-quantised and plain
-  fp32 absmax, one tile and many tiles per CTA.
+  (forward) and MN-major (dX) operand layouts, on the CTA-pair kernel (256-
+  and 512-row tiles) and the one-CTA kernel, double-quantised and plain fp32
+  absmax, one tile and many tiles per CTA.
 * The full QLoRA forward / backward through the fused GEMM (LoRA K-block,
   bias, residual add, M not a multiple of the 256-row tile) against the
   oracle within the 1e-2 contract, and against the dequant + bf16 GEMM path.
@@ -38,10 +39,25 @@ def _weight(n, k, seed, dev, nested=True):
     return st, Nf4WeightCRef(packed, qs)
 
 
+KERNELS = ["pair256", "pair512", "1cta"]
+
+
+def _set_kernel(monkeypatch, kernel):
+    """pair256 / pair512: the CTA-pair kernel with 256- or 512-row tiles where
+    the output columns are a multiple of 256 (the one-CTA kernel otherwise);
+    1cta: the one-CTA kernel throughout."""
+    if kernel == "1cta":
+        monkeypatch.setenv("FITQ_NF4_GEMM", "1cta")
+    else:
+        monkeypatch.setenv("FITQ_NF4_MSUB", "2" if kernel == "pair512" else "1")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("n,k,nested", [(128, 64, True), (384, 512, True), (256, 1024, False),
                                         (1024, 2048, True), (640, 1280, False)])
-def test_fused_decode_bit_exact(cuda_dev, monkeypatch, n, k, nested):
+def test_fused_decode_bit_exact(cuda_dev, monkeypatch, n, k, nested, kernel):
     monkeypatch.setenv("FITQ_NF4_FUSED", "1")
+    _set_kernel(monkeypatch, kernel)
     from fitllm_b200 import ops
     st, wref = _weight(n, k, 900 + n + k, cuda_dev, nested)
     ref = onf4.dequant(st, "bf16")  # uint16 bits [n, k]
@@ -56,10 +72,12 @@ def test_fused_decode_bit_exact(cuda_dev, monkeypatch, n, k, nested):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("m,n,k,r,nested", [(1000, 384, 640, 16, True), (300, 1280, 5120, 16, True),
                                             (2048, 1024, 1024, 32, False), (777, 256, 2048, 0, True),
-                                            (4096, 512, 512, 64, True)])
-def test_fused_qlora_vs_oracle_and_dequant_path(cuda_dev, monkeypatch, m, n, k, r, nested):
+                                            (4096, 512, 512, 64, True), (5000, 2048, 1536, 16, True)])
+def test_fused_qlora_vs_oracle_and_dequant_path(cuda_dev, monkeypatch, m, n, k, r, nested, kernel):
+    _set_kernel(monkeypatch, kernel)
     from fitllm_b200 import ops
     s = 2.0
     st, wref = _weight(n, k, 950 + m, cuda_dev, nested)

@@ -44,17 +44,18 @@ def test_abi_rejects_bad_arguments_without_a_device():
     assert L.fitq_nf4_dequant(ctypes.byref(w2), 16, 0, 0, None) == 2  # K % 64 != 0
     assert L.fitq_gemm_bf16_tn(16, 16, 16, None, 128, 100, 64, None) == 2  # N % 16 != 0
     assert b"N % 16 == 0" in L.fitq_last_error()
-    # NF4 decoded inside the GEMM: no dequantised copy of W in the workspace
-    assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) < 5120 * 5120 // 2
-    assert L.fitq_qlora_bwd_workspace(512, 5120, 5120, 16) < 5120 * 5120 // 2
-    # the dequant + bf16 GEMM path holds W (bf16) in the workspace
     import os
-    os.environ["FITQ_NF4_FUSED"] = "0"
     try:
+        # NF4 decoded inside the GEMM: no dequantised copy of W in the workspace
+        os.environ["FITQ_NF4_FUSED"] = "1"
+        assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) < 5120 * 5120 // 2
+        assert L.fitq_qlora_bwd_workspace(512, 5120, 5120, 16) < 5120 * 5120 // 2
+        # the dequant + bf16 GEMM path holds W (bf16) in the workspace
+        os.environ["FITQ_NF4_FUSED"] = "0"
         assert L.fitq_qlora_fwd_workspace(512, 5120, 5120, 16) > 5120 * 5120 * 2
         assert L.fitq_qlora_bwd_workspace(512, 5120, 5120, 16) > 5120 * 5120 * 2
     finally:
-        del os.environ["FITQ_NF4_FUSED"]
+        os.environ.pop("FITQ_NF4_FUSED", None)
     # shapes the fused GEMM does not take (N % 128 != 0) keep the dequant path
     assert L.fitq_qlora_fwd_workspace(512, 320, 256, 16) > 320 * 256 * 2
 
@@ -257,6 +258,49 @@ def test_per_layer_allreduce_two_gloo_ranks():
     for _, vals, uniform in res:
         assert vals == [total * 1.0, total * 2.0, total * 3.0]
         assert uniform
+
+
+def _rank_store_main(rank, world, port, q):
+    import torch.distributed as dist
+    from fitllm_b200.scheduler import ShardScheduler, shard_ranges
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    g = torch.Generator().manual_seed(5)
+    layers = [{"w": torch.randint(0, 256, (10_001 + 97 * l,), generator=g, dtype=torch.uint8),
+               "b": torch.randn(33, generator=g).bfloat16()} for l in range(3)]
+    part = ShardScheduler(3, "cpu", pin_memory=False)
+    full = ShardScheduler(3, "cpu", pin_memory=False, store_full=True)
+    ok = part.shard_upload and not part.store_full and full.store_full
+    for l, t in enumerate(layers):
+        part.add_layer(l, t)
+        full.add_layer(l, t)
+        _, ranges = shard_ranges(full.layer_bytes(l), world)
+        a, b = ranges[rank]
+        ok = ok and part.layer_bytes(l) == full.layer_bytes(l)
+        ok = ok and torch.equal(part._host[l], full._host[l][a:b])
+        ok = ok and part.upload_bytes(l) == b - a
+    q.put((rank, ok, part.host_bytes(), full.host_bytes()))
+    dist.destroy_process_group()
+
+
+def test_sharded_host_store_keeps_only_the_rank_range():
+    """With data-parallel ranks each rank pins only the byte range of every
+    layer arena that it uploads (its part of the in-place all-gather); the
+    range equals the same bytes of the whole arena."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_store_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _, _ in res)
+    assert sum(h for _, _, h, _ in res) == res[0][3]  # the two ranges make up the arenas
 
 
 def test_shard_ranges_cover_arena():
