@@ -169,7 +169,7 @@ def cpu_baseline(a, seq):
                       f"{r['step_s']:.1f} s step (quantisation {r['quantize_s']:.1f} s untimed)"}
 
 
-def gemv_sweep(dev, peak_gbs, reps=20):
+def gemv_sweep(dev, peak_gbs, reps=20, cpu=True):
     """NF4 GEMV decode sweep: HBM GB/s of the weight stream.
 
     Every shape rotates over enough distinct weights to exceed 2x L2, one
@@ -219,14 +219,26 @@ def gemv_sweep(dev, peak_gbs, reps=20):
             del graph
         del sets
         torch.cuda.empty_cache()
+        if cpu:
+            from oracle import layer_ref
+            c = layer_ref.time_cpu_gemv(n, k, 1, r)
+            out[f"{name}_{n}x{k}_m1"]["cpu_baseline"] = {
+                "value": round(c["GB/s"], 3), "unit": "GB/s", "cores": c["threads"], "kind": "port",
+                "sample": f"one M=1 call on the host cores: torch dequant in the oracle's op order + "
+                          f"fp32 product ({c['us'] / 1000:.1f} ms)"}
     return out
 
 
-def qproj_linear(dev, reps=20):
+def qproj_linear(dev, reps=20, cpu=True):
     """BASELINE config 1 on the GPU: one NF4 QLoRA q_proj (5120 -> 5120, r=16,
     alpha 32) forward + backward (dX, dA, dB) over x [512, 5120] through the
-    module API.  FLOPs per call = M (4 N K + 6 r (N + K))."""
+    C-ABI calls (fitq_qlora_fwd / fitq_qlora_bwd), replayed from a CUDA graph
+    with L2 flushed (a 256 MB write) before every replay; device time by CUDA
+    events.  FLOPs per call = M (4 N K + 6 r (N + K)).  Also the same call
+    through the module API (autograd, eager launches: host-launch bound at this
+    size), and the CPU restatement."""
     import torch
+    from fitllm_b200 import ops
     from fitllm_b200.qlora import Linear4bit, QLoRALinear4bit
     m, n, k, r = 512, 5120, 5120, 16
     g = torch.Generator(device=dev).manual_seed(0)
@@ -237,29 +249,75 @@ def qproj_linear(dev, reps=20):
         mod.lora_B["default"].weight.normal_(0.0, 0.01, generator=g)
     x = torch.randn(m, k, generator=g, device=dev).bfloat16().requires_grad_(True)
     dy = torch.randn(m, n, generator=g, device=dev).bfloat16()
+    wref = mod.base_layer.wref()
+    A = mod.lora_A["default"].weight.detach().float().contiguous()
+    B = mod.lora_B["default"].weight.detach().float().contiguous()
+    xd = x.detach()
+    s = mod.scaling["default"]
 
-    def call():
+    def abi_call():
+        y, t = ops.qlora_forward(xd, wref, A, B, s, want_t=True)
+        return ops.qlora_backward(xd, dy, wref, A, B, s, t_saved=t)
+
+    for _ in range(3):
+        abi_call()
+    torch.cuda.synchronize()
+    cs = torch.cuda.Stream(device=dev)
+    cs.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cs):
+        abi_call()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cs):
+            abi_call()
+    torch.cuda.synchronize()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        graph.replay()
+        e_ev.record()
+        torch.cuda.synchronize()
+        times.append(s_ev.elapsed_time(e_ev))
+    ms = statistics.median(times)
+    del graph, flush
+
+    def mod_call():
         mod.zero_grad(set_to_none=True)
         x.grad = None
         mod(x).backward(dy)
 
     for _ in range(3):
-        call()
+        mod_call()
     torch.cuda.synchronize()
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s_ev.record()
     for _ in range(reps):
-        call()
+        mod_call()
     e_ev.record()
     torch.cuda.synchronize()
-    ms = s_ev.elapsed_time(e_ev) / reps
+    ms_mod = s_ev.elapsed_time(e_ev) / reps
     flops = m * (4 * n * k + 6 * r * (n + k))
-    return {"metric": "NF4 QLoRA q_proj fwd+bwd (x [512, 5120], r=16)", "ms": round(ms, 4),
-            "tokens_per_s": round(m / (ms / 1000.0), 1),
-            "tflops": round(flops / (ms / 1000.0) / 1e12, 1), "flop_per_call": flops}
+    out = {"metric": "NF4 QLoRA q_proj fwd+bwd (x [512, 5120], r=16)", "ms": round(ms, 4),
+           "tokens_per_s": round(m / (ms / 1000.0), 1),
+           "tflops": round(flops / (ms / 1000.0) / 1e12, 1), "flop_per_call": flops,
+           "timing": "C-ABI fwd + bwd replayed from a CUDA graph, L2 flushed before each replay, median of "
+                     f"{reps}",
+           "module_api_eager_ms": round(ms_mod, 4)}
+    if cpu:
+        from oracle import layer_ref
+        c = layer_ref.time_cpu_qproj(m, n, k, r)
+        out["cpu_baseline"] = {"value": round(c["tokens_per_s"], 1), "unit": "tokens/s",
+                               "cores": c["threads"], "kind": "port",
+                               "sample": f"the whole call (x [512, 5120]) in fp32 torch on the host "
+                                         f"cores with the oracle-dequantised weight: "
+                                         f"{c['call_s'] * 1000:.1f} ms per fwd+bwd"}
+    return out
 
 
-def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, reps=10):
+def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, reps=10, cpu=True):
     """one speculative-verify pass over 64 random-init NF4
     Qwen2.5-32B-shaped layers (LoRA r=16 on q/v), batch 8 x (4 draft + 1)
     tokens against a 4096-position KV cache -> every projection an M = 40 NF4
@@ -300,15 +358,24 @@ def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, re
     gbs = (wbytes + kv) / (ms / 1000.0) / 1e9
     del graph, out, layers, cache
     torch.cuda.empty_cache()
-    return {"metric": "speculative verify pass, 64 NF4 layers, batch 8 x 5 tokens, KV 4096",
-            "ms_per_pass": round(ms, 3), "tokens_per_s": round(batch * t / (ms / 1000.0), 1),
-            "bytes_per_pass": int(wbytes + kv), "GB/s": round(gbs, 1),
-            "frac_of_hbm": round(gbs / peak_gbs, 3), "m_per_projection": batch * t,
-            "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention on the "
-                    "split-KV verify kernel (fitq_verify_attention)"}
+    out = {"metric": "speculative verify pass, 64 NF4 layers, batch 8 x 5 tokens, KV 4096",
+           "ms_per_pass": round(ms, 3), "tokens_per_s": round(batch * t / (ms / 1000.0), 1),
+           "bytes_per_pass": int(wbytes + kv), "GB/s": round(gbs, 1),
+           "frac_of_hbm": round(gbs / peak_gbs, 3), "m_per_projection": batch * t,
+           "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention on the "
+                   "split-KV verify kernel (fitq_verify_attention)"}
+    if cpu:
+        from oracle import layer_ref
+        c = layer_ref.time_cpu_verify_layer(batch, t, context)
+        out["cpu_baseline"] = {"value": round(c["tokens_per_s"], 3), "unit": "tokens/s",
+                               "cores": c["threads"], "kind": "port",
+                               "sample": f"one layer of the KV-cached verify step in fp32 torch on the "
+                                         f"host cores ({c['layer_s'] * 1000:.1f} ms), extrapolated to "
+                                         f"64 layers ({c['pass_s_64_layers']:.2f} s per pass)"}
+    return out
 
 
-def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, steps=2):
+def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, steps=2, cpu=True):
     """One full synthetic training step over 64 random-init
     NF4 Qwen2.5-32B-shaped layers whose shards live in pinned host memory and
     stream through the device ring (sharded upload + NCCL all-gather when
@@ -373,6 +440,15 @@ def full_step_bench(dev, rank, world, layers_n=64, microbatches=16, seq=1024, st
                    "the lm_head adds 2 GEMMs of 2 x 5120 x 152064 FLOP per token"}
     del eng, sched, store, opt, h0, labels, head
     torch.cuda.empty_cache()
+    if cpu and rank == 0:
+        from oracle import layer_ref
+        c = layer_ref.time_cpu_step(seq=seq, microbatches=1)
+        out["cpu_baseline"] = {"value": round(c["tokens_per_s"] / layers_n, 3), "unit": "tokens/s",
+                               "cores": c["threads"], "kind": "port",
+                               "sample": f"1 micro-batch x {seq} tokens through one layer step (fwd + "
+                                         f"recompute + bwd) in fp32 torch on the host cores "
+                                         f"({c['step_s']:.1f} s), extrapolated to {layers_n} layers "
+                                         "(the lm_head and optimizer not counted)"}
     return out
 
 
@@ -652,7 +728,7 @@ def main():
         if e2e is not None:
             del h_host, g_host, gin_host, lora_host, pipe
         torch.cuda.empty_cache()
-        full_step = full_step_bench(dev, rank, world)
+        full_step = full_step_bench(dev, rank, world, cpu=not a.no_cpu_baseline)
 
     if rank != 0:
         return
@@ -665,6 +741,11 @@ def main():
     if peak is None:
         peak, peak_src = 1400.0, "of fallback (sustained 1.4 PFLOP/s)"
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+    # DRAM read + write per GEMM launch: 509.1 MB measured by ncu over the 70
+    # GEMM launches of the same step at 2 x 2048 tokens
+    # (profiles/gemm_bf16_tn_dram_traffic_qwen25_32b_layer_2x2048.md), scaled
+    # by the rows each launch processes (the traffic grows with M).
+    traffic = 509.1e6 * (a.microbatches * a.seq) / (2 * 2048)
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 3),
@@ -672,6 +753,8 @@ def main():
         "data": "synthetic (seeded NF4 weights, token ids, upstream grad)",
         "config": workload(a),
         "model_tflops": round(tokens * flops_per_token(a.seq) / (ms / 1000.0) / 1e12, 1),
+        "value_recompute_every_layer": round(tokens / (ms_rc / 1000.0), 1),
+        "ms_per_step_recompute_every_layer": round(ms_rc, 3),
         "recompute": {"layers_kept_without_recompute": kept, "layers": 1,
                       "note": "forward keeps its autograd state for the layers whose activations fit "
                               "the HBM budget, so their backward skips the recompute",
@@ -680,7 +763,9 @@ def main():
         "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn (tcgen05: the cta_group::2 pair kernel, the one-CTA kernel for K >= 4N)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if achieved else None,
-                     "peak_source": peak_src, "traffic": None,
+                     "peak_source": peak_src, "traffic": round(traffic),
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum at "
+                                     "2 x 2048 tokens, scaled by the rows)",
                      "launches": n_t, "gemm_ms_per_step": round(gemm_ms / a.steps, 3),
                      "gemm_share_of_step": round(gemm_ms / a.steps / ms, 3)},
         "clocks": clk,
@@ -692,12 +777,12 @@ def main():
         out["gemv"] = {"metric": "NF4 GEMV decode HBM GB/s (weight bytes / time, CUDA-graph replay, "
                                  "weights rotated over > 2x L2)", "peak_gbs": hbm,
                        "peak_source": "of measured (hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
-                       "results": gemv_sweep(dev, hbm)}
+                       "results": gemv_sweep(dev, hbm, cpu=not a.no_cpu_baseline)}
     if full_step is not None:
         out["full_step"] = full_step
     if world == 1 and not a.no_gemv:
-        out["qproj_linear"] = qproj_linear(dev)
-        out["verify"] = verify_bench(dev, peaks.get("hbm_gbs", 6650.0))
+        out["qproj_linear"] = qproj_linear(dev, cpu=not a.no_cpu_baseline)
+        out["verify"] = verify_bench(dev, peaks.get("hbm_gbs", 6650.0), cpu=not a.no_cpu_baseline)
     if world == 1 and not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(a, a.cpu_seq)
     print(json.dumps(out), flush=True)

@@ -41,6 +41,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "nf4_decode.cuh"
 
 namespace fitq {
 namespace {
@@ -94,41 +95,6 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
   const int local = tile - group * per_group;
   mb = first_m + local % gsz;
   nb = local / gsz;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Smem descriptor of an MN-major, 128-byte-swizzled operand.
-__device__ __forceinline__ uint64_t umma_smem_desc_sw128_mn(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((MN_LBO >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((MN_SBO >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1u) << 46;
-  d |= static_cast<uint64_t>(2u) << 61;
-  return d;
-}
-
-// Four weights from the 16-bit half of a packed word.  Nibble j of `s` picks
-// output byte j; for packed bytes (e0<<4 | e1), (e2<<4 | e3) the nibbles are
-// e1, e0, e3, e2.  L / H hold the low / high bytes of the 16 table entries
-// (entries 4i..4i+3 in register i); bit 3 of a nibble selects the upper eight.
-__device__ __forceinline__ void lookup4(uint32_t h, const uint32_t (&L)[4], const uint32_t (&H)[4],
-                                        uint32_t& w01, uint32_t& w23) {
-  const uint32_t s = h & 0x7777u;
-  const uint32_t m = prmt(0u, 0xFFFFFFFFu, (h >> 1) & 0x4444u);  // 0xFF where bit 3 set
-  const uint32_t lo = (prmt(L[0], L[1], s) & ~m) | (prmt(L[2], L[3], s) & m);
-  const uint32_t hi = (prmt(H[0], H[1], s) & ~m) | (prmt(H[2], H[3], s) & m);
-  w01 = prmt(lo, hi, 0x4051u);  // e0 | e1 << 16
-  w23 = prmt(lo, hi, 0x6273u);  // e2 | e3 << 16
 }
 
 // Walks one decoder group's iterations (tile, kb) in order: the K steps of
@@ -282,7 +248,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t idesc_k = umma_idesc_bf16_f32(128, BN);
       const uint64_t a_desc0 = umma_smem_desc_sw128(smem_u32(sA));
       const uint64_t b_desc0 = umma_smem_desc_sw128(smem_u32(sB));
-      const uint64_t b_desc0_mn = umma_smem_desc_sw128_mn(smem_u32(sB));
+      const uint64_t b_desc0_mn = umma_smem_desc_sw128_mn(smem_u32(sB), MN_LBO, MN_SBO);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -460,27 +426,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int ps = my_pit % PSTAGES;
           const uint32_t pph = static_cast<uint32_t>(my_pit / PSTAGES) & 1u;
           if (!mbar_wait(&pfull[ps], pph, abort_flag, p.status)) { ok = false; break; }
-          const uint8_t* src = sP + ps * P_BYTES + src_off;
-          const uint4 q0 = *reinterpret_cast<const uint4*>(src);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(src + 16);
-          // the block's table: entry i = bf16(fl(qm[i] * am)), as byte planes
-          uint32_t L[4], H[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t e01 = pack_bf16x2(__fmul_rn(qm[4 * i], am), __fmul_rn(qm[4 * i + 1], am));
-            const uint32_t e23 = pack_bf16x2(__fmul_rn(qm[4 * i + 2], am), __fmul_rn(qm[4 * i + 3], am));
-            L[i] = prmt(e01, e23, 0x6420u);
-            H[i] = prmt(e01, e23, 0x7531u);
-          }
-          const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-          uint8_t* dst = sB + stage * B_BYTES + dst_off;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 o;
-            lookup4(words[c], L, H, o.x, o.y);
-            lookup4(words[c] >> 16, L, H, o.z, o.w);
-            *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(c) ^ swz) << 4)) = o;
-          }
+          nf4_decode_row(sP + ps * P_BYTES + src_off, sB + stage * B_BYTES + dst_off, swz, qm, am);
           fence_proxy_async_smem();
           // the packed slot is released only after its bytes were consumed
           __syncwarp();

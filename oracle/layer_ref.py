@@ -113,12 +113,21 @@ def layer_step(w, h, grad_out) -> Tuple[torch.Tensor, Dict[str, torch.Tensor]]:
     return x.grad, {k: p.grad for k, p in params.items()}
 
 
+_LAYER_CACHE: Dict[int, Dict[str, torch.Tensor]] = {}
+
+
+def _cached_layer(seed: int) -> Dict[str, torch.Tensor]:
+    if seed not in _LAYER_CACHE:
+        _LAYER_CACHE[seed] = build_layer(seed=seed)
+    return _LAYER_CACHE[seed]
+
+
 def time_cpu_step(seq=2048, microbatches=1, seed=0, threads=None) -> Dict[str, float]:
     """Time one layer step on the host cores; returns tokens/s and details."""
     threads = threads or os.cpu_count()
     torch.set_num_threads(threads)
     t0 = time.perf_counter()
-    w = build_layer(seed=seed)
+    w = _cached_layer(seed)
     t_build = time.perf_counter() - t0
     g = torch.Generator().manual_seed(seed + 5)
     hidden = int(w["cfg"][0])
@@ -129,3 +138,118 @@ def time_cpu_step(seq=2048, microbatches=1, seed=0, threads=None) -> Dict[str, f
     dt = time.perf_counter() - t0
     return {"tokens_per_s": microbatches * seq / dt, "step_s": dt, "threads": threads,
             "quantize_s": t_build, "tokens": microbatches * seq}
+
+
+# ----------------------------------------------------------------------------
+# CPU baselines of the other workloads (timed on the host cores, all threads)
+# ----------------------------------------------------------------------------
+def time_cpu_qproj(m=512, n=5120, k=5120, r=16, alpha=32.0, threads=None) -> Dict[str, float]:
+    """One NF4 QLoRA q_proj linear, forward + backward (dX, dA, dB), in fp32
+    torch on the host cores: the oracle-dequantised weight (untimed), PEFT
+    LoRA (A Kaiming-uniform [r, K], B N(0, 0.01) [N, r]), x and dY N(0, 1)."""
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    st = onf4.quantize((torch.randn(n, k, generator=g) * 0.02).numpy())
+    w = onf4.dequant_torch(st)
+    A = ((torch.rand(r, k, generator=g) * 2 - 1) / math.sqrt(k)).requires_grad_(True)
+    B = (torch.randn(n, r, generator=g) * 0.01).requires_grad_(True)
+    x = torch.randn(m, k, generator=g).bfloat16().float().requires_grad_(True)
+    dy = torch.randn(m, n, generator=g).bfloat16().float()
+    s = alpha / r
+
+    def call():
+        A.grad = B.grad = x.grad = None
+        y = x @ w.T + s * (x @ A.T) @ B.T
+        y.backward(dy)
+
+    call()
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        call()
+    dt = (time.perf_counter() - t0) / reps
+    return {"tokens_per_s": m / dt, "call_s": dt, "threads": threads,
+            "tflops": m * (4 * n * k + 6 * r * (n + k)) / dt / 1e12}
+
+
+def time_cpu_gemv(n, k, m, r=0, threads=None) -> Dict[str, float]:
+    """One NF4 GEMV call on the host cores: dequant of the weight (torch ops,
+    the oracle's op order) + the [m, K] x [K, N] product (+ LoRA), fp32."""
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(n + k)
+    st = onf4.quantize((torch.randn(n, k, generator=g) * 0.02).numpy())
+    x = torch.randn(m, k, generator=g).bfloat16().float()
+    A = torch.randn(r, k, generator=g) * 0.01 if r else None
+    B = torch.randn(n, r, generator=g) * 0.01 if r else None
+
+    def call():
+        w = onf4.dequant_torch(st)
+        y = x @ w.T
+        if r:
+            y = y + 2.0 * (x @ A.T) @ B.T
+        return y
+
+    call()
+    t0 = time.perf_counter()
+    reps = 2
+    for _ in range(reps):
+        call()
+    dt = (time.perf_counter() - t0) / reps
+    wbytes = n * k // 2 + n * k // 64 + ((n * k // 64 + 255) // 256) * 4
+    return {"us": dt * 1e6, "GB/s": wbytes / dt / 1e9, "threads": threads}
+
+
+def time_cpu_verify_layer(batch=8, t_new=5, prefix=4096, seed=0, threads=None) -> Dict[str, float]:
+    """One decoder layer of a KV-cached speculative-verify pass on the host
+    cores (fp32 torch): the batch x t_new new tokens through the projections
+    (oracle-dequantised NF4 weights, LoRA on q/v), RoPE at positions prefix..,
+    attention of token i over cache positions <= prefix + i (GQA), MLP.  The
+    64-layer pass time is 64 x this layer's (stated as extrapolated)."""
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    w = _cached_layer(seed)
+    hidden, heads, kv_heads, head_dim, inter = [int(v) for v in w["cfg"]]
+    s = float(w["scale"])
+    g = torch.Generator().manual_seed(seed + 9)
+    h = torch.randn(batch, t_new, hidden, generator=g).bfloat16().float()
+    L = prefix + t_new
+    kc = torch.randn(batch, kv_heads, L, head_dim, generator=g).bfloat16().float()
+    vc = torch.randn(batch, kv_heads, L, head_dim, generator=g).bfloat16().float()
+
+    def lin(name, x):
+        y = x @ w[name].T
+        if name + ".bias" in w:
+            y = y + w[name + ".bias"]
+        if name + ".lora_A" in w:
+            y = y + s * (x @ w[name + ".lora_A"].T) @ w[name + ".lora_B"].T
+        return y
+
+    def call():
+        x = _rms(h)
+        q = lin("q_proj", x).view(batch, t_new, heads, head_dim).transpose(1, 2)
+        k = lin("k_proj", x).view(batch, t_new, kv_heads, head_dim).transpose(1, 2)
+        v = lin("v_proj", x).view(batch, t_new, kv_heads, head_dim).transpose(1, 2)
+        cos, sin = _rope(L, head_dim)
+        cos, sin = cos[prefix:], sin[prefix:]
+        q, k = q * cos + _rot(q) * sin, k * cos + _rot(k) * sin
+        kc[:, :, prefix:] = k
+        vc[:, :, prefix:] = v
+        pos = torch.arange(L)
+        lim = prefix + torch.arange(t_new)
+        mask = pos[None, :] <= lim[:, None]
+        o = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=True)
+        h1 = h + lin("o_proj", o.transpose(1, 2).reshape(batch, t_new, heads * head_dim))
+        x2 = _rms(h1)
+        return h1 + lin("down_proj", F.silu(lin("gate_proj", x2)) * lin("up_proj", x2))
+
+    with torch.no_grad():
+        call()
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            call()
+        dt = (time.perf_counter() - t0) / reps
+    return {"layer_s": dt, "pass_s_64_layers": 64 * dt,
+            "tokens_per_s": batch * t_new / (64 * dt), "threads": threads}

@@ -249,6 +249,21 @@ def dequant_np(st: NF4State) -> np.ndarray:
     return f32_to_bf16_bits(v).reshape(st.shape)
 
 
+def dequant_torch(st: NF4State):
+    """The dequant of ``dequant_np`` in torch CPU ops (all host threads): the
+    same two rounded fp32 operations per block and one per weight, then RNE to
+    bf16.  Returns fp32 values [shape] (exactly bf16-representable)."""
+    import torch
+    codes = torch.from_numpy(st.absmax_code).long()
+    nb = codes.numel()
+    nabs = torch.from_numpy(st.nested_absmax).repeat_interleave(DQ_BLOCK)[:nb]
+    am = torch.from_numpy(st.nested_quant_map)[codes] * nabs + torch.tensor(st.offset)
+    packed = torch.from_numpy(st.packed)
+    nib = torch.stack(((packed >> 4) & 0x0F, packed & 0x0F), dim=1).reshape(-1).long()
+    w = torch.from_numpy(st.quant_map)[nib].view(nb, NF4_BLOCK) * am[:, None]
+    return w.to(torch.bfloat16).float().reshape(st.shape)
+
+
 # ----------------------------------------------------------------------------
 # QLoRA linear reference math (fp64 on the exact bf16-valued inputs)
 # ----------------------------------------------------------------------------

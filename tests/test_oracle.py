@@ -107,3 +107,16 @@ def test_qlora_reference_math_consistency():
             fm = f(*(q if i == ["x", "A", "B"].index(name) else v for i, v in enumerate(args)))
             num[idx] = (fp - fm) / (2 * eps)
         assert np.allclose(num, grad, rtol=1e-5, atol=1e-6), name
+
+
+def test_torch_dequant_matches_oracle_bits():
+    """The multi-threaded torch restatement of the dequant (used by the timed
+    CPU baselines) gives the C oracle's values bit for bit."""
+    from oracle import nf4 as onf4
+    import torch
+    w = (torch.randn(192, 640, generator=torch.Generator().manual_seed(4)) * 0.02).numpy()
+    w[3, :64] = 0.0
+    st = onf4.quantize(w)
+    got = onf4.dequant_torch(st).numpy().view(np.uint32)
+    ref = onf4.bf16_bits_to_f32(onf4.dequant(st, "bf16")).view(np.uint32)
+    assert np.array_equal(got, ref)
