@@ -67,6 +67,10 @@ SIGNATURES = {
     "fitq_timing_read": (I32, [P, P, I32]),
     "fitq_launch_count": (ctypes.c_longlong, []),
     "fitq_nf4_gemv_noalloc": (I32, [WP, P, I64, P, P, I32, F32, P, P, P, P]),
+    "fitq_nf4_gateup_swiglu_workspace": (SZ, [I64, I64, I64]),
+    "fitq_nf4_gateup_swiglu": (I32, [WP, WP, P, I64, P, P, P, P, SZ, P]),
+    "fitq_nf4_down_dswiglu_workspace": (SZ, [I64, I64, I64]),
+    "fitq_nf4_down_dswiglu": (I32, [WP, P, I64, P, P, P, P, P, SZ, P]),
     "fitq_rmsnorm_fwd": (I32, [P, P, P, I64, I64, F32, P]),
     "fitq_rmsnorm_bwd": (I32, [P, P, P, P, I64, I64, F32, P]),
     "fitq_rope": (I32, [P, P, P, P, I64, I32, I32, I64, I32, P]),

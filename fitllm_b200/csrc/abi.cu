@@ -711,6 +711,95 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
   return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm (dx)");
 }
 
+size_t fitq_nf4_gateup_swiglu_workspace(int64_t m, int64_t n_out, int64_t k_in) {
+  (void)m;
+  Carve c{nullptr, 0};
+  c.take(bf16_bytes(n_out * k_in));
+  c.take(bf16_bytes(n_out * k_in));
+  return c.used;
+}
+
+int fitq_nf4_gateup_swiglu(const fitq_nf4_weight* w_gate, const fitq_nf4_weight* w_up, const void* x,
+                           int64_t m, void* act, void* gate_out, void* up_out, void* workspace,
+                           size_t workspace_bytes, fitq_stream_t stream) {
+  fitq::Nf4Args g, u;
+  int rc = check_weight(w_gate, &g);
+  if (rc) return rc;
+  if ((rc = check_weight(w_up, &u))) return rc;
+  if (g.n_out != u.n_out || g.k_in != u.k_in)
+    return fail(FITQ_ERR_SHAPE, "gateup_swiglu: gate and up must have the same shape");
+  if (!x || !act) return fail(FITQ_ERR_ARG, "gateup_swiglu: x and act are required");
+  if (m <= 0 || m >= (1ll << 31)) return fail(FITQ_ERR_SHAPE, "gateup_swiglu: bad M=%lld", (long long)m);
+  const int64_t N = g.n_out, K = g.k_in;
+  if (N % 128 != 0)
+    return fail(FITQ_ERR_SHAPE, "gateup_swiglu: N=%lld not a multiple of 128", (long long)N);
+  if (!al16(x) || !al16(act) || (gate_out && !al16(gate_out)) || (up_out && !al16(up_out)))
+    return fail(FITQ_ERR_ALIGN, "gateup_swiglu: x/act/gate_out/up_out must be 16-byte aligned");
+  const size_t need = fitq_nf4_gateup_swiglu_workspace(m, N, K);
+  if (!workspace || workspace_bytes < need)
+    return fail(FITQ_ERR_WORKSPACE, "gateup_swiglu: workspace %zu < %zu bytes", workspace_bytes, need);
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  void* wg = c.take(bf16_bytes(N * K));
+  void* wu = c.take(bf16_bytes(N * K));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = fitq::launch_nf4_dequant(g, wg, FITQ_DTYPE_BF16, 0, st, sms)))
+    return launch_status(rc, "nf4_dequant (gate)");
+  if ((rc = fitq::launch_nf4_dequant(u, wu, FITQ_DTYPE_BF16, 0, st, sms)))
+    return launch_status(rc, "nf4_dequant (up)");
+  fitq::GemmArgs a{};
+  a.a = x; a.lda = K;
+  a.b = wg; a.b2 = wu; a.ldb = K;
+  a.c = act; a.ldc = N;
+  a.m = m; a.n = N; a.k = K;
+  a.epi = fitq::GEMM_EPI_SWIGLU;
+  a.aux0 = gate_out; a.aux1 = up_out;
+  a.status = status_ptr();
+  return launch_status(fitq::launch_gemm(a, st, sms), "tcgen05 gemm (gate/up + SwiGLU)");
+}
+
+size_t fitq_nf4_down_dswiglu_workspace(int64_t m, int64_t n_out, int64_t k_in) {
+  (void)m;
+  Carve c{nullptr, 0};
+  c.take(bf16_bytes(n_out * k_in));
+  return c.used;
+}
+
+int fitq_nf4_down_dswiglu(const fitq_nf4_weight* w_down, const void* dy, int64_t m, const void* gate,
+                          const void* up, void* d_gate, void* d_up, void* workspace,
+                          size_t workspace_bytes, fitq_stream_t stream) {
+  fitq::Nf4Args a;
+  int rc = check_weight(w_down, &a);
+  if (rc) return rc;
+  if (!dy || !gate || !up || !d_gate || !d_up)
+    return fail(FITQ_ERR_ARG, "down_dswiglu: dy, gate, up, d_gate and d_up are required");
+  if (m <= 0 || m >= (1ll << 31)) return fail(FITQ_ERR_SHAPE, "down_dswiglu: bad M=%lld", (long long)m);
+  const int64_t N = a.n_out, K = a.k_in;  // dX [M, K] = dy [M, N] . W [N, K]
+  if (N % 64 != 0 || K % 16 != 0)
+    return fail(FITQ_ERR_SHAPE, "down_dswiglu: need N %% 64 == 0 and K %% 16 == 0 (N=%lld K=%lld)",
+                (long long)N, (long long)K);
+  if (!al16(dy) || !al16(gate) || !al16(up) || !al16(d_gate) || !al16(d_up))
+    return fail(FITQ_ERR_ALIGN, "down_dswiglu: 16-byte alignment");
+  const size_t need = fitq_nf4_down_dswiglu_workspace(m, N, K);
+  if (!workspace || workspace_bytes < need)
+    return fail(FITQ_ERR_WORKSPACE, "down_dswiglu: workspace %zu < %zu bytes", workspace_bytes, need);
+  int sms = current_sms(&rc);
+  if (!sms) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = fitq::launch_nf4_dequant(a, workspace, FITQ_DTYPE_BF16, 1, st, sms)))
+    return launch_status(rc, "nf4_dequant (transposed)");
+  fitq::GemmArgs g{};
+  g.a = dy; g.lda = N;
+  g.b = workspace; g.ldb = N;
+  g.c = d_gate; g.ldc = K;
+  g.m = m; g.n = K; g.k = N;
+  g.epi = fitq::GEMM_EPI_DSWIGLU;
+  g.src0 = gate; g.src1 = up; g.aux0 = d_up;
+  g.status = status_ptr();
+  return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm (down dX + SwiGLU backward)");
+}
+
 int fitq_gemm_bf16_tn(const void* a, const void* b, void* c, const void* c_add, int64_t m,
                       int64_t n, int64_t k, fitq_stream_t stream) {
   if (!a || !b || !c) return fail(FITQ_ERR_ARG, "gemm: NULL operand");

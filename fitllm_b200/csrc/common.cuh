@@ -207,4 +207,16 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
 
 __device__ __forceinline__ bool elect_one_lane() { return (threadIdx.x & 31) == 0; }
 
+// ---------------------------------------------------------------- SwiGLU
+// act = silu(g) * u and its gradient, fp32 on bf16-valued inputs; shared by
+// the elementwise kernels and the GEMM epilogues so both give the same bits.
+__device__ __forceinline__ float sigmoidf_(float g) { return 1.0f / (1.0f + __expf(-g)); }
+__device__ __forceinline__ float swiglu_elem(float g, float u) { return g * sigmoidf_(g) * u; }
+// dg = d * u * s * (1 + g (1 - s)),  du = d * g * s,   s = sigmoid(g)
+__device__ __forceinline__ void swiglu_grad_elem(float d, float g, float u, float& dg, float& du) {
+  const float s = sigmoidf_(g);
+  dg = d * u * s * (1.0f + g * (1.0f - s));
+  du = d * g * s;
+}
+
 }  // namespace fitq

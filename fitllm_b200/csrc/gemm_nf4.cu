@@ -359,9 +359,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int dw = warp - DEC_WARP0;
     const int group = dw >> 2;           // takes the K steps of this parity
     const int u = (dw & 3) * 32 + lane;  // unit: one 64-weight NF4 block of one W row
-    float qm[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) qm[i] = __ldg(p.qm + i);
+    uint64_t qm[8];
+    nf4_load_qm_pairs(p.qm, qm);
     // Unit geometry within the stage.
     //   forward: W row nb*128 + u, block kb; operand row u (K-major).
     //   dX:      W row kb*64 + u/2, block nb*2 + (u & 1); K-row u/2 of the

@@ -384,9 +384,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int dw = warp - DEC_WARP0;
     const int group = dw >> 2;
     const int u = (dw & 3) * 32 + lane;  // unit: one 64-weight NF4 block of one W row
-    float qm[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) qm[i] = __ldg(p.qm + i);
+    uint64_t qm[8];
+    nf4_load_qm_pairs(p.qm, qm);
     // forward: W row col0 + u, block kb -> operand row u (K-major);
     // dX: W row kb*64 + u/2, block col0/64 + (u & 1) -> K-row u/2, MN atom u & 1.
     const int r_local = p.trans ? (u >> 1) : u;

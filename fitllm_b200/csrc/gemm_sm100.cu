@@ -351,6 +351,7 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
 }
 
 int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms) {
+  if (g.epi != GEMM_EPI_PLAIN) return launch_gemm_bf16_tn_2cta(g, st, num_sms);  // pair-only epilogues
   const char* v = getenv("FITQ_GEMM_VARIANT");
   bool pair;
   if (v && v[0] == '1') {

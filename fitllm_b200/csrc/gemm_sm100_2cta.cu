@@ -47,6 +47,11 @@ struct Params {
   int num_m, num_n;
   int group_m;  // M-tiles per raster group (L2 reuse of the B tiles)  // in pair tiles
   int* status;
+  int epi;                        // GEMM_EPI_* (kernels.cuh)
+  const __nv_bfloat16* src0;      // DSWIGLU: gate [m, n]
+  const __nv_bfloat16* src1;      // DSWIGLU: up [m, n]
+  __nv_bfloat16* aux0;            // SWIGLU: gate out; DSWIGLU: d_up
+  __nv_bfloat16* aux1;            // SWIGLU: up out
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb,
@@ -75,7 +80,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tn_2cta_kernel(const __grid_constant__ CUtensorMap tm_a,
                              const __grid_constant__ CUtensorMap tm_b,
                              const __grid_constant__ CUtensorMap tm_pa,
-                             const __grid_constant__ CUtensorMap tm_pb, const Params p) {
+                             const __grid_constant__ CUtensorMap tm_pb,
+                             const __grid_constant__ CUtensorMap tm_b2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -141,7 +147,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         int mb, nb;
         tile_coords(tile, p.num_m, p.num_n, p.group_m, mb, nb);
         const int row_a = mb * 2 * BM + static_cast<int>(rank) * BM;
-        const int row_b = nb * BN + static_cast<int>(rank) * BN_HALF;
+        // gate/up in one launch: CTA 0 of the pair loads gate rows, CTA 1 up
+        // rows, so both CTAs' accumulators hold matching gate | up columns
+        const bool two_b = p.epi == GEMM_EPI_SWIGLU;
+        const int row_b = two_b ? nb * BN_HALF : nb * BN + static_cast<int>(rank) * BN_HALF;
+        const CUtensorMap* tmb = two_b && rank == 1 ? &tm_b2 : &tm_b;
         bool ok = true;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
@@ -153,7 +163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           if (kb < num_kb) {
             tma_load_2d_pair(sA + stage * A_BYTES, &tm_a, bar, kb * BK, row_a);
-            tma_load_2d_pair(sB + stage * B_BYTES, &tm_b, bar, kb * BK, row_b);
+            tma_load_2d_pair(sB + stage * B_BYTES, tmb, bar, kb * BK, row_b);
           } else {
             tma_load_2d_pair(sA + stage * A_BYTES, &tm_pa, bar, 0, row_a);
             tma_load_2d_pair(sB + stage * B_BYTES, &tm_pb, bar, 0, row_b);
@@ -219,6 +229,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const bool row_ok = row < p.m;
       __nv_bfloat16* crow = p.c + (int64_t)row * p.ldc;
       const __nv_bfloat16* arow = p.c_add ? p.c_add + (int64_t)row * p.ldc_add : nullptr;
+      const uint32_t tlane = static_cast<uint32_t>(quarter * 32) << 16;
+      if (p.epi == GEMM_EPI_SWIGLU) {
+        // TMEM columns [0, 128): gate, [128, 256): up, for act columns nb*128 ..
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN_HALF / 32; ++chunk) {
+          const int col0 = nb * BN_HALF + chunk * 32;
+          uint32_t rg[32], ru[32];
+          tmem_ld_32x32b_x32(tmem_base + tlane + static_cast<uint32_t>(acc * BN + chunk * 32), rg);
+          tmem_ld_32x32b_x32(tmem_base + tlane + static_cast<uint32_t>(acc * BN + BN_HALF + chunk * 32), ru);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = col0 + v * 8;
+              uint32_t gp[4], up[4], ap[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                gp[j] = pack_bf16x2(__uint_as_float(rg[v * 8 + 2 * j]), __uint_as_float(rg[v * 8 + 2 * j + 1]));
+                up[j] = pack_bf16x2(__uint_as_float(ru[v * 8 + 2 * j]), __uint_as_float(ru[v * 8 + 2 * j + 1]));
+                const float2 g2 = unpack_bf16x2(gp[j]), u2 = unpack_bf16x2(up[j]);
+                ap[j] = pack_bf16x2(swiglu_elem(g2.x, u2.x), swiglu_elem(g2.y, u2.y));
+              }
+              const int64_t o = (int64_t)row * p.ldc + col;
+              *reinterpret_cast<uint4*>(p.c + o) = make_uint4(ap[0], ap[1], ap[2], ap[3]);
+              if (p.aux0) *reinterpret_cast<uint4*>(p.aux0 + o) = make_uint4(gp[0], gp[1], gp[2], gp[3]);
+              if (p.aux1) *reinterpret_cast<uint4*>(p.aux1 + o) = make_uint4(up[0], up[1], up[2], up[3]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) remote_arrive(tempty_leader[acc]);
+        if (++acc == NUM_ACC) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
 #pragma unroll 1
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         const int col0 = nb * BN + chunk * 32;
@@ -236,6 +281,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
               float f[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[v * 8 + j]);
+              if (p.epi == GEMM_EPI_DSWIGLU) {
+                // d = bf16(product); gate / up rows at the same columns
+                const int64_t o = (int64_t)row * p.ldc + col;
+                const uint4 gq = *reinterpret_cast<const uint4*>(p.src0 + o);
+                const uint4 uq = *reinterpret_cast<const uint4*>(p.src1 + o);
+                const uint32_t ga[4] = {gq.x, gq.y, gq.z, gq.w}, ua[4] = {uq.x, uq.y, uq.z, uq.w};
+                uint32_t dg[4], du[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 d2 = unpack_bf16x2(pack_bf16x2(f[2 * j], f[2 * j + 1]));
+                  const float2 g2 = unpack_bf16x2(ga[j]), u2 = unpack_bf16x2(ua[j]);
+                  float g0, g1, u0, u1;
+                  swiglu_grad_elem(d2.x, g2.x, u2.x, g0, u0);
+                  swiglu_grad_elem(d2.y, g2.y, u2.y, g1, u1);
+                  dg[j] = pack_bf16x2(g0, g1);
+                  du[j] = pack_bf16x2(u0, u1);
+                }
+                *reinterpret_cast<uint4*>(crow + col) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+                *reinterpret_cast<uint4*>(p.aux0 + o) = make_uint4(du[0], du[1], du[2], du[3]);
+                continue;
+              }
               if (p.bias) add_bf16x8(f, p.bias + col);
               if (arow) add_bf16x8(f, arow + col);
               uint4 o;
@@ -304,9 +370,19 @@ constexpr int kMaxDev = 64;
 }  // namespace
 
 int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms) {
-  CUtensorMap ta, tb, tpa, tpb;
+  CUtensorMap ta, tb, tpa, tpb, tb2;
+  const bool two_b = g.epi == GEMM_EPI_SWIGLU;
+  if (two_b && (g.n % BN_HALF != 0 || g.b2 == nullptr || g.lora_k != 0 || g.bias || g.c_add))
+    return FITQ_ERR_UNSUPPORTED;
+  if (g.epi == GEMM_EPI_DSWIGLU && (!g.src0 || !g.src1 || !g.aux0 || g.bias || g.c_add))
+    return FITQ_ERR_UNSUPPORTED;
   if (!make_tmap(&ta, g.a, g.m, g.k, g.lda, BM)) return FITQ_ERR_CUDA;
   if (!make_tmap(&tb, g.b, g.n, g.k, g.ldb, BN_HALF)) return FITQ_ERR_CUDA;
+  if (two_b) {
+    if (!make_tmap(&tb2, g.b2, g.n, g.k, g.ldb, BN_HALF)) return FITQ_ERR_CUDA;
+  } else {
+    tb2 = tb;
+  }
   if (g.lora_k) {
     if (!make_tmap(&tpa, g.pa, g.m, 64, 64, BM)) return FITQ_ERR_CUDA;
     if (!make_tmap(&tpb, g.pb, g.n, 64, 64, BN_HALF)) return FITQ_ERR_CUDA;
@@ -325,8 +401,13 @@ int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms) {
   p.k = static_cast<int>(g.k);
   p.lora_k = g.lora_k;
   p.num_m = static_cast<int>((g.m + 2 * BM - 1) / (2 * BM));
-  p.num_n = static_cast<int>((g.n + BN - 1) / BN);
+  p.num_n = two_b ? static_cast<int>(g.n / BN_HALF) : static_cast<int>((g.n + BN - 1) / BN);
   p.status = g.status;
+  p.epi = g.epi;
+  p.src0 = static_cast<const __nv_bfloat16*>(g.src0);
+  p.src1 = static_cast<const __nv_bfloat16*>(g.src1);
+  p.aux0 = static_cast<__nv_bfloat16*>(g.aux0);
+  p.aux1 = static_cast<__nv_bfloat16*>(g.aux1);
   {
     const char* gm = getenv("FITQ_GEMM_GROUP_M");
     // 16 pair tiles (4,096 rows) per group when there are many N tiles: half
@@ -348,9 +429,9 @@ int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms) {
   const int tiles = p.num_m * p.num_n;
   const int clusters = tiles < num_sms / 2 ? tiles : num_sms / 2;
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *
-                       static_cast<double>(g.k + g.lora_k);
+                       static_cast<double>(g.k + g.lora_k) * (two_b ? 2.0 : 1.0);
   const int slot = timing_begin(st, flops);
-  gemm_bf16_tn_2cta_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, p);
+  gemm_bf16_tn_2cta_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, tb2, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

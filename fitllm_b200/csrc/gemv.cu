@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(256)
       for (int sl = 0; sl < slices; ++sl) u += __ldcg(o2.partial + sl * total + e);
       const float a = __bfloat162float(__float2bfloat16_rn(dec_value(out, nullptr, N, tk, n, v)));
       const float b = __bfloat162float(__float2bfloat16_rn(dec_value(o2, nullptr, N, tk, n, u)));
-      gf.act[e] = __float2bfloat16_rn(a * (1.0f / (1.0f + __expf(-a))) * b);
+      gf.act[e] = __float2bfloat16_rn(swiglu_elem(a, b));
     }
   }
 }

@@ -44,7 +44,21 @@ struct GemmArgs {
   int64_t m, n, k;
   int lora_k;
   int* status;  // device status word (bounded-wait timeouts)
+  // Epilogue modes of the pair kernel (launch_gemm_bf16_tn_2cta):
+  //   GEMM_EPI_SWIGLU: gate and up in one launch -- b = W_gate, b2 = W_up
+  //     (bf16 [n, k] each, pitch ldb); c[m, n] = silu(g) * u of the
+  //     bf16-rounded products g = a.W_gate^T, u = a.W_up^T; g, u also stored
+  //     into aux0 / aux1 (pitch ldc) when non-null.  No LoRA, bias or c_add.
+  //   GEMM_EPI_DSWIGLU: with d = bf16(a.b^T), g = src0, u = src1 (bf16
+  //     [m, n], pitch ldc): c = d(silu(g) * u)/dg, aux0 = .../du.
+  int epi;
+  const void* b2;
+  const void* src0;
+  const void* src1;
+  void* aux0;
+  void* aux1;
 };
+constexpr int GEMM_EPI_PLAIN = 0, GEMM_EPI_SWIGLU = 1, GEMM_EPI_DSWIGLU = 2;
 int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms);
 // Same contract on CTA pairs (cta_group::2, 256x256 tiles), gemm_sm100_2cta.cu.
 int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms);

@@ -221,7 +221,6 @@ __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ q, const __
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float g) { return 1.0f / (1.0f + __expf(-g)); }
 
 // act = silu(g) * u
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ g,
@@ -233,7 +232,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ g,
     load8(g + e * 8, a);
     load8(u + e * 8, b);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = a[i] * sigmoidf_(a[i]) * b[i];
+    for (int i = 0; i < 8; ++i) a[i] = swiglu_elem(a[i], b[i]);
     store8(act + e * 8, a);
   }
 }
@@ -251,11 +250,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ d,
     load8(g + e * 8, a);
     load8(u + e * 8, b);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float s = sigmoidf_(a[i]);
-      og[i] = dd[i] * b[i] * s * (1.0f + a[i] * (1.0f - s));
-      ou[i] = dd[i] * a[i] * s;
-    }
+    for (int i = 0; i < 8; ++i) swiglu_grad_elem(dd[i], a[i], b[i], og[i], ou[i]);
     store8(dg + e * 8, og);
     store8(du + e * 8, ou);
   }

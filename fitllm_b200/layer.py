@@ -11,11 +11,14 @@ shard keys of fitllm/forward.py:95-109 load unchanged, and runs:
 * every projection as an NF4 ``Linear4bit`` / ``QLoRALinear4bit`` on the
   sm_100a kernels (the residual adds of o_proj and down_proj ride in the GEMM
   epilogue);
-* RMSNorm, the rotary embedding and SwiGLU as fused one-pass kernels of the
-  same library (layer_ops.cu); attention with torch SDPA (library kernel).
+* RMSNorm and the rotary embedding as fused one-pass kernels of the same
+  library (layer_ops.cu); gate/up as one GEMM with SwiGLU in its epilogue and
+  the SwiGLU backward in down_proj's dX epilogue; attention with torch SDPA
+  (library kernel).
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Optional, Sequence, Tuple
 
@@ -134,14 +137,63 @@ class Attention(nn.Module):
         return self.o_proj(o, residual=residual)
 
 
+class _FusedMLPFn(torch.autograd.Function):
+    """out = down(silu(gate(x)) * up(x)) + residual with plain NF4 projections.
+
+    Forward: gate and up as one GEMM whose epilogue applies the SwiGLU, then
+    down_proj with the residual in its epilogue.  Backward: down_proj's dX
+    GEMM applies the SwiGLU backward in its epilogue (d_gate, d_up), then the
+    gate and up dX GEMMs accumulate into one dx.  Bit-identical to the
+    separate projections + SwiGLU kernels (same GEMMs, same epilogue math)."""
+
+    @staticmethod
+    def forward(ctx, x, residual, wg, wu, wd):
+        from . import ops
+        lead = x.shape[:-1]
+        x2 = ops._bf16_2d(x, wg.c.k_in)
+        keep = ctx.needs_input_grad[0]
+        act, gate, up = ops.nf4_gateup_swiglu(x2, wg, wu, keep_gate_up=keep)
+        res2 = ops._bf16_2d(residual, wd.c.n_out)
+        y, _ = ops.qlora_forward(act, wd, None, None, 1.0, y_add=res2)
+        ctx.refs = (wg, wu, wd)
+        ctx.lead = lead
+        ctx.save_for_backward(gate, up)
+        return y.view(*lead, wd.c.n_out)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        gate, up = ctx.saved_tensors
+        wg, wu, wd = ctx.refs
+        dy2 = ops._bf16_2d(dy, wd.c.n_out)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            d_gate, d_up = ops.nf4_down_dswiglu(dy2, wd, gate, up)
+            dx, _, _ = ops.qlora_backward(None, d_gate, wg, None, None, 1.0)
+            ops.qlora_backward(None, d_up, wu, None, None, 1.0, dx=dx)
+            dx = dx.view(*ctx.lead, wg.c.k_in)
+        dres = dy if ctx.needs_input_grad[1] else None
+        return dx, dres, None, None, None
+
+
+def _plain_nf4(mod) -> bool:
+    return isinstance(mod, Linear4bit) and mod.bias is None and mod.quant_state is not None
+
+
 class MLP(nn.Module):
     def __init__(self, cfg: LayerConfig, device=None):
         super().__init__()
         self.gate_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
         self.up_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
         self.down_proj = Linear4bit(cfg.intermediate, cfg.hidden, device=device)
+        # gate/up + SwiGLU in one GEMM, SwiGLU backward in down's dX (FITQ_MLP_FUSED=0: separate)
+        self.fused = os.environ.get("FITQ_MLP_FUSED", "1") != "0"
 
     def forward(self, x, residual):
+        if (self.fused and x.is_cuda and _plain_nf4(self.gate_proj) and _plain_nf4(self.up_proj)
+                and _plain_nf4(self.down_proj) and self.gate_proj.out_features % 128 == 0):
+            return _FusedMLPFn.apply(x, residual, self.gate_proj.wref(), self.up_proj.wref(),
+                                     self.down_proj.wref())
         return self.down_proj(swiglu(self.gate_proj(x), self.up_proj(x)), residual=residual)
 
 

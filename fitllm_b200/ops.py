@@ -162,6 +162,47 @@ def nf4_gemv_swiglu(x2: torch.Tensor, gate_job, up_job) -> torch.Tensor:
     return act
 
 
+def nf4_gateup_swiglu(x2: torch.Tensor, w_gate: Nf4WeightCRef, w_up: Nf4WeightCRef,
+                      keep_gate_up: bool = False):
+    """act = silu(x.Wg^T) * (x.Wu^T) as ONE tcgen05 GEMM over both NF4 weights
+    (fitq_nf4_gateup_swiglu).  x2: bf16 [M, K].  Returns (act, gate, up), bf16
+    [M, N]; gate / up only with keep_gate_up (for the backward), else None."""
+    L = _lib.load()
+    m = x2.shape[0]
+    n, k = w_gate.c.n_out, w_gate.c.k_in
+    dev = x2.device
+    act = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    gate = torch.empty_like(act) if keep_gate_up else None
+    up = torch.empty_like(act) if keep_gate_up else None
+    with torch.cuda.device(dev):
+        nbytes = L.fitq_nf4_gateup_swiglu_workspace(m, n, k)
+        ws = _workspace(nbytes, dev)
+        _lib.check(L.fitq_nf4_gateup_swiglu(w_gate.ref, w_up.ref, x2.data_ptr(), m, act.data_ptr(),
+                                            _lib.ptr(gate), _lib.ptr(up), ws.data_ptr(), nbytes,
+                                            _stream(dev)), "fitq_nf4_gateup_swiglu")
+    return act, gate, up
+
+
+def nf4_down_dswiglu(dy2: torch.Tensor, w_down: Nf4WeightCRef, gate: torch.Tensor,
+                     up: torch.Tensor):
+    """(d_gate, d_up) of act = silu(gate) * up through down_proj: the dX GEMM of
+    down_proj with the SwiGLU backward in its epilogue (fitq_nf4_down_dswiglu)."""
+    L = _lib.load()
+    m = dy2.shape[0]
+    k = w_down.c.k_in
+    dev = dy2.device
+    d_gate = torch.empty(m, k, dtype=torch.bfloat16, device=dev)
+    d_up = torch.empty_like(d_gate)
+    with torch.cuda.device(dev):
+        nbytes = L.fitq_nf4_down_dswiglu_workspace(m, w_down.c.n_out, k)
+        ws = _workspace(nbytes, dev)
+        _lib.check(L.fitq_nf4_down_dswiglu(w_down.ref, dy2.data_ptr(), m, gate.data_ptr(),
+                                           up.data_ptr(), d_gate.data_ptr(), d_up.data_ptr(),
+                                           ws.data_ptr(), nbytes, _stream(dev)),
+                   "fitq_nf4_down_dswiglu")
+    return d_gate, d_up
+
+
 def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                      prefix: int) -> torch.Tensor:
     """Attention of T new tokens over a KV cache (fitq_verify_attention).

@@ -289,6 +289,30 @@ FITQ_API int fitq_verify_attention(const void* q, const void* k_cache, const voi
 FITQ_API int fitq_swiglu_bwd(const void* d_act, const void* gate, const void* up, void* d_gate,
                              void* d_up, int64_t n, fitq_stream_t stream);
 
+/* The MLP input of a Qwen2 decoder layer, act_fn(gate_proj(x)) * up_proj(x)
+ * (HF Qwen2MLP as FitLLM runs it, fitllm/forward.py:680-686), as ONE tcgen05
+ * GEMM over both NF4 weights: each output tile holds matching gate and up
+ * columns and the epilogue stores act = silu(g) * u of the bf16-rounded
+ * products g, u (the arithmetic of fitq_swiglu_fwd, so the result is
+ * bit-identical to two fitq_qlora_fwd calls + fitq_swiglu_fwd).  gate_out /
+ * up_out (bf16 [m, N], may be NULL) receive g and u for the backward.  The two
+ * weights have the same shape [N, K], N % 128 == 0, no bias or LoRA. */
+FITQ_API size_t fitq_nf4_gateup_swiglu_workspace(int64_t m, int64_t n_out, int64_t k_in);
+FITQ_API int fitq_nf4_gateup_swiglu(const fitq_nf4_weight* w_gate, const fitq_nf4_weight* w_up,
+                                    const void* x, int64_t m, void* act, void* gate_out,
+                                    void* up_out, void* workspace, size_t workspace_bytes,
+                                    fitq_stream_t stream);
+/* down_proj's input gradient fused with the SwiGLU backward (the autograd of
+ * down_proj(act_fn(gate) * up) at h_out.backward, fitllm/backward.py:234):
+ * d_act = dy [m, N] . W_down [N, K] rounded to bf16, then d_gate and d_up
+ * (bf16 [m, K]) from the saved gate / up with the arithmetic of
+ * fitq_swiglu_bwd -- bit-identical to fitq_qlora_bwd (dX) + fitq_swiglu_bwd;
+ * d_act itself is never stored.  No LoRA on down_proj. */
+FITQ_API size_t fitq_nf4_down_dswiglu_workspace(int64_t m, int64_t n_out, int64_t k_in);
+FITQ_API int fitq_nf4_down_dswiglu(const fitq_nf4_weight* w_down, const void* dy, int64_t m,
+                                   const void* gate, const void* up, void* d_gate, void* d_up,
+                                   void* workspace, size_t workspace_bytes, fitq_stream_t stream);
+
 /* Number of kernels this library has launched in this process so far. */
 FITQ_API long long fitq_launch_count(void);
 
