@@ -186,8 +186,11 @@ class MLP(nn.Module):
         self.gate_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
         self.up_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
         self.down_proj = Linear4bit(cfg.intermediate, cfg.hidden, device=device)
-        # gate/up + SwiGLU in one GEMM, SwiGLU backward in down's dX (FITQ_MLP_FUSED=0: separate)
-        self.fused = os.environ.get("FITQ_MLP_FUSED", "1") != "0"
+        # FITQ_MLP_FUSED=1: gate/up + SwiGLU in one GEMM, SwiGLU backward in
+        # down's dX.  Off by default: on a power-capped B200 the Qwen2.5-32B
+        # layer step measured 3-6% slower with it (the fused GEMMs ran at a
+        # lower SM clock) although it removes three element-wise passes.
+        self.fused = os.environ.get("FITQ_MLP_FUSED", "0") == "1"
 
     def forward(self, x, residual):
         if (self.fused and x.is_cuda and _plain_nf4(self.gate_proj) and _plain_nf4(self.up_proj)

@@ -75,6 +75,7 @@ def test_mlp_module_fused_vs_unfused(cuda_dev, m, hidden, inter):
     from fitllm_b200.qlora import Linear4bit
     cfg = LayerConfig(hidden=hidden, intermediate=inter, heads=4, kv_heads=2, head_dim=hidden // 4)
     mlp = MLP(cfg, device=cuda_dev)
+    assert not mlp.fused  # opt-in (FITQ_MLP_FUSED=1)
     g = torch.Generator(device=cuda_dev).manual_seed(inter)
     dense = {}
     for name, (o, i) in {"gate_proj": (inter, hidden), "up_proj": (inter, hidden),
