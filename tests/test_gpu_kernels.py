@@ -171,6 +171,9 @@ def test_gemv_paths(cuda_dev, m, n, k, r):
 
 @pytest.mark.parametrize("variant", ["default", "wide", "tc"])
 @pytest.mark.parametrize("m,n,k,r,nested", [(1, 2048, 5120, 16, True), (3, 512, 27648, 0, True),
+                                            (2, 1024, 5120, 16, True), (4, 2048, 1024, 0, False),
+                                            (1, 6912, 5120, 0, True), (2, 1280, 27648, 0, True),
+                                            (1, 640, 2048, 0, False), (4, 1536, 4096, 32, True),
                                             (8, 3072, 1024, 16, False), (5, 1024, 5120, 0, False),
                                             (1, 128, 256, 0, True), (16, 2048, 5120, 16, True),
                                             (40, 1024, 5120, 16, True), (64, 512, 1024, 0, False),
@@ -202,7 +205,8 @@ def test_gemv_decode_kernels(cuda_dev, monkeypatch, variant, m, n, k, r, nested)
     assert ops.device_status() == 0
 
 
-@pytest.mark.parametrize("m,n,k,r", [(1, 2048, 5120, 16), (4, 1024, 27648, 0), (8, 512, 1024, 32)])
+@pytest.mark.parametrize("m,n,k,r", [(1, 2048, 5120, 16), (4, 1024, 27648, 0), (8, 512, 1024, 32),
+                                     (2, 5120, 5120, 16), (1, 6912, 5120, 0)])
 def test_gemv_decode_deterministic(cuda_dev, monkeypatch, m, n, k, r):
     """The decode path (GEMV, LoRA T and finishing launches) gives the same
     bits on three calls over one reused workspace, within the 1e-2 contract of
