@@ -18,7 +18,7 @@ ERRORS = {
     1: "FITQ_ERR_ARG", 2: "FITQ_ERR_SHAPE", 3: "FITQ_ERR_ALIGN", 4: "FITQ_ERR_UNSUPPORTED",
     5: "FITQ_ERR_WORKSPACE", 6: "FITQ_ERR_CUDA", 7: "FITQ_ERR_TIMEOUT", 8: "FITQ_ERR_NO_DEVICE",
 }
-DTYPE_BF16, DTYPE_F16 = 0, 1
+DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 
 # Every symbol include/fitq.h declares, with (restype, argtypes).
 P, I32, I64, F32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -67,6 +67,7 @@ SIGNATURES = {
     "fitq_timing_read": (I32, [P, P, I32]),
     "fitq_launch_count": (ctypes.c_longlong, []),
     "fitq_nf4_gemv_noalloc": (I32, [WP, P, I64, P, P, I32, F32, P, P, P, P]),
+    "fitq_lora_merge": (I32, [P, I32, I64, I64, P, P, I32, F32, P]),
     "fitq_nf4_gateup_swiglu_workspace": (SZ, [I64, I64, I64]),
     "fitq_nf4_gateup_swiglu": (I32, [WP, WP, P, I64, P, P, P, P, SZ, P]),
     "fitq_nf4_down_dswiglu_workspace": (SZ, [I64, I64, I64]),

@@ -759,6 +759,27 @@ int fitq_nf4_gateup_swiglu(const fitq_nf4_weight* w_gate, const fitq_nf4_weight*
   return launch_status(fitq::launch_gemm(a, st, sms), "tcgen05 gemm (gate/up + SwiGLU)");
 }
 
+int fitq_lora_merge(void* w, int w_dtype, int64_t n_out, int64_t k_in, const float* lora_a,
+                    const float* lora_b, int rank, float scale, fitq_stream_t stream) {
+  if (!w || !lora_a || !lora_b) return fail(FITQ_ERR_ARG, "lora_merge: w, lora_a and lora_b are required");
+  if (w_dtype != FITQ_DTYPE_BF16 && w_dtype != FITQ_DTYPE_F16 && w_dtype != FITQ_DTYPE_F32)
+    return fail(FITQ_ERR_ARG, "lora_merge: unknown w_dtype %d", w_dtype);
+  if (n_out <= 0 || k_in <= 0 || (k_in & 1) || n_out >= (1ll << 31) || k_in >= (1ll << 31) ||
+      (n_out + 15) / 16 > 65535)
+    return fail(FITQ_ERR_SHAPE, "lora_merge: bad shape N=%lld K=%lld (K even)", (long long)n_out,
+                (long long)k_in);
+  if (rank < 1 || rank > 256) return fail(FITQ_ERR_SHAPE, "lora_merge: rank %d not in 1..256", rank);
+  if ((reinterpret_cast<uintptr_t>(w) & (w_dtype == FITQ_DTYPE_F32 ? 7u : 3u)) ||
+      (reinterpret_cast<uintptr_t>(lora_a) & 7u) ||
+      (reinterpret_cast<uintptr_t>(lora_b) & 3u))
+    return fail(FITQ_ERR_ALIGN, "lora_merge: w 4-byte (fp32: 8-byte), lora_a 8-byte, lora_b 4-byte alignment");
+  int rc = 0;
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_lora_merge(w, w_dtype, n_out, k_in, lora_a, lora_b, rank, scale,
+                                               static_cast<cudaStream_t>(stream)),
+                       "lora_merge");
+}
+
 size_t fitq_nf4_down_dswiglu_workspace(int64_t m, int64_t n_out, int64_t k_in) {
   (void)m;
   Carve c{nullptr, 0};

@@ -241,6 +241,9 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
 int timing_begin(cudaStream_t st, double flops);
 // Counts kernel launches made by the library (read by fitq_launch_count).
 void note_launch();
+// W[n,k] (bf16 / fp16, in place) += scale * (B[n,:] . A[:,k]); see merge.cu.
+int launch_lora_merge(void* w, int out_dtype, int64_t n, int64_t k, const float* a, const float* b,
+                      int rank, float scale, cudaStream_t st);
 
 // One thread waits with mbar_wait_for on an mbarrier nothing completes; after
 // limit_ns it records FITQ_ERR_TIMEOUT in *status and returns (selftest.cu).

@@ -87,8 +87,9 @@ typedef struct fitq_nf4_weight {
   int64_t k_in;
 } fitq_nf4_weight;
 
-/* Output dtypes of fitq_nf4_dequant. */
-enum { FITQ_DTYPE_BF16 = 0, FITQ_DTYPE_F16 = 1 };
+/* Output dtypes of fitq_nf4_dequant (bf16, fp16) and weight dtypes of
+ * fitq_lora_merge (all three). */
+enum { FITQ_DTYPE_BF16 = 0, FITQ_DTYPE_F16 = 1, FITQ_DTYPE_F32 = 2 };
 
 FITQ_API const char* fitq_version(void);
 
@@ -312,6 +313,20 @@ FITQ_API size_t fitq_nf4_down_dswiglu_workspace(int64_t m, int64_t n_out, int64_
 FITQ_API int fitq_nf4_down_dswiglu(const fitq_nf4_weight* w_down, const void* dy, int64_t m,
                                    const void* gate, const void* up, void* d_gate, void* d_up,
                                    void* workspace, size_t workspace_bytes, fitq_stream_t stream);
+
+/* LoRA merge into a dense weight, in place: W[N,K] <- W + scale * (B . A),
+ * the per-weight step of FitLLM's merge_lora_into_shards
+ * (fitllm/inference.py:127-131: (W.float() + scale * (B @ A)).to(dtype)).
+ * w: bf16, fp16 or fp32 (w_dtype FITQ_DTYPE_BF16 / _F16 / _F32), row-major,
+ * 4-byte (fp32: 8-byte) aligned, K even; lora_a fp32 [rank, K] (8-byte aligned), lora_b
+ * fp32 [N, rank]; 1 <= rank <= 256.  Per element the rank sum runs in fp32
+ * in rank order with every product and sum rounded, then
+ * fl(W + fl(scale * sum)) is rounded to w's dtype.  An NF4 weight is merged
+ * by dequantising it (fitq_nf4_dequant), merging, and re-quantising
+ * (fitq_nf4_quantize). */
+FITQ_API int fitq_lora_merge(void* w, int w_dtype, int64_t n_out, int64_t k_in,
+                             const float* lora_a, const float* lora_b, int rank, float scale,
+                             fitq_stream_t stream);
 
 /* Number of kernels this library has launched in this process so far. */
 FITQ_API long long fitq_launch_count(void);
