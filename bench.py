@@ -52,6 +52,10 @@ def parse():
                     help="B,H,KVH,T,prefix: run the verify attention on one shape and exit")
     ap.add_argument("--ce-case", default=None,
                     help="rows,vocab: run the cross-entropy kernel on one shape and exit")
+    ap.add_argument("--qproj-case", action="store_true",
+                    help="run only the q_proj QLoRA fwd+bwd (512 x 5120 x 5120, r=16) and exit")
+    ap.add_argument("--decode-case", default=None,
+                    help="layers,batch,drafts: run only the decode / verify pass and exit")
     ap.add_argument("--full-step", choices=["auto", "on", "off"], default="auto",
                     help="also time a full 64-layer step with shards streamed from pinned host "
                          "memory (each rank pins only its 1/N byte range of every layer)")
@@ -317,16 +321,10 @@ def qproj_linear(dev, reps=20, cpu=True):
     return out
 
 
-def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, reps=10, cpu=True):
-    """BASELINE config 5: one speculative-verify pass over 64 random-init NF4
-    Qwen2.5-32B-shaped layers (LoRA r=16 on q/v), batch 8 x (4 draft + 1)
-    tokens against a 4096-position KV cache -> every projection an M = 40 NF4
-    GEMM.  CUDA-graph replay; bytes = NF4 weights + KV read per pass."""
-    import torch
+def nf4_layers(dev, layers_n=64):
+    """64 random-init NF4 Qwen2.5-32B-shaped layers with LoRA r=16 on q/v."""
     from fitllm_b200.layer import DecoderLayer, LayerConfig, add_lora_, quantize_layer_
-    from fitllm_b200.verify import KVCache, verify_pass
     cfg = LayerConfig.qwen25_32b()
-    t = drafts + 1
     layers = []
     for i in range(layers_n):
         layer = DecoderLayer(cfg, device=dev)
@@ -334,6 +332,22 @@ def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, re
         add_lora_(layer, cfg.lora_rank, cfg.lora_alpha, cfg.lora_targets, seed=i, b_std=0.01)
         layer.eval()
         layers.append(layer)
+    return layers
+
+
+def verify_bench(dev, peak_gbs, layers, batch=8, drafts=4, context=4096, reps=10, cpu=True):
+    """BASELINE config 5: one speculative-verify pass over 64 random-init NF4
+    Qwen2.5-32B-shaped layers (LoRA r=16 on q/v), batch 8 x (4 draft + 1)
+    tokens against a 4096-position KV cache -> every projection an M = 40 NF4
+    GEMM; with batch 1 and no drafts, the single-token decode pass (every
+    projection an M = 1 NF4 GEMV).  CUDA-graph replay; bytes = NF4 weights +
+    KV read per pass."""
+    import torch
+    from fitllm_b200.layer import LayerConfig
+    from fitllm_b200.verify import KVCache, verify_pass
+    cfg = LayerConfig.qwen25_32b()
+    t = drafts + 1
+    layers_n = len(layers)
     cache = KVCache(layers_n, batch, cfg.kv_heads, cfg.head_dim, context + t, dev)
     cache.fill_random_(context, seed=3)
     g = torch.Generator(device=dev).manual_seed(4)
@@ -356,14 +370,17 @@ def verify_bench(dev, peak_gbs, layers_n=64, batch=8, drafts=4, context=4096, re
                          4 * ((cfg.nf4_weights_per_layer() // 64 + 255) // 256))
     kv = cache.bytes_read(context + t)
     gbs = (wbytes + kv) / (ms / 1000.0) / 1e9
-    del graph, out, layers, cache
+    del graph, out, cache
     torch.cuda.empty_cache()
-    out = {"metric": "speculative verify pass, 64 NF4 layers, batch 8 x 5 tokens, KV 4096",
+    what = (f"speculative verify pass, {layers_n} NF4 layers, batch {batch} x {t} tokens, KV {context}"
+            if t > 1 else f"single-token decode pass, {layers_n} NF4 layers, batch {batch}, KV {context}")
+    out = {"metric": what,
            "ms_per_pass": round(ms, 3), "tokens_per_s": round(batch * t / (ms / 1000.0), 1),
            "bytes_per_pass": int(wbytes + kv), "GB/s": round(gbs, 1),
            "frac_of_hbm": round(gbs / peak_gbs, 3), "m_per_projection": batch * t,
-           "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs, attention on the "
-                   "split-KV verify kernel (fitq_verify_attention)"}
+           "note": "CUDA-graph replay; projections on the NF4 skinny GEMMs"
+                   + (" (M <= 8: the decode GEMV kernel)" if batch * t <= 8 else "")
+                   + ", attention on the split-KV verify kernel (fitq_verify_attention)"}
     if cpu:
         from oracle import layer_ref
         c = layer_ref.time_cpu_verify_layer(batch, t, context)
@@ -593,6 +610,16 @@ def main():
             if rank == 0:
                 print(json.dumps(fn(dev, case)), flush=True)
             return
+    if a.qproj_case:
+        print(json.dumps(qproj_linear(dev, cpu=False)), flush=True)
+        return
+    if a.decode_case:
+        n_layers, batch, drafts = (int(v) for v in a.decode_case.split(","))
+        pk_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        hbm = json.load(open(pk_path)).get("hbm_gbs", 6650.0) if os.path.exists(pk_path) else 6650.0
+        print(json.dumps(verify_bench(dev, hbm, nf4_layers(dev, n_layers), batch=batch, drafts=drafts,
+                                      cpu=False)), flush=True)
+        return
 
     cfg = LayerConfig.qwen25_32b()
     sched, store = build_synthetic_model(cfg, 1, dev, seed=0)
@@ -782,7 +809,11 @@ def main():
         out["full_step"] = full_step
     if world == 1 and not a.no_gemv:
         out["qproj_linear"] = qproj_linear(dev, cpu=not a.no_cpu_baseline)
-        out["verify"] = verify_bench(dev, peaks.get("hbm_gbs", 6650.0), cpu=not a.no_cpu_baseline)
+        layers = nf4_layers(dev)
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        out["verify"] = verify_bench(dev, hbm, layers, cpu=not a.no_cpu_baseline)
+        out["decode"] = verify_bench(dev, hbm, layers, batch=1, drafts=0, cpu=not a.no_cpu_baseline)
+        del layers
     if world == 1 and not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(a, a.cpu_seq)
     print(json.dumps(out), flush=True)
