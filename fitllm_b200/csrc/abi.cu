@@ -73,6 +73,72 @@ int* status_ptr() {
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// A second stream per device for the weight-side launches of one call (the
+// NF4 dequant and the LoRA weight padding), which depend on nothing the
+// activation-side launches (LoRA casts, row and column projections) produce:
+// the call forks it from the caller's stream, runs the two sides
+// concurrently and joins it back before the GEMM that needs both.  Fork and
+// join are an event record + stream wait each (both allowed during stream
+// capture, so a captured call captures the fork); a mutex keeps each
+// record/wait pair together when several host threads call in.  When the
+// stream cannot be created (or FITQ_SIDE_STREAM=0) the call runs on the
+// caller's stream alone, in the same order.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  bool tried = false;
+};
+std::mutex g_side_mu;
+
+SideStream* side_stream() {
+  static SideStream side[kMaxDevices];
+  static const bool off = [] {
+    const char* e = getenv("FITQ_SIDE_STREAM");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (off) return nullptr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_side_mu);
+  SideStream& ss = side[dev];
+  if (!ss.tried) {
+    ss.tried = true;
+    if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      ss.s = nullptr;
+    }
+  }
+  return ss.s ? &ss : nullptr;
+}
+
+// The stream the weight side runs on: the side stream after a fork from
+// `main`, else `main`.
+cudaStream_t fork_side(cudaStream_t main, SideStream* ss) {
+  if (!ss) return main;
+  std::lock_guard<std::mutex> lk(g_side_mu);
+  if (cudaEventRecord(ss->fork, main) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess) {
+    cudaGetLastError();
+    return main;
+  }
+  return ss->s;
+}
+
+// Make `main` wait for everything issued on `side` (no-op when side == main).
+int join_side(cudaStream_t main, cudaStream_t side, SideStream* ss) {
+  if (side == main) return FITQ_OK;
+  std::lock_guard<std::mutex> lk(g_side_mu);
+  if (cudaEventRecord(ss->join, side) != cudaSuccess || cudaStreamWaitEvent(main, ss->join, 0) != cudaSuccess)
+    return fail(FITQ_ERR_CUDA, "side stream join: %s", cudaGetErrorString(cudaGetLastError()));
+  return FITQ_OK;
+}
+
+
+
 int check_weight(const fitq_nf4_weight* w, fitq::Nf4Args* a) {
   if (!w) return fail(FITQ_ERR_ARG, "weight descriptor is NULL");
   if (!w->packed || !w->quant_map)
@@ -383,14 +449,29 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
                            "nf4_gemv decode finish");
     return FITQ_OK;
   }
+  // GEMM path: the weight side (s.B padding, NF4 dequant) on the side stream
+  // while T = x.A^T runs on the caller's stream; joined before the GEMM.
+  SideStream* ss = (!p.gemv && !p.fused) ? side_stream() : nullptr;
+  cudaStream_t wst = fork_side(st, ss);
+  int wrc = FITQ_OK;
+  const char* wwhat = "";
+  if (!p.gemv) {
+    if (rank > 0 && (wrc = fitq::launch_pad_lora_weight(lora_b, N, rank, scale, 0, p.b_pad, wst)))
+      wwhat = "lora B pad";
+    if (!wrc && !p.fused && (wrc = fitq::launch_nf4_dequant(a, p.wdeq, FITQ_DTYPE_BF16, 0, wst, sms)))
+      wwhat = "nf4_dequant";
+  }
   if (rank > 0) {
     rc = fitq::launch_f32_to_bf16(lora_a, static_cast<int64_t>(rank) * K, p.a_bf16, st);
-    if (rc) return launch_status(rc, "lora_a cast");
-    rc = p.t_part ? fitq::launch_lora_rowproj_small(x, K, m, K, p.a_bf16, rank, p.t_part, p.t_pad,
-                                                    t_out, st)
-                  : fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
-    if (rc) return launch_status(rc, "lora T = x.A^T");
+    if (!rc)
+      rc = p.t_part ? fitq::launch_lora_rowproj_small(x, K, m, K, p.a_bf16, rank, p.t_part, p.t_pad,
+                                                      t_out, st)
+                    : fitq::launch_lora_rowproj(x, K, m, K, p.a_bf16, rank, p.t_pad, t_out, st, sms);
   }
+  const int jrc = join_side(st, wst, ss);
+  if (wrc) return launch_status(wrc, wwhat);
+  if (rc) return launch_status(rc, "lora T = x.A^T");
+  if (jrc) return jrc;
   if (p.gemv) {
     int splits = 1;
     rc = fitq::launch_nf4_gemv_core(a, x, m, p.partial, st, sms, &splits);
@@ -398,10 +479,6 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
     rc = fitq::launch_gemv_finish(p.partial, splits, m, N, p.t_pad, lora_b, rank, scale, bias,
                                   y_add, y, st, sms);
     return launch_status(rc, "nf4_gemv finish");
-  }
-  if (rank > 0) {
-    rc = fitq::launch_pad_lora_weight(lora_b, N, rank, scale, 0, p.b_pad, st);
-    if (rc) return launch_status(rc, "lora B pad");
   }
   if (p.fused) {
     fitq::Nf4GemmArgs g{};
@@ -416,8 +493,6 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
     g.status = status_ptr();
     return launch_status(fitq::launch_gemm_nf4(g, st, sms), "tcgen05 nf4 gemm");
   }
-  rc = fitq::launch_nf4_dequant(a, p.wdeq, FITQ_DTYPE_BF16, 0, st, sms);
-  if (rc) return launch_status(rc, "nf4_dequant");
   fitq::GemmArgs g{};
   g.a = x; g.lda = K;
   g.b = p.wdeq; g.ldb = K;
@@ -620,6 +695,11 @@ size_t fitq_qlora_bwd_workspace(int64_t m, int64_t n_out, int64_t k_in, int rank
   return plan_bwd(c, m, n_out, k_in, rank, true, true, sms_for_sizing(), &p);
 }
 
+static int lora_bwd_side(const void* x, const void* dy, int64_t m, int64_t N, int64_t K,
+                         const float* lora_a, const float* lora_b, int rank, float scale,
+                         const void* t_saved, bool need_t, float* grad_a, float* grad_b,
+                         int grad_accumulate, const BwdPlan& p, cudaStream_t st, int sms);
+
 int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int64_t m,
                    const float* lora_a, const float* lora_b, int rank, float scale,
                    const void* t_saved, void* dx, int dx_accumulate, float* grad_a,
@@ -650,6 +730,58 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
   plan_bwd(c, m, N, K, rank, need_dx, need_t, sms, &p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
+  // The weight side of dX (s.A^T padding, transposed NF4 dequant) on the side
+  // stream while the LoRA projections run on the caller's stream.
+  SideStream* ss = (need_dx && !p.fused) ? side_stream() : nullptr;
+  cudaStream_t wst = fork_side(st, ss);
+  int wrc = FITQ_OK;
+  const char* wwhat = "";
+  if (need_dx) {
+    if (rank > 0 && (wrc = fitq::launch_pad_lora_weight(lora_a, K, rank, scale, 1, p.at_pad, wst)))
+      wwhat = "lora A^T pad";
+    if (!wrc && !p.fused && (wrc = fitq::launch_nf4_dequant(a, p.wt, FITQ_DTYPE_BF16, 1, wst, sms)))
+      wwhat = "nf4_dequant (transposed)";
+  }
+  rc = lora_bwd_side(x, dy, m, N, K, lora_a, lora_b, rank, scale, t_saved, need_t, grad_a, grad_b,
+                     grad_accumulate, p, st, sms);
+  const int jrc = join_side(st, wst, ss);
+  if (wrc) return launch_status(wrc, wwhat);
+  if (rc) return rc;
+  if (jrc) return jrc;
+  if (!need_dx) return FITQ_OK;
+  // dx[M, K] = dy[M, N].W[N, K] + U.(s.A), W decoded inside the GEMM, or
+  // W^T materialised [K, N] bf16 first (bit-exact dequant either way).
+  if (p.fused) {
+    fitq::Nf4GemmArgs g{};
+    g.w = a; g.trans = 1;
+    g.a = dy; g.lda = N;
+    g.pa = p.u_pad; g.pb = p.at_pad;
+    g.c = dx; g.ldc = K;
+    g.c_add = dx_accumulate ? dx : nullptr; g.ldc_add = K;
+    g.m = m;
+    g.lora_k = rank;
+    g.status = status_ptr();
+    return launch_status(fitq::launch_gemm_nf4(g, st, sms), "tcgen05 nf4 gemm (dx)");
+  }
+  fitq::GemmArgs g{};
+  g.a = dy; g.lda = N;
+  g.b = p.wt; g.ldb = N;
+  g.pa = p.u_pad; g.pb = p.at_pad;
+  g.c = dx; g.ldc = K;
+  g.c_add = dx_accumulate ? dx : nullptr; g.ldc_add = K;
+  g.m = m; g.n = K; g.k = N;
+  g.lora_k = rank;
+  g.status = status_ptr();
+  return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm (dx)");
+}
+
+// LoRA part of the backward on stream st: T recompute (when not saved),
+// U = dy.B, dB = s.dy^T.T, dA = s.U^T.x.
+static int lora_bwd_side(const void* x, const void* dy, int64_t m, int64_t N, int64_t K,
+                         const float* lora_a, const float* lora_b, int rank, float scale,
+                         const void* t_saved, bool need_t, float* grad_a, float* grad_b,
+                         int grad_accumulate, const BwdPlan& p, cudaStream_t st, int sms) {
+  int rc = FITQ_OK;
   const void* t_ptr = t_saved;
   int64_t t_ld = rank;
   if (rank > 0) {
@@ -678,37 +810,7 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
                                    grad_accumulate, p.partial, st, sms);
     if (rc) return launch_status(rc, "lora dA");
   }
-  if (!need_dx) return FITQ_OK;
-  // dx[M, K] = dy[M, N].W[N, K] + U.(s.A), W decoded inside the GEMM, or
-  // W^T materialised [K, N] bf16 first (bit-exact dequant either way).
-  if (rank > 0) {
-    rc = fitq::launch_pad_lora_weight(lora_a, K, rank, scale, 1, p.at_pad, st);
-    if (rc) return launch_status(rc, "lora A^T pad");
-  }
-  if (p.fused) {
-    fitq::Nf4GemmArgs g{};
-    g.w = a; g.trans = 1;
-    g.a = dy; g.lda = N;
-    g.pa = p.u_pad; g.pb = p.at_pad;
-    g.c = dx; g.ldc = K;
-    g.c_add = dx_accumulate ? dx : nullptr; g.ldc_add = K;
-    g.m = m;
-    g.lora_k = rank;
-    g.status = status_ptr();
-    return launch_status(fitq::launch_gemm_nf4(g, st, sms), "tcgen05 nf4 gemm (dx)");
-  }
-  rc = fitq::launch_nf4_dequant(a, p.wt, FITQ_DTYPE_BF16, 1, st, sms);
-  if (rc) return launch_status(rc, "nf4_dequant (transposed)");
-  fitq::GemmArgs g{};
-  g.a = dy; g.lda = N;
-  g.b = p.wt; g.ldb = N;
-  g.pa = p.u_pad; g.pb = p.at_pad;
-  g.c = dx; g.ldc = K;
-  g.c_add = dx_accumulate ? dx : nullptr; g.ldc_add = K;
-  g.m = m; g.n = K; g.k = N;
-  g.lora_k = rank;
-  g.status = status_ptr();
-  return launch_status(fitq::launch_gemm(g, st, sms), "tcgen05 gemm (dx)");
+  return FITQ_OK;
 }
 
 size_t fitq_nf4_gateup_swiglu_workspace(int64_t m, int64_t n_out, int64_t k_in) {
