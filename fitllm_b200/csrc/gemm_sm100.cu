@@ -20,15 +20,23 @@
 namespace fitq {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
+// Tile width BN is a template parameter: 256 by default; narrower tiles
+// (a multiple of 16) when the tile count of the 256-wide grid would leave
+// most of a wave idle (few rows: 512 x 5120 has 80 tiles of 128 x 256 on 148
+// SMs, but 144 tiles of 128 x 144).  The two accumulators sit 256 TMEM
+// columns apart whatever BN is.
+constexpr int BM = 128, BK = 64;
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_ACC = 2;
+constexpr int ACC_STRIDE = 256;
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;  // M-tiles (128 rows) per raster group
-constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 256;
+template <int BN>
+constexpr int b_bytes() { return BN * BK * 2; }
+template <int BN>
+constexpr size_t smem_bytes() { return 1024 /*align slack*/ + STAGES * (A_BYTES + b_bytes<BN>()) + 256; }
 
 struct Params {
   __nv_bfloat16* c;
@@ -53,11 +61,14 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
   nb = local / gsz;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tm_a,
                         const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_pa,
                         const __grid_constant__ CUtensorMap tm_pb, const Params p) {
+  static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "UMMA N for M = 128");
+  constexpr int B_BYTES = b_bytes<BN>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -157,7 +168,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
@@ -192,19 +203,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __nv_bfloat16* crow = p.c + (int64_t)row * p.ldc;
       const __nv_bfloat16* arow = p.c_add ? p.c_add + (int64_t)row * p.ldc_add : nullptr;
 #pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      for (int chunk = 0; chunk < (BN + 31) / 32; ++chunk) {
         const int col0 = nb * BN + chunk * 32;
         if (col0 >= p.n) break;  // warp-uniform
         uint32_t r[32];
+        // (a last chunk of 16 reads 16 columns past the tile, inside the allocation)
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                               static_cast<uint32_t>(acc * BN + chunk * 32),
+                               static_cast<uint32_t>(acc * ACC_STRIDE + chunk * 32),
                            r);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int col = col0 + v * 8;
-            if (col < p.n) {
+            if (col < p.n && chunk * 32 + v * 8 < BN) {
               float f[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[v * 8 + j]);
@@ -303,7 +315,44 @@ bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base,
          CUDA_SUCCESS;
 }
 
+// Tile width: 256 unless a narrower one finishes the grid in less tile time
+// (waves x width, one CTA per SM); FITQ_GEMM_BN forces one of the built widths.
+int pick_bn(int64_t m, int64_t n, int num_sms) {
+  static const int widths[] = {256, 192, 160, 144, 128};
+  const char* e = getenv("FITQ_GEMM_BN");
+  if (e != nullptr)
+    for (int w : widths)
+      if (atoi(e) == w) return w;
+  const int64_t mt = (m + BM - 1) / BM;
+  int best = 256;
+  int64_t best_cost = -1;
+  for (int w : widths) {
+    const int64_t tiles = mt * ((n + w - 1) / w);
+    const int64_t cost = (tiles + num_sms - 1) / num_sms * w;
+    if (best_cost < 0 || cost < best_cost) {  // ties keep the wider tile
+      best = w;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+int launch_gemm_bf16_tn_bn(const GemmArgs& g, cudaStream_t st, int num_sms);
+
 int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
+  switch (pick_bn(g.m, g.n, num_sms)) {
+    case 192: return launch_gemm_bf16_tn_bn<192>(g, st, num_sms);
+    case 160: return launch_gemm_bf16_tn_bn<160>(g, st, num_sms);
+    case 144: return launch_gemm_bf16_tn_bn<144>(g, st, num_sms);
+    case 128: return launch_gemm_bf16_tn_bn<128>(g, st, num_sms);
+    default: return launch_gemm_bf16_tn_bn<256>(g, st, num_sms);
+  }
+}
+
+template <int BN>
+int launch_gemm_bf16_tn_bn(const GemmArgs& g, cudaStream_t st, int num_sms) {
+  constexpr size_t SMEM_BYTES = smem_bytes<BN>();
   CUtensorMap ta, tb, tpa, tpb;
   if (!make_tmap(&ta, g.a, g.m, g.k, g.lda, BM)) return FITQ_ERR_CUDA;
   if (!make_tmap(&tb, g.b, g.n, g.k, g.ldb, BN)) return FITQ_ERR_CUDA;
@@ -334,7 +383,7 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   }
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(SMEM_BYTES)) != cudaSuccess)
       return FITQ_ERR_CUDA;
     attr_set = true;
@@ -344,7 +393,7 @@ int launch_gemm_bf16_tn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *
                        static_cast<double>(g.k + g.lora_k);
   const int slot = timing_begin(st, flops);
-  gemm_bf16_tn_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, p);
+  gemm_bf16_tn_kernel<BN><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

@@ -23,19 +23,26 @@
 namespace fitq {
 namespace {
 
+// Output columns per pair tile, BN, is a template parameter (a multiple of
+// 16; each CTA loads BN / 2 rows of B): 256 by default, narrower when the
+// 256-wide grid would leave most pairs idle (few rows).  The two
+// accumulators sit 256 TMEM columns apart whatever BN is.
 constexpr int BM = 128;        // rows of A per CTA (pair tile: 256)
-constexpr int BN_HALF = 128;   // rows of B per CTA (pair tile: 256)
-constexpr int BN = 256;        // output columns per tile
 constexpr int BK = 64;
 constexpr int STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN_HALF * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_ACC = 2;
+constexpr int ACC_STRIDE = 256;
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 8;  // in pair tiles (256 rows)
-constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+template <int BN>
+struct PairTile {
+  static constexpr int BN_HALF = BN / 2;                 // rows of B per CTA
+  static constexpr int B_BYTES = BN_HALF * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+};
 
 struct Params {
   __nv_bfloat16* c;
@@ -76,12 +83,17 @@ __device__ __forceinline__ void add_bf16x8(float (&f)[8], const __nv_bfloat16* p
   }
 }
 
+template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tn_2cta_kernel(const __grid_constant__ CUtensorMap tm_a,
                              const __grid_constant__ CUtensorMap tm_b,
                              const __grid_constant__ CUtensorMap tm_pa,
                              const __grid_constant__ CUtensorMap tm_pb,
                              const __grid_constant__ CUtensorMap tm_b2, const Params p) {
+  static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "pair UMMA N for M = 256");
+  constexpr int BN_HALF = PairTile<BN>::BN_HALF;
+  constexpr int B_BYTES = PairTile<BN>::B_BYTES;
+  constexpr int STAGE_BYTES = PairTile<BN>::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -195,7 +207,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
@@ -236,8 +248,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         for (int chunk = 0; chunk < BN_HALF / 32; ++chunk) {
           const int col0 = nb * BN_HALF + chunk * 32;
           uint32_t rg[32], ru[32];
-          tmem_ld_32x32b_x32(tmem_base + tlane + static_cast<uint32_t>(acc * BN + chunk * 32), rg);
-          tmem_ld_32x32b_x32(tmem_base + tlane + static_cast<uint32_t>(acc * BN + BN_HALF + chunk * 32), ru);
+          tmem_ld_32x32b_x32(tmem_base + tlane + static_cast<uint32_t>(acc * ACC_STRIDE + chunk * 32), rg);
+          tmem_ld_32x32b_x32(tmem_base + tlane + static_cast<uint32_t>(acc * ACC_STRIDE + BN_HALF + chunk * 32), ru);
           tmem_ld_wait();
           if (row_ok) {
 #pragma unroll
@@ -265,19 +277,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         continue;
       }
 #pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      for (int chunk = 0; chunk < (BN + 31) / 32; ++chunk) {
         const int col0 = nb * BN + chunk * 32;
         if (col0 >= p.n) break;  // warp-uniform
         uint32_t r[32];
+        // (a last chunk of 16 reads 16 columns past the tile, inside the allocation)
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                               static_cast<uint32_t>(acc * BN + chunk * 32),
+                               static_cast<uint32_t>(acc * ACC_STRIDE + chunk * 32),
                            r);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int col = col0 + v * 8;
-            if (col < p.n) {
+            if (col < p.n && chunk * 32 + v * 8 < BN) {
               float f[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[v * 8 + j]);
@@ -369,9 +382,50 @@ constexpr int kMaxDev = 64;
 
 }  // namespace
 
+// Pair tile width: 256 unless a narrower one finishes the grid in less tile
+// time (waves of num_sms / 2 pairs x width); the SwiGLU epilogues need 256.
+// FITQ_GEMM_BN2 forces one of the built widths.
+int pick_bn_pair(const GemmArgs& g, int num_sms) {
+  static const int widths[] = {256, 192, 160, 144, 128};
+  if (g.epi != GEMM_EPI_PLAIN) return 256;
+  const char* e = getenv("FITQ_GEMM_BN2");
+  if (e != nullptr)
+    for (int w : widths)
+      if (atoi(e) == w) return w;
+  const int64_t mt = (g.m + 2 * BM - 1) / (2 * BM), pairs = num_sms / 2;
+  int best = 256;
+  int64_t best_cost = -1;
+  for (int w : widths) {
+    const int64_t tiles = mt * ((g.n + w - 1) / w);
+    const int64_t cost = (tiles + pairs - 1) / pairs * w;
+    if (best_cost < 0 || cost < best_cost) {  // ties keep the wider tile
+      best = w;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+int launch_gemm_bf16_tn_2cta_bn(const GemmArgs& g, cudaStream_t st, int num_sms);
+
 int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms) {
+  switch (pick_bn_pair(g, num_sms)) {
+    case 192: return launch_gemm_bf16_tn_2cta_bn<192>(g, st, num_sms);
+    case 160: return launch_gemm_bf16_tn_2cta_bn<160>(g, st, num_sms);
+    case 144: return launch_gemm_bf16_tn_2cta_bn<144>(g, st, num_sms);
+    case 128: return launch_gemm_bf16_tn_2cta_bn<128>(g, st, num_sms);
+    default: return launch_gemm_bf16_tn_2cta_bn<256>(g, st, num_sms);
+  }
+}
+
+template <int BN>
+int launch_gemm_bf16_tn_2cta_bn(const GemmArgs& g, cudaStream_t st, int num_sms) {
+  constexpr int BN_HALF = PairTile<BN>::BN_HALF;
+  constexpr size_t SMEM_BYTES = PairTile<BN>::SMEM_BYTES;
   CUtensorMap ta, tb, tpa, tpb, tb2;
   const bool two_b = g.epi == GEMM_EPI_SWIGLU;
+  if (g.epi != GEMM_EPI_PLAIN && BN != 256) return FITQ_ERR_UNSUPPORTED;
   if (two_b && (g.n % BN_HALF != 0 || g.b2 == nullptr || g.lora_k != 0 || g.bias || g.c_add))
     return FITQ_ERR_UNSUPPORTED;
   if (g.epi == GEMM_EPI_DSWIGLU && (!g.src0 || !g.src1 || !g.aux0 || g.bias || g.c_add))
@@ -421,7 +475,7 @@ int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDev) return FITQ_ERR_NO_DEVICE;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_bf16_tn_2cta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_bf16_tn_2cta_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(SMEM_BYTES)) != cudaSuccess)
       return FITQ_ERR_CUDA;
     attr_set[dev] = true;
@@ -431,7 +485,7 @@ int launch_gemm_bf16_tn_2cta(const GemmArgs& g, cudaStream_t st, int num_sms) {
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *
                        static_cast<double>(g.k + g.lora_k) * (two_b ? 2.0 : 1.0);
   const int slot = timing_begin(st, flops);
-  gemm_bf16_tn_2cta_kernel<<<2 * clusters, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, tb2, p);
+  gemm_bf16_tn_2cta_kernel<BN><<<2 * clusters, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, tb2, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

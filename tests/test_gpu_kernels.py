@@ -100,6 +100,62 @@ def test_gemm_bf16_tn(cuda_dev, m, n, k, variant, monkeypatch):
     assert onf4.rel_err(c2.float().cpu().numpy(), (ref + add.float()).cpu().numpy()) < 4e-3
 
 
+@pytest.mark.parametrize("bn", [256, 192, 160, 144, 128])
+@pytest.mark.parametrize("m,n,k", [(512, 5120, 512), (300, 272, 192), (1000, 1008, 320), (129, 144, 64)])
+def test_gemm_one_cta_tile_widths(cuda_dev, m, n, k, bn, monkeypatch):
+    """The one-CTA tcgen05 GEMM at every built tile width (ragged N tiles,
+    ragged rows, bias + residual epilogue, the LoRA K block) against fp32."""
+    monkeypatch.setenv("FITQ_GEMM_VARIANT", "1cta")
+    monkeypatch.setenv("FITQ_GEMM_BN", str(bn))
+    from fitllm_b200.ops import gemm_bf16_tn
+    g = torch.Generator(device="cpu").manual_seed(m + n + bn)
+    a = _bf16(torch.randn(m, k, generator=g)).to(cuda_dev)
+    b = _bf16(torch.randn(n, k, generator=g)).to(cuda_dev)
+    add = _bf16(torch.randn(m, n, generator=g)).to(cuda_dev)
+    ref = a.float() @ b.float().T
+    c = gemm_bf16_tn(a, b, add)
+    assert onf4.rel_err(c.float().cpu().numpy(), (ref + add.float()).cpu().numpy()) < 4e-3
+
+
+@pytest.mark.parametrize("bn", [256, 192, 160, 144, 128])
+@pytest.mark.parametrize("m,n,k", [(512, 5120, 512), (300, 272, 192), (1000, 1008, 320), (600, 144, 64)])
+def test_gemm_pair_tile_widths(cuda_dev, m, n, k, bn, monkeypatch):
+    """The CTA-pair tcgen05 GEMM at every built tile width (each CTA loads
+    bn / 2 rows of B; ragged N tiles and rows; residual epilogue)."""
+    monkeypatch.setenv("FITQ_GEMM_VARIANT", "2cta")
+    monkeypatch.setenv("FITQ_GEMM_BN2", str(bn))
+    from fitllm_b200.ops import gemm_bf16_tn
+    g = torch.Generator(device="cpu").manual_seed(m + n + bn + 1)
+    a = _bf16(torch.randn(m, k, generator=g)).to(cuda_dev)
+    b = _bf16(torch.randn(n, k, generator=g)).to(cuda_dev)
+    add = _bf16(torch.randn(m, n, generator=g)).to(cuda_dev)
+    ref = a.float() @ b.float().T
+    c = gemm_bf16_tn(a, b, add)
+    assert onf4.rel_err(c.float().cpu().numpy(), (ref + add.float()).cpu().numpy()) < 4e-3
+
+
+@pytest.mark.parametrize("variant,env,bn", [("1cta", "FITQ_GEMM_BN", 144), ("2cta", "FITQ_GEMM_BN2", 144),
+                                            ("2cta", "FITQ_GEMM_BN2", 192)])
+def test_qlora_tile_widths_identical(cuda_dev, variant, env, bn, monkeypatch):
+    """QLoRA fwd / bwd at the q_proj shape: the tile width changes the
+    schedule, not the arithmetic (every output element's K sum is the same
+    sequence of MMAs), so y and dX are bit-identical across widths."""
+    from fitllm_b200 import ops
+    monkeypatch.setenv("FITQ_NF4_FUSED", "0")
+    monkeypatch.setenv("FITQ_GEMM_VARIANT", variant)
+    st, wref, w_deq, A, B, x, dy = _qlora_case(512, 5120, 5120, 16, 77, cuda_dev)
+    Ad, Bd, xd, dyd = A.to(cuda_dev), B.to(cuda_dev), x.to(cuda_dev), dy.to(cuda_dev)
+    out = {}
+    for w in (256, bn):
+        monkeypatch.setenv(env, str(w))
+        y, t = ops.qlora_forward(xd, wref, Ad, Bd, 2.0, want_t=True)
+        dx, ga, gb = ops.qlora_backward(xd, dyd, wref, Ad, Bd, 2.0, t_saved=t)
+        out[w] = (y, dx, ga, gb)
+    torch.cuda.synchronize()
+    for i in range(4):
+        assert torch.equal(out[256][i], out[bn][i])
+
+
 def _qlora_case(m, n, k, r, seed, dev):
     from fitllm_b200.nf4 import Nf4WeightCRef
     st = onf4.quantize(_weights(n, k, seed))
