@@ -557,6 +557,23 @@ static bool grouped_tc(const fitq_gemv_job* jobs, int count, int64_t m, int sms,
   return fitq::gemv_tc_plan(m, n_total, w0->k_in, sms, slices);
 }
 
+// Grouped decode launch (M <= 8): two or three jobs sharing K and the scale
+// format, N % 64 == 0 each, and a decode plan for the summed N.
+static bool grouped_dec(const fitq_gemv_job* jobs, int count, int64_t m, int sms, int* slices) {
+  if (count < 2 || count > 3) return false;
+  const fitq_nf4_weight* w0 = jobs[0].w;
+  if (!w0) return false;
+  const bool nested = w0->absmax_f32 == nullptr;
+  int64_t n_total = 0;
+  for (int g = 0; g < count; ++g) {
+    const fitq_nf4_weight* w = jobs[g].w;
+    if (!w || w->k_in != w0->k_in || (w->absmax_f32 == nullptr) != nested || w->n_out % 64 != 0)
+      return false;
+    n_total += w->n_out;
+  }
+  return fitq::gemv_dec_plan(m, n_total, w0->k_in, sms, slices);
+}
+
 static size_t grouped_bytes(const fitq_gemv_job* jobs, int count, int64_t m, int slices) {
   Carve c{nullptr, 0};
   for (int g = 0; g < count; ++g) {
@@ -578,7 +595,8 @@ static size_t grouped_workspace(const fitq_gemv_job* jobs, int count, int64_t m,
     if (!jobs[g].w) return 0;
   const int sms = sms_for_sizing();
   int slices = 0;
-  if (grouped_tc(jobs, count, m, sms, &slices)) return grouped_bytes(jobs, count, m, slices);
+  if (grouped_tc(jobs, count, m, sms, &slices) || grouped_dec(jobs, count, m, sms, &slices))
+    return grouped_bytes(jobs, count, m, slices);
   size_t need = 0;
   for (int g = 0; g < count; ++g) {
     const size_t b = fitq_nf4_gemv_workspace(m, jobs[g].w->n_out, jobs[g].w->k_in, jobs[g].rank);
@@ -605,7 +623,8 @@ static int grouped_impl(const fitq_gemv_job* jobs, int count, const void* x, int
   if (!sms) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int slices = 0;
-  if (!grouped_tc(jobs, count, m, sms, &slices)) {
+  const bool tc = grouped_tc(jobs, count, m, sms, &slices);
+  if (!tc && !grouped_dec(jobs, count, m, sms, &slices)) {
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     size_t left = workspace_bytes;
     void* y[3] = {nullptr, nullptr, nullptr};
@@ -653,8 +672,9 @@ static int grouped_impl(const fitq_gemv_job* jobs, int count, const void* x, int
       t_part[g] = static_cast<float*>(c.take(fitq::lora_t_workspace(m, a[g].k_in, jobs[g].rank)));
   }
   const int64_t K = a[0].k_in;
-  rc = fitq::launch_nf4_gemv_tc_grouped(a, count, x, m, partial, status_ptr(), st, sms);
-  if (rc) return launch_status(rc, "nf4_gemv_grouped tcgen05");
+  rc = tc ? fitq::launch_nf4_gemv_tc_grouped(a, count, x, m, partial, status_ptr(), st, sms)
+          : fitq::launch_nf4_gemv_dec_grouped(a, count, x, m, partial, status_ptr(), st, sms);
+  if (rc) return launch_status(rc, tc ? "nf4_gemv_grouped tcgen05" : "nf4_gemv_grouped decode");
   fitq::GemvEpilogue ep[3];
   int64_t n_out[3];
   for (int g = 0; g < count; ++g) {

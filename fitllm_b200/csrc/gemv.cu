@@ -317,15 +317,27 @@ __device__ __forceinline__ void dec_store(const GemvEpilogue& o, const float* tl
       __float2bfloat16_rn(dec_value(o, tl, N, tk, n, s));
 }
 
+// Staged row r (r & 3 == lane >> 3 for every copy of a lane): 16-byte chunk k
+// at chunk k ^ 2*(r & 3) of the 128-byte row.
+__device__ __forceinline__ uint32_t dst_lane_of(int lane) {
+  return static_cast<uint32_t>((lane >> 3) * 128 + 16 * ((lane & 7) ^ (2 * (lane >> 3))));
+}
+
+// Which weight of a grouped launch tile t belongs to (DecJobs in kernels.cuh).
+__device__ __forceinline__ int dec_job(const DecJobs& jb, int t) {
+  return (t >= jb.tile0[1]) + (t >= jb.tile0[2]);
+}
+
 template <bool NESTED>
 __global__ void __launch_bounds__(kThreads, 1)
-    nf4_gemv_dec_kernel(Nf4Args w, const __nv_bfloat16* __restrict__ x, int M, Gemv8Plan pl,
+    nf4_gemv_dec_kernel(DecJobs jb, const __nv_bfloat16* __restrict__ x, int M, Gemv8Plan pl,
                         GemvEpilogue out) {
   constexpr int R = kDecRing, D = kDecDepth;
+  const Nf4Args& w = jb.w[0];  // K, code tables (shared by every weight of the launch)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int K = static_cast<int>(w.k_in), N = static_cast<int>(w.n_out);
-  const int nblk = K / 64, T = N / 16;
+  const int K = static_cast<int>(w.k_in);
+  const int nblk = K / 64, T = jb.tile0[3];
   const int qn = 1 << pl.lqn;  // token lanes q < qn hold tokens 2q, 2q+1 < 2*qn >= M
 
   const int slice = blockIdx.x / pl.cs, j = blockIdx.x % pl.cs;
@@ -337,10 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_u = t0 < T ? (T - 1 - t0) / tstride + 1 : 0;
 
   // Before the dependency wait: L2 prefetch of this warp's first tiles only.
-  if (lane < 16 && (reinterpret_cast<uintptr_t>(w.packed) & 15) == 0) {
-    for (int u = 0; u < kDecDepth && u < n_u; ++u)
-      prefetch_l2(w.packed + (static_cast<int64_t>(16 * (t0 + u * tstride) + lane) * nblk + b0) * 32,
+  if (lane < 16) {
+    for (int u = 0; u < kDecDepth && u < n_u; ++u) {
+      const int t = t0 + u * tstride, jj = dec_job(jb, t);
+      prefetch_l2(jb.w[jj].packed +
+                      (static_cast<int64_t>(16 * (t - jb.tile0[jj]) + lane) * nblk + b0) * 32,
                   kDecKB * 32);
+    }
   }
   // Wait first, then let dependents launch: a LoRA T kernel launched right
   // behind this one reads x without waiting (see launch_lora_t).
@@ -374,16 +389,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_u_max = j < T ? (T - 1 - j) / tstride + 1 : 0;  // row group 0 has the most
   const int rounds = (n_u_max + D) / R;
   const int nblk8 = 8 * nblk;
-  const int fstep = 16 * tstride * nblk;   // flat-block step between the warp's tiles
-  int f_next = (16 * t0 + g) * nblk + b0;   // flat block of row a of the next tile's scales
   // copies: lane covers 16 bytes (lane & 7) of rows (lane >> 3) + 4j, j = 0..3
   const int64_t row_bytes = K / 2;
-  const uint8_t* src = w.packed + (static_cast<int64_t>(16 * t0 + (lane >> 3)) * nblk + b0) * 32 +
-                       16 * (lane & 7);
-  const int64_t src_step = static_cast<int64_t>(16) * tstride * row_bytes;
-  // staged row r (r & 3 == lane >> 3 for every copy of this lane): chunk k at k ^ 2*(r & 3)
-  const uint32_t dst_lane =
-      static_cast<uint32_t>((lane >> 3) * 128 + 16 * ((lane & 7) ^ (2 * (lane >> 3))));
+  // tile u of this warp: its weight's copies and scales (flat block of row g)
+  auto issue_tile = [&](uint32_t stg, ScaleBuf<NESTED>& sbuf, int u, uint64_t pol) {
+    const int t = t0 + u * tstride, jj = dec_job(jb, t), tl = t - jb.tile0[jj];
+    const uint8_t* src = jb.w[jj].packed + (static_cast<int64_t>(16 * tl + (lane >> 3)) * nblk + b0) * 32 +
+                         16 * (lane & 7);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) cp_async16(stg + dst_lane_of(lane) + c * 512, src + c * 4 * row_bytes, pol);
+    load_scales(sbuf, jb.w[jj], (16 * tl + g) * nblk + b0, nblk8);
+  };
   uint32_t frag[kDecKB];  // fragment reads: row g, bytes 32c + 8q, swizzled
 #pragma unroll
   for (int c = 0; c < kDecKB; ++c)
@@ -400,15 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   ScaleBuf<NESTED> sb[R];
 #pragma unroll
   for (int d = 0; d < D; ++d) {
-    if (d < n_u) {
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj)
-        cp_async16(stage[d] + dst_lane + jj * 512, src + jj * 4 * row_bytes, pol);
-      load_scales(sb[d], w, f_next, nblk8);
-    }
+    if (d < n_u) issue_tile(stage[d], sb[d], d, pol);
     cp_async_commit();
-    f_next += fstep;
-    src += src_step;
   }
   // entry e (256 B): lanes' bf16 pairs {qm[e >> 4], qm[e & 15]} at 4l, nested map at 128 + 4g;
   // two threads per entry, 16-byte stores
@@ -422,6 +431,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (NESTED) {
       const uint32_t nv = __float_as_uint(__ldg(w.nested_quant_map + e));
       table[e * 16 + 8 + h] = make_uint4(nv, nv, nv, nv);
+    }
+    // One code table serves every weight of a grouped launch: their maps must hold the same values.
+    for (int gg = 1; gg < jb.groups; ++gg) {
+      bool same = true;
+      if (threadIdx.x < 16) same = __ldg(jb.w[gg].quant_map + threadIdx.x) == __ldg(w.quant_map + threadIdx.x);
+      if (NESTED && threadIdx.x < 256)
+        same = same && __ldg(jb.w[gg].nested_quant_map + threadIdx.x) == __ldg(w.nested_quant_map + threadIdx.x);
+      if (!same) report_device_error(jb.status, FITQ_ERR_UNSUPPORTED);
     }
   }
 
@@ -446,21 +463,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int r = 0; r < R; ++r) {
       const int u = rd * R + r;
       __syncwarp();  // every lane is done with the stage refilled below (decoded last step)
-      if (u + D < n_u) {
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj)
-          cp_async16(stage[(r + D) % R] + dst_lane + jj * 512, src + jj * 4 * row_bytes, pol);
-        load_scales(sb[(r + D) % R], w, f_next, nblk8);
-      }
+      if (u + D < n_u) issue_tile(stage[(r + D) % R], sb[(r + D) % R], u + D, pol);
       cp_async_commit();
-      f_next += fstep;
-      src += src_step;
       cp_async_wait<D>();  // this lane's copies of tile u have landed
       __syncwarp();        // ... and every other lane's
       float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
       if (u < n_u) {
         float4 am_a, am_b;
-        tile_scales(sb[r], nq_base, sel_q, w.offset, sc_w, sc_lane, g, am_a, am_b);
+        const float offset = jb.groups > 1 ? jb.w[dec_job(jb, t0 + u * tstride)].offset : w.offset;
+        tile_scales(sb[r], nq_base, sel_q, offset, sc_w, sc_lane, g, am_a, am_b);
         o = compute_tile(stage[r], frag, am_a, am_b, xr, lb);
       }
       if (q < qn) red[((r + R * (rd & 1)) * kWarps + warp) * red_warp + (g << pl.lqn) + q] = o;
@@ -483,8 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* srcf = rf + (((r * kWarps + (rgo << pl.lkw)) * red_warp) << 2) + f;
       float s = 0.f;
       for (int pp = 0; pp < pl.kw; ++pp) s += srcf[(pp * red_warp) << 2];
-      if (out.partial == nullptr) dec_store(out, nullptr, N, tk, t * 16 + rr, s);
-      else out.partial[(static_cast<int64_t>(slice) * M + tk) * N + t * 16 + rr] = s;
+      const int jj = dec_job(jb, t);
+      const int nj = static_cast<int>(jb.w[jj].n_out), row = (t - jb.tile0[jj]) * 16 + rr;
+      if (jb.partial[jj] == nullptr) dec_store(out, nullptr, nj, tk, row, s);
+      else jb.partial[jj][(static_cast<int64_t>(slice) * M + tk) * nj + row] = s;
     }
     __syncthreads();  // reduction area rewritten from the next round on
   }
@@ -925,11 +938,54 @@ bool gemv_dec_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* sli
 
 bool gemv_dec_needs_partial(int slices, int rank) { return slices > 1 || rank > 0; }
 
+static int launch_dec(const DecJobs& jb, const void* x, int64_t m, const GemvEpilogue& out,
+                      const Gemv8Plan& pl, cudaStream_t st);
+
 int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEpilogue& out,
                         cudaStream_t st, int num_sms) {
   Gemv8Plan pl;
   if (!gemv_dec_plan(m, w.n_out, w.k_in, num_sms, nullptr) || !use_m8(m, w.n_out, w.k_in, num_sms, &pl))
     return FITQ_ERR_UNSUPPORTED;
+  DecJobs jb{};
+  jb.w[0] = jb.w[1] = jb.w[2] = w;
+  jb.partial[0] = out.partial;
+  const int T = static_cast<int>(w.n_out / 16);
+  jb.tile0[0] = 0;
+  jb.tile0[1] = jb.tile0[2] = jb.tile0[3] = T;
+  jb.groups = 1;
+  return launch_dec(jb, x, m, out, pl, st);
+}
+
+int launch_nf4_gemv_dec_grouped(const Nf4Args* w, int groups, const void* x, int64_t m,
+                                float* const* partial, int* status, cudaStream_t st, int num_sms) {
+  if (groups < 1 || groups > 3) return FITQ_ERR_UNSUPPORTED;
+  int64_t n_total = 0;
+  DecJobs jb{};
+  jb.tile0[0] = 0;
+  for (int g = 0; g < 3; ++g) {
+    const int gg = g < groups ? g : groups - 1;
+    jb.w[g] = w[gg];
+    jb.partial[g] = g < groups ? partial[g] : nullptr;
+    if (g < groups) {
+      if (w[g].k_in != w[0].k_in || w[g].n_out % 16 != 0 || !partial[g] ||
+          (w[g].absmax_f32 == nullptr) != (w[0].absmax_f32 == nullptr))
+        return FITQ_ERR_UNSUPPORTED;
+      n_total += w[g].n_out;
+    }
+    jb.tile0[g + 1] = static_cast<int>(n_total / 16);
+  }
+  jb.groups = groups;
+  jb.status = status;
+  Gemv8Plan pl;
+  if (!gemv_dec_plan(m, n_total, w[0].k_in, num_sms, nullptr) || !use_m8(m, n_total, w[0].k_in, num_sms, &pl))
+    return FITQ_ERR_UNSUPPORTED;
+  GemvEpilogue out{};  // partials only: the group finishing kernel applies the epilogues
+  return launch_dec(jb, x, m, out, pl, st);
+}
+
+static int launch_dec(const DecJobs& jb, const void* x, int64_t m, const GemvEpilogue& out,
+                      const Gemv8Plan& pl, cudaStream_t st) {
+  const Nf4Args& w = jb.w[0];
   auto xb = static_cast<const __nv_bfloat16*>(x);
   const int M = static_cast<int>(m);
   const dim3 grid(static_cast<unsigned>(pl.cs * pl.slices));
@@ -943,8 +999,8 @@ int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEp
     attr[nested] = true;
   }
   cudaError_t e =
-      nested ? launch_pdl(nf4_gemv_dec_kernel<true>, grid, dim3(kThreads), kDecSmem, st, w, xb, M, pl, out)
-             : launch_pdl(nf4_gemv_dec_kernel<false>, grid, dim3(kThreads), kDecSmem, st, w, xb, M, pl, out);
+      nested ? launch_pdl(nf4_gemv_dec_kernel<true>, grid, dim3(kThreads), kDecSmem, st, jb, xb, M, pl, out)
+             : launch_pdl(nf4_gemv_dec_kernel<false>, grid, dim3(kThreads), kDecSmem, st, jb, xb, M, pl, out);
   note_launch();
   return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }

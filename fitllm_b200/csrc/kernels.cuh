@@ -176,6 +176,19 @@ struct GemvEpilogue {
   float scale;
   float* partial;        // fp32 [slices, M, N] when the finishing kernel runs
 };
+// Up to three weights with one K streamed by one decode launch (the q/k/v or
+// gate/up projections of a layer on the same x): tiles (16 rows)
+// [tile0[j], tile0[j + 1]) are weight j's; tile0[3] = all tiles.  Weight j
+// writes fp32 partials [slices, M, N_j] to partial[j] (null: the single-weight
+// launch writes y through its epilogue).  status: where a grouped launch whose
+// weights carry different code tables reports FITQ_ERR_UNSUPPORTED.
+struct DecJobs {
+  Nf4Args w[3];
+  float* partial[3];
+  int tile0[4];
+  int groups;
+  int* status;
+};
 // True when the decode kernel takes (m, N, K); *slices = its K slices.
 bool gemv_dec_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* slices);
 // Whether the decode GEMV writes fp32 partials (several K slices, or a LoRA
@@ -185,6 +198,10 @@ bool gemv_dec_plan(int64_t m, int64_t n_out, int64_t k_in, int num_sms, int* sli
 bool gemv_dec_needs_partial(int slices, int rank);
 int launch_nf4_gemv_dec(const Nf4Args& w, const void* x, int64_t m, const GemvEpilogue& out,
                         cudaStream_t st, int num_sms);
+// The decode kernel over 1-3 weights sharing K and x (partials only; the plan
+// of the summed N: gemv_dec_plan(m, sum N, K, ...)).
+int launch_nf4_gemv_dec_grouped(const Nf4Args* w, int groups, const void* x, int64_t m,
+                                float* const* partial, int* status, cudaStream_t st, int num_sms);
 int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
                                cudaStream_t st, int num_sms);
 // The finishing pass of a grouped launch (up to three epilogues, one grid);

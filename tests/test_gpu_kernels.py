@@ -396,10 +396,14 @@ def test_lm_head_loss_and_grad(cuda_dev):
 @pytest.mark.parametrize("m,shapes,nested", [(40, [(512, 1024, 16), (128, 1024, 0), (128, 1024, 16)], True),
                                              (16, [(1024, 2048, 0), (1024, 2048, 0)], True),
                                              (64, [(384, 512, 0), (256, 512, 16)], False),
-                                             (4, [(256, 512, 16), (128, 512, 0)], True)])
+                                             (4, [(256, 512, 16), (128, 512, 0)], True),
+                                             (1, [(1024, 5120, 16), (256, 5120, 0), (256, 5120, 16)], True),
+                                             (2, [(2048, 1024, 0), (2048, 1024, 0)], False),
+                                             (8, [(512, 1024, 32), (192, 1024, 0), (64, 1024, 16)], True)])
 def test_gemv_grouped(cuda_dev, m, shapes, nested):
     """fitq_nf4_gemv_grouped: up to three projections of one x (one tcgen05
-    launch over all their tiles for 8 < M <= 64, per-job calls otherwise) give
+    launch over all their tiles for 8 < M <= 64, one decode-kernel launch for
+    M <= 8) give
     each projection's fitq_nf4_gemv result within 1e-2 of the oracle, with
     LoRA, bias and y_add per job."""
     from fitllm_b200 import ops
