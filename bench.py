@@ -714,10 +714,15 @@ def main():
         pipe = HostBatchPipeline(dev, [h_host, g_host])
 
         def e2e_step(bufs):
-            sched.invalidate()  # the layer shard is uploaded from pinned host memory every step
             store.zero_grad()
             gin = eng.step(bufs[0], bufs[1])
             opt.step()
+            # The layer shard is uploaded from pinned host memory for every step:
+            # the next step's upload is queued now, into the ring's other slot,
+            # so it overlaps this step's work (as layer l + 1's upload overlaps
+            # layer l in a multi-layer model).
+            sched.invalidate()
+            sched.prefetch(0)
             # a copy: the next step zeroes the gradient buffer while this one is read back
             return [gin, store.layer_slice(store.grad, 0).clone()]
 
@@ -725,12 +730,14 @@ def main():
             pipe.run(e2e_step, [(h_host, g_host)] * n, [(gin_host, lora_host)] * n)
 
         e2e_run(2)
+        sched.wait_uploads()
         barrier()
         torch.cuda.synchronize()
         s2 = torch.cuda.Event(enable_timing=True)
         e2 = torch.cuda.Event(enable_timing=True)
         s2.record()
         e2e_run(a.steps)
+        sched.wait_uploads()  # the timed region holds one shard upload per step
         e2.record()
         torch.cuda.synchronize()
         barrier()
@@ -746,7 +753,8 @@ def main():
                        "ring, hidden states and upstream grad H2D, input grad and LoRA grads D2H, "
                        "every step inside the timed region; the batch copies run on their own "
                        "streams through fitllm_b200.host_io.HostBatchPipeline (next batch's H2D "
-                       "and previous result's D2H overlap the step)"}
+                       "and previous result's D2H overlap the step) and the next step's shard "
+                       "upload goes into the ring's other slot while the step runs"}
 
     # every rank takes part in the full-step measurement (it has collectives)
     full_step = None

@@ -104,6 +104,7 @@ class ShardScheduler:
         self._slot_layer: List[int] = [-1] * ring_slots
         self._ready: List[Optional[torch.cuda.Event]] = [None] * ring_slots
         self._free: List[Optional[torch.cuda.Event]] = [None] * ring_slots
+        self._generation = 0  # slot map offset (advanced by invalidate)
         self._copy_stream: Optional[torch.cuda.Stream] = None
         self.h2d_bytes = 0
 
@@ -182,7 +183,7 @@ class ShardScheduler:
                 self._free[s] = None
 
     def slot_of(self, layer_idx: int) -> int:
-        return layer_idx % self.ring_slots
+        return (layer_idx + self._generation) % self.ring_slots
 
     def prefetch(self, layer_idx: int) -> None:
         """Start the async upload of a layer into its ring slot (idempotent)."""
@@ -234,8 +235,20 @@ class ShardScheduler:
         self._free[s] = ev
 
     def invalidate(self) -> None:
-        """Forget which layers the ring holds, so the next get re-uploads."""
+        """Forget which layers the ring holds, so the next get re-uploads.
+
+        The slot map advances by one, so with two or more slots the next
+        upload of a layer lands in a different slot than the one the work
+        queued so far may still read: a caller can invalidate and prefetch
+        the next step's first layer right after queueing the current step,
+        and that upload overlaps the current step's work."""
         self._slot_layer = [-1] * self.ring_slots
+        self._generation += 1
+
+    def wait_uploads(self) -> None:
+        """Make the current stream wait for every upload queued so far."""
+        if self._copy_stream is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
 
     # reference-compatible names
     def prefetch_to_cpu(self, layer_idx: int, verify_checksums: bool = False) -> None:

@@ -483,3 +483,36 @@ def test_host_batch_pipeline_matches_serial_steps(cuda_dev):
         assert torch.equal(a_gin, b_gin)
         assert torch.equal(a_grad, b_grad)
     assert not torch.equal(results[1][0][0], results[1][1][0])  # the batches really differ
+
+
+def test_reupload_into_rotated_slot_matches(cuda_dev):
+    """One-layer engine steps with the shard re-uploaded every step: queued
+    right after the previous step into the ring's other slot (invalidate +
+    prefetch, the pipelined upload) they return bit-identically what steps
+    with the upload in stream order return."""
+    from fitllm_b200.engine import ShardStationaryEngine, build_synthetic_model
+    cfg = _cfg()
+    g = torch.Generator().manual_seed(43)
+    shape = (2, 64, SMALL["hidden"])
+    batches = [(torch.randn(*shape, generator=g).bfloat16().to(cuda_dev),
+                torch.randn(*shape, generator=g).bfloat16().to(cuda_dev)) for _ in range(4)]
+    results = []
+    for mode in ("in_order", "rotated"):
+        sched, store = build_synthetic_model(cfg, 1, cuda_dev, seed=6)
+        eng = ShardStationaryEngine(cfg, sched, store, cuda_dev, keep_activations=0)
+        outs = []
+        for h, go in batches:
+            if mode == "in_order":
+                sched.invalidate()
+            store.zero_grad()
+            gin = eng.step(h, go)
+            outs.append((gin.clone(), store.grad.clone()))
+            if mode == "rotated":
+                sched.invalidate()
+                sched.prefetch(0)
+        sched.wait_uploads()
+        torch.cuda.synchronize()
+        results.append(outs)
+    for (a_gin, a_grad), (b_gin, b_grad) in zip(*results):
+        assert torch.equal(a_gin, b_gin)
+        assert torch.equal(a_grad, b_grad)

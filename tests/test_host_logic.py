@@ -200,6 +200,16 @@ def test_shard_store_layout_drops_lora_keys():
     assert s.quant_meta(0)["a.weight"]["nested_offset"] == 0.5
 
 
+def test_ring_slot_map_advances_on_invalidate():
+    from fitllm_b200.scheduler import ShardScheduler
+    s = ShardScheduler(3, "cpu", ring_slots=2, pin_memory=False)
+    assert [s.slot_of(l) for l in range(3)] == [0, 1, 0]
+    s.invalidate()
+    assert [s.slot_of(l) for l in range(3)] == [1, 0, 1]
+    s.invalidate()
+    assert [s.slot_of(l) for l in range(3)] == [0, 1, 0]
+
+
 def test_microbatch_split():
     from fitllm_b200.distributed import microbatch_range
     for n in (16, 15, 3):
