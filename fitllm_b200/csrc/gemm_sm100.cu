@@ -324,6 +324,9 @@ int pick_bn(int64_t m, int64_t n, int num_sms) {
     for (int w : widths)
       if (atoi(e) == w) return w;
   const int64_t mt = (m + BM - 1) / BM;
+  // Only grids of under two waves at 256 columns lose much to the last wave;
+  // larger ones keep the wide tile (fewer A re-reads, better MMA efficiency).
+  if (mt * ((n + 255) / 256) >= 2 * num_sms) return 256;
   int best = 256;
   int64_t best_cost = -1;
   for (int w : widths) {

@@ -393,6 +393,9 @@ int pick_bn_pair(const GemmArgs& g, int num_sms) {
     for (int w : widths)
       if (atoi(e) == w) return w;
   const int64_t mt = (g.m + 2 * BM - 1) / (2 * BM), pairs = num_sms / 2;
+  // Only grids of under two waves at 256 columns lose much to the last wave;
+  // larger ones keep the wide tile (fewer A re-reads, better MMA efficiency).
+  if (mt * ((g.n + 255) / 256) >= 2 * pairs) return 256;
   int best = 256;
   int64_t best_cost = -1;
   for (int w : widths) {
