@@ -458,6 +458,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   __syncthreads();  // table ready
 
+  // barrier of the kw warps of row group rg (a single warp needs none)
+  auto group_sync = [&]() {
+    if (pl.kw == 1) {
+      __syncwarp();
+    } else {
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + rg), "r"(pl.kw * 32) : "memory");
+    }
+  };
+
   for (int rd = 0; rd < rounds; ++rd) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -476,16 +485,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (q < qn) red[((r + R * (rd & 1)) * kWarps + warp) * red_warp + (g << pl.lqn) + q] = o;
     }
-    if ((rd & 1) == 0 && rd + 1 < rounds) continue;  // CTA-uniform: reduce two rounds at once
-    __syncthreads();
+    if ((rd & 1) == 0 && rd + 1 < rounds) continue;  // reduce two rounds at once
+    // Only the kw warps of this row group exchange partial sums: they meet on
+    // their own named barrier (1 + rg), so row groups do not wait on each other.
+    group_sync();
     // sum the kw parts of each tile of rounds rd0..rd in k order; slot f = (g*qn + q)*4 + component
     const int rd0 = rd & ~1;
     const int fbits = 5 + pl.lqn;
-    const int outs = (((rd - rd0 + 1) * R) << pl.lrtg) << fbits;
+    const int outs = ((rd - rd0 + 1) * R) << fbits;
     const float* rf = reinterpret_cast<const float*>(red);
-    for (int e = threadIdx.x; e < outs; e += kThreads) {
-      const int f = e & ((1 << fbits) - 1), hi = e >> fbits;
-      const int rgo = hi & (pl.rtg - 1), r = hi >> pl.lrtg;
+    for (int e = p * 32 + lane; e < outs; e += pl.kw * 32) {
+      const int f = e & ((1 << fbits) - 1), r = e >> fbits;
+      const int rgo = rg;
       const int ls = f >> 2, comp = f & 3;
       const int rr = (ls >> pl.lqn) + 8 * (comp >> 1);
       const int tk = 2 * (ls & (qn - 1)) + (comp & 1);
@@ -499,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (jb.partial[jj] == nullptr) dec_store(out, nullptr, nj, tk, row, s);
       else jb.partial[jj][(static_cast<int64_t>(slice) * M + tk) * nj + row] = s;
     }
-    __syncthreads();  // reduction area rewritten from the next round on
+    group_sync();  // the group's reduction slots are rewritten from the next round on
   }
   cp_async_wait<0>();
 }
