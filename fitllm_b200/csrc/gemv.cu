@@ -102,7 +102,8 @@ __device__ __forceinline__ uint32_t lut(uint32_t v, uint32_t lane4) {
 // map lives in the unused upper half of each 256-byte entry (8 copies, one per
 // lane row g): an absmax costs one prmt + one ld.shared + the reference's two
 // rounded fp32 ops.  The kw partial sums of a tile are combined through shared
-// memory once per round of 3 tiles, in k order (deterministic).
+// memory every second round of 3 tiles, in k order (deterministic), by the kw
+// warps of the row group alone, which meet on a named barrier of their own.
 //
 // Epilogue: with one K slice and no LoRA the sums go straight to y (+ bias +
 // y_add, bf16) in this kernel.  Otherwise each slice writes fp32 partials
