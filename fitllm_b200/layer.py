@@ -147,7 +147,7 @@ class _FusedMLPFn(torch.autograd.Function):
     separate projections + SwiGLU kernels (same GEMMs, same epilogue math)."""
 
     @staticmethod
-    def forward(ctx, x, residual, wg, wu, wd):
+    def forward(ctx, x, residual, wg, wu, wd, bwd_fused=True):
         from . import ops
         lead = x.shape[:-1]
         x2 = ops._bf16_2d(x, wg.c.k_in)
@@ -157,6 +157,7 @@ class _FusedMLPFn(torch.autograd.Function):
         y, _ = ops.qlora_forward(act, wd, None, None, 1.0, y_add=res2)
         ctx.refs = (wg, wu, wd)
         ctx.lead = lead
+        ctx.bwd_fused = bwd_fused
         ctx.save_for_backward(gate, up)
         return y.view(*lead, wd.c.n_out)
 
@@ -168,12 +169,17 @@ class _FusedMLPFn(torch.autograd.Function):
         dy2 = ops._bf16_2d(dy, wd.c.n_out)
         dx = None
         if ctx.needs_input_grad[0]:
-            d_gate, d_up = ops.nf4_down_dswiglu(dy2, wd, gate, up)
+            if ctx.bwd_fused:
+                d_gate, d_up = ops.nf4_down_dswiglu(dy2, wd, gate, up)
+            else:  # down_proj dX, then the separate SwiGLU backward kernel
+                from .layer_ops import swiglu_backward
+                d_act, _, _ = ops.qlora_backward(None, dy2, wd, None, None, 1.0)
+                d_gate, d_up = swiglu_backward(d_act, gate, up)
             dx, _, _ = ops.qlora_backward(None, d_gate, wg, None, None, 1.0)
             ops.qlora_backward(None, d_up, wu, None, None, 1.0, dx=dx)
             dx = dx.view(*ctx.lead, wg.c.k_in)
         dres = dy if ctx.needs_input_grad[1] else None
-        return dx, dres, None, None, None
+        return dx, dres, None, None, None, None
 
 
 def _plain_nf4(mod) -> bool:
@@ -187,16 +193,19 @@ class MLP(nn.Module):
         self.up_proj = Linear4bit(cfg.hidden, cfg.intermediate, device=device)
         self.down_proj = Linear4bit(cfg.intermediate, cfg.hidden, device=device)
         # FITQ_MLP_FUSED=1: gate/up + SwiGLU in one GEMM, SwiGLU backward in
-        # down's dX.  Off by default: on a power-capped B200 the Qwen2.5-32B
-        # layer step measured 3-6% slower with it (the fused GEMMs ran at a
-        # lower SM clock) although it removes three element-wise passes.
-        self.fused = os.environ.get("FITQ_MLP_FUSED", "0") == "1"
+        # down's dX; FITQ_MLP_FUSED=fwd: the forward fusion only.  Off by
+        # default: on a power-capped B200 the Qwen2.5-32B layer step measured
+        # 3-6% slower with both (the fused GEMMs ran at a lower SM clock)
+        # although they remove three element-wise passes.
+        mode = os.environ.get("FITQ_MLP_FUSED", "0")
+        self.fused = mode in ("1", "fwd")
+        self.fused_backward = mode == "1"
 
     def forward(self, x, residual):
         if (self.fused and x.is_cuda and _plain_nf4(self.gate_proj) and _plain_nf4(self.up_proj)
                 and _plain_nf4(self.down_proj) and self.gate_proj.out_features % 128 == 0):
             return _FusedMLPFn.apply(x, residual, self.gate_proj.wref(), self.up_proj.wref(),
-                                     self.down_proj.wref())
+                                     self.down_proj.wref(), self.fused_backward)
         return self.down_proj(swiglu(self.gate_proj(x), self.up_proj(x)), residual=residual)
 
 

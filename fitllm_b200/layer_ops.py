@@ -132,5 +132,17 @@ def rope_kv_append(q, k, v, cos_half, sin_half, k_cache, v_cache, prefix: int, h
     return out.view(b, t, heads, d)
 
 
+def swiglu_backward(d, gate, up):
+    """(d_gate, d_up) of act = silu(gate) * up for upstream d (fitq_swiglu_bwd)."""
+    gate, up = _c(gate), _c(up)
+    d = _c(d.to(gate.dtype)).view(gate.shape)
+    dg, du = torch.empty_like(gate), torch.empty_like(up)
+    L = _lib.load()
+    with torch.cuda.device(gate.device):
+        _lib.check(L.fitq_swiglu_bwd(d.data_ptr(), gate.data_ptr(), up.data_ptr(), dg.data_ptr(),
+                                     du.data_ptr(), gate.numel(), _st(gate)), "fitq_swiglu_bwd")
+    return dg, du
+
+
 def swiglu(gate, up):
     return SwiGLUFn.apply(gate, up)

@@ -89,8 +89,9 @@ def test_mlp_module_fused_vs_unfused(cuda_dev, m, hidden, inter):
     res = (torch.randn(m, seq, hidden, generator=g, device=cuda_dev)).bfloat16()
     dy = (torch.randn(m, seq, hidden, generator=g, device=cuda_dev)).bfloat16()
 
-    def run(fused):
+    def run(fused, fused_backward=True):
         mlp.fused = fused
+        mlp.fused_backward = fused_backward
         xi = x.clone().requires_grad_(True)
         ri = res.clone().requires_grad_(True)
         out = mlp(xi, ri)
@@ -98,8 +99,11 @@ def test_mlp_module_fused_vs_unfused(cuda_dev, m, hidden, inter):
         return out.detach(), xi.grad, ri.grad
 
     yf, dxf, drf = run(True)
+    yh, dxh, drh = run(True, fused_backward=False)
     yu, dxu, dru = run(False)
     torch.cuda.synchronize()
+    # forward fused, backward through the separate SwiGLU kernel: same bits as fused
+    assert torch.equal(yh, yf) and torch.equal(dxh, dxf) and torch.equal(drh, drf)
     assert torch.equal(yf, yu)
     assert torch.equal(drf, dru)
     # the two dx sums differ by the rounding of one bf16 term: a few bf16 ulps
