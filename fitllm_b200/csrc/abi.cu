@@ -1072,6 +1072,20 @@ std::atomic<long long> g_launches{0};
 }
 namespace fitq {
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool set_smem_limit(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<int, const void*>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& d : done)
+    if (d.first == dev && d.second == fn) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done.emplace_back(dev, fn);
+  return true;
+}
 }  // namespace fitq
 extern "C" long long fitq_launch_count(void) { return g_launches.load(); }
 

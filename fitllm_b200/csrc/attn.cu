@@ -331,8 +331,7 @@ int att_ctas_per_sm() {
   static int n = 0;
   if (n == 0) {
     int v = 0;
-    if (cudaFuncSetAttribute(verify_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kAttSmem) != cudaSuccess ||
+    if (!set_smem_limit(verify_attn_kernel, kAttSmem) ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, verify_attn_kernel, kAttThreads, kAttSmem) !=
             cudaSuccess ||
         v < 1)
@@ -392,13 +391,7 @@ int launch_verify_attention(const void* q, const void* k_cache, const void* v_ca
   p.splits = splits;
   p.tiles_per_split = (tiles + splits - 1) / splits;
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kAttD));
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(verify_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kAttSmem) != cudaSuccess)
-      return FITQ_ERR_CUDA;
-    attr = true;
-  }
+  if (!set_smem_limit(verify_attn_kernel, kAttSmem)) return FITQ_ERR_CUDA;
   cudaError_t e = launch_pdl(verify_attn_kernel, dim3(splits, kv_heads, static_cast<unsigned>(batch)),
                              dim3(kAttThreads), kAttSmem, st, p);
   note_launch();

@@ -384,13 +384,7 @@ int launch_gemm_bf16_tn_bn(const GemmArgs& g, cudaStream_t st, int num_sms) {
     p.group_m = gm ? atoi(gm) : GROUP_M;
     if (p.group_m < 1) p.group_m = GROUP_M;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMEM_BYTES)) != cudaSuccess)
-      return FITQ_ERR_CUDA;
-    attr_set = true;
-  }
+  if (!set_smem_limit(gemm_bf16_tn_kernel<BN>, static_cast<int>(SMEM_BYTES))) return FITQ_ERR_CUDA;
   const int tiles = p.num_m * p.num_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *

@@ -1001,15 +1001,9 @@ static int launch_dec(const DecJobs& jb, const void* x, int64_t m, const GemvEpi
   auto xb = static_cast<const __nv_bfloat16*>(x);
   const int M = static_cast<int>(m);
   const dim3 grid(static_cast<unsigned>(pl.cs * pl.slices));
-  static bool attr[2] = {false, false};
   const bool nested = w.absmax_f32 == nullptr;
-  if (!attr[nested]) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        nested ? nf4_gemv_dec_kernel<true> : nf4_gemv_dec_kernel<false>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
-    if (e != cudaSuccess) return FITQ_ERR_CUDA;
-    attr[nested] = true;
-  }
+  if (!set_smem_limit(nested ? nf4_gemv_dec_kernel<true> : nf4_gemv_dec_kernel<false>, kDecSmem))
+    return FITQ_ERR_CUDA;
   cudaError_t e =
       nested ? launch_pdl(nf4_gemv_dec_kernel<true>, grid, dim3(kThreads), kDecSmem, st, jb, xb, M, pl, out)
              : launch_pdl(nf4_gemv_dec_kernel<false>, grid, dim3(kThreads), kDecSmem, st, jb, xb, M, pl, out);
@@ -1074,19 +1068,17 @@ int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* part
   const int grid = static_cast<int>(items < num_sms ? items : num_sms);
   auto xb = static_cast<const __nv_bfloat16*>(x);
   const int M = static_cast<int>(m);
-  static bool attr[9][3] = {};
   cudaError_t e = cudaSuccess;
 #define FITQ_GEMV_CASE(T, C)                                                                      \
   if (p.nt8 == T && p.ch == C) {                                                                  \
-    if (!attr[T][C / 2]) {                                                                        \
-      e = cudaFuncSetAttribute(nf4_gemv_kernel<T, C>,                                             \
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);          \
-      attr[T][C / 2] = (e == cudaSuccess);                                                        \
+    if (!set_smem_limit(nf4_gemv_kernel<T, C>, 200 * 1024)) {                                    \
+      e = cudaErrorInvalidValue;                                                                  \
+    } else {                                                                                      \
+      nf4_gemv_kernel<T, C><<<grid, kThreads, p.smem, st>>>(w, xb, M, p.rt, p.kcb,                \
+                                                             static_cast<int>(p.row_groups),      \
+                                                             static_cast<int>(items), partial);   \
+      note_launch();                                                                              \
     }                                                                                             \
-    nf4_gemv_kernel<T, C><<<grid, kThreads, p.smem, st>>>(w, xb, M, p.rt, p.kcb,                  \
-                                                           static_cast<int>(p.row_groups),        \
-                                                           static_cast<int>(items), partial);     \
-    note_launch();                                                                                \
   }
   FITQ_GEMV_CASE(1, 4)
   FITQ_GEMV_CASE(2, 4)

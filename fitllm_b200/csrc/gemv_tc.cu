@@ -554,13 +554,8 @@ int launch_nf4_gemv_tc_grouped(const Nf4Args* w, int groups, const void* x, int6
   cudaError_t e = cudaSuccess;
 #define FITQ_TC_CASE(NT)                                                                        \
   if (pl.ntok == NT) {                                                                          \
-    static bool attr[2] = {false, false};                                                       \
     auto kern = nested ? nf4_gemv_tc_kernel<NT, true> : nf4_gemv_tc_kernel<NT, false>;          \
-    if (!attr[nested]) {                                                                        \
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);     \
-      if (e != cudaSuccess) return FITQ_ERR_CUDA;                                               \
-      attr[nested] = true;                                                                      \
-    }                                                                                           \
+    if (!set_smem_limit(kern, kTcSmem)) return FITQ_ERR_CUDA;                                   \
     e = launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(kTcThreads), kTcSmem, st,     \
                    tm_w[0], tm_w[1], tm_w[2], tm_x, p);                                         \
   }

@@ -258,6 +258,15 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
 int timing_begin(cudaStream_t st, double flops);
 // Counts kernel launches made by the library (read by fitq_launch_count).
 void note_launch();
+// Raise a kernel's dynamic shared-memory limit to `bytes` on the current
+// device, once per (device, kernel): kernel attributes belong to a device's
+// context, so a process that drives several GPUs sets them on each.  False
+// when CUDA refuses.
+bool set_smem_limit(const void* fn, int bytes);
+template <typename F>
+bool set_smem_limit(F* fn, int bytes) {
+  return set_smem_limit(reinterpret_cast<const void*>(fn), bytes);
+}
 // W[n,k] (bf16 / fp16, in place) += scale * (B[n,:] . A[:,k]); see merge.cu.
 int launch_lora_merge(void* w, int out_dtype, int64_t n, int64_t k, const float* a, const float* b,
                       int rank, float scale, cudaStream_t st);

@@ -457,13 +457,8 @@ int launch_lora_t(const void* x, int64_t M, int64_t K, const float* a, int r, fl
                   cudaStream_t st) {
   if (K % kTCols != 0 || M < 1 || M > 64 || r < 1 || r > 64 || r % 4 != 0) return FITQ_ERR_UNSUPPORTED;
   const size_t smem = static_cast<size_t>(r + M) * (kTCols + 1) * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(lora_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (64 + 64) * (kTCols + 1) * static_cast<int>(sizeof(float))) != cudaSuccess)
-      return FITQ_ERR_CUDA;
-    attr = true;
-  }
+  if (!set_smem_limit(lora_t_kernel, (64 + 64) * (kTCols + 1) * static_cast<int>(sizeof(float))))
+    return FITQ_ERR_CUDA;
   int tp = 32;  // lanes per (m, j) dot product: fill the 256 threads
   while (tp > 1 && static_cast<int64_t>(256 / tp) < M * r) tp >>= 1;
   const cudaError_t e = launch_pdl(lora_t_kernel, dim3(static_cast<unsigned>(K / kTCols)), dim3(256),
