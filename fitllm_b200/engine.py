@@ -96,6 +96,7 @@ class ShardStationaryEngine:
         for the backward's temporaries."""
         self.keep_activations = keep_activations
         self.keep_budget_fraction = keep_budget_fraction
+        self._keep_cache = {}  # tokens -> layers kept ("auto")
         self._graphs: Dict[int, tuple] = {}
         self.last_kept = 0
         self.cfg = cfg
@@ -137,13 +138,22 @@ class ShardStationaryEngine:
     def _layers_to_keep(self, tokens: int) -> int:
         k = self.keep_activations
         if k == "auto":
+            # Measured on the first step of a token count and reused after:
+            # cudaMemGetInfo costs ~1 ms of host time and can wait behind the
+            # queued work, which at a few micro-batches per GPU starves the
+            # device of launches.
+            cached = self._keep_cache.get(tokens)
+            if cached is not None:
+                return cached
             # free HBM plus what the caching allocator holds but does not use
             # (the previous step's kept activations come back to it)
             free, _ = torch.cuda.mem_get_info(self.device)
             free += torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
             budget = self.keep_budget_fraction * free
             per = tokens * self.saved_bytes_per_token()
-            k = int(budget // max(per, 1))
+            k = max(0, min(int(budget // max(per, 1)), self.num_layers))
+            self._keep_cache[tokens] = k
+            return k
         return max(0, min(int(k), self.num_layers))
 
     def forward(self, h: torch.Tensor) -> List[torch.Tensor]:
