@@ -64,7 +64,16 @@ enum {
   FITQ_ERR_NO_DEVICE = 8    /* no usable sm_100 device                       */
 };
 
-/* A cudaStream_t (CUstream) handle; NULL is the legacy default stream. */
+/* A cudaStream_t (CUstream) handle; NULL is the legacy default stream.
+ * Every call is asynchronous on the given stream.  fitq_qlora_fwd and
+ * fitq_qlora_bwd on the GEMM path (M > 64) fork the weight-side launches
+ * (NF4 dequant, LoRA weight padding) onto one internal stream per device and
+ * join it back before returning, with events, so a call captured into a CUDA
+ * graph captures the fork too; set FITQ_SIDE_STREAM=0 in the environment to
+ * keep every launch on the given stream.  The internal stream is shared by
+ * the process's calls on that device: a stream capture on one host thread
+ * must not overlap uncaptured GEMM-path calls on the same device from
+ * another thread. */
 typedef void* fitq_stream_t;
 
 /* One NF4 weight W[N,K] in the bitsandbytes Params4bit layout (flat keys
