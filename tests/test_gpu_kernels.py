@@ -495,3 +495,38 @@ def test_bounded_wait_timeout_leaves_context_usable(cuda_dev):
     c = ops.gemm_bf16_tn(a, b)
     assert onf4.rel_err(c.float().cpu().numpy(), (a.float() @ b.float().T).cpu().numpy()) < 4e-3
     assert ops.device_status() == 0
+
+
+def test_side_stream_off_gives_same_bits(cuda_dev, tmp_path):
+    """The QLoRA GEMM path with its weight side on the caller's stream
+    (FITQ_SIDE_STREAM=0, read once per process, so run in a child process)
+    returns the same bits as with the forked side stream."""
+    import subprocess
+    import sys
+    script = tmp_path / "side.py"
+    out = tmp_path / "out_{}.pt"
+    script.write_text(
+        "import sys, torch\n"
+        "sys.path.insert(0, %r)\n"
+        "from fitllm_b200 import ops\n"
+        "from fitllm_b200.qlora import Linear4bit\n"
+        "dev = torch.device('cuda', 0)\n"
+        "g = torch.Generator(device=dev).manual_seed(3)\n"
+        "w = Linear4bit.from_float(torch.randn(1024, 768, generator=g, device=dev) * 0.02, None).wref()\n"
+        "x = torch.randn(300, 768, generator=g, device=dev).bfloat16()\n"
+        "dy = torch.randn(300, 1024, generator=g, device=dev).bfloat16()\n"
+        "A = torch.randn(16, 768, generator=g, device=dev) * 0.02\n"
+        "B = torch.randn(1024, 16, generator=g, device=dev) * 0.02\n"
+        "y, t = ops.qlora_forward(x, w, A, B, 2.0, want_t=True)\n"
+        "dx, ga, gb = ops.qlora_backward(x, dy, w, A, B, 2.0, t_saved=t)\n"
+        "torch.cuda.synchronize()\n"
+        "torch.save([v.cpu() for v in (y, t, dx, ga, gb)], sys.argv[1])\n" % str(__import__('pathlib').Path(__file__).resolve().parents[1]))
+    import os
+    res = []
+    for side in ("1", "0"):
+        env = dict(os.environ, FITQ_SIDE_STREAM=side, FITQ_NF4_FUSED="0")
+        path = str(out).format(side)
+        subprocess.run([sys.executable, str(script), path], check=True, env=env, timeout=300)
+        res.append(torch.load(path))
+    for a, b in zip(*res):
+        assert torch.equal(a, b)
