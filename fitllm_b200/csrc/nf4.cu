@@ -42,25 +42,43 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args w, OutT* __res
   if (threadIdx.x < 16) s_qm[threadIdx.x] = w.quant_map[threadIdx.x];
   if (w.nested_quant_map != nullptr) s_nqm[threadIdx.x] = w.nested_quant_map[threadIdx.x];
   __syncthreads();
-  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < n_items;
-       it += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(w.packed) + it);
-    const float am = absmax_of_block(w, it >> 1, s_nqm);
-    uint32_t words[4] = {q.x, q.y, q.z, q.w};
-    uint32_t o[16];
+  // Four items per thread per pass, their loads issued together: one item's
+  // load-to-use latency alone left HBM half idle.
+  constexpr int U = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t it0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it0 < n_items; it0 += U * stride) {
+    uint4 q[U];
+    float am[U];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        uint32_t byte = (words[j] >> (8 * b)) & 0xFFu;
-        float hi = __fmul_rn(s_qm[byte >> 4], am);
-        float lo = __fmul_rn(s_qm[byte & 0xF], am);
-        o[j * 4 + b] = pack2<OutT>(hi, lo);  // element 2i (high nibble) first in memory
-      }
+    for (int u = 0; u < U; ++u) {
+      const int64_t it = it0 + u * stride;
+      if (it < n_items) q[u] = __ldg(reinterpret_cast<const uint4*>(w.packed) + it);
     }
-    uint4* dst = reinterpret_cast<uint4*>(out) + it * 4;
 #pragma unroll
-    for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+    for (int u = 0; u < U; ++u) {
+      const int64_t it = it0 + u * stride;
+      am[u] = it < n_items ? absmax_of_block(w, it >> 1, s_nqm) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t it = it0 + u * stride;
+      if (it >= n_items) break;
+      const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+      uint32_t o[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          uint32_t byte = (words[j] >> (8 * b)) & 0xFFu;
+          float hi = __fmul_rn(s_qm[byte >> 4], am[u]);
+          float lo = __fmul_rn(s_qm[byte & 0xF], am[u]);
+          o[j * 4 + b] = pack2<OutT>(hi, lo);  // element 2i (high nibble) first in memory
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out) + it * 4;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+    }
   }
 }
 
@@ -70,42 +88,62 @@ template <typename OutT>
 __global__ void __launch_bounds__(256) nf4_dequant_t_kernel(Nf4Args w, OutT* __restrict__ out) {
   __shared__ float s_qm[16];
   __shared__ float s_nqm[256];
-  __shared__ uint16_t s_t[64][64 + 8];  // [k][n], padded rows
+  // [tile of the pass][k][n], padded rows; two tiles per pass, their loads
+  // issued together (one 8-byte load in flight per thread left HBM idle)
+  __shared__ uint16_t s_t[2][64][64 + 8];
   if (threadIdx.x < 16) s_qm[threadIdx.x] = w.quant_map[threadIdx.x];
   if (w.nested_quant_map != nullptr) s_nqm[threadIdx.x] = w.nested_quant_map[threadIdx.x];
   __syncthreads();
   const int64_t N = w.n_out, K = w.k_in;
   const int64_t tiles_k = K / 64;
   const int64_t n_tiles = (N / 64) * tiles_k;
-  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-    const int64_t n0 = (tile / tiles_k) * 64, k0 = (tile % tiles_k) * 64;
-    const int r = threadIdx.x >> 2;  // row n0 + r
-    const int part = threadIdx.x & 3;  // weights k0 + 16*part .. +15
-    const int64_t elem = (n0 + r) * K + k0 + 16 * part;
-    const uint2 q = __ldg(reinterpret_cast<const uint2*>(w.packed + (elem >> 1)));
-    const float am = absmax_of_block(w, elem >> 6, s_nqm);
-    uint32_t words[2] = {q.x, q.y};
+  const int r = threadIdx.x >> 2;  // row n0 + r
+  const int part = threadIdx.x & 3;  // weights k0 + 16*part .. +15
+  for (int64_t tile0 = blockIdx.x; tile0 < n_tiles; tile0 += 2 * (int64_t)gridDim.x) {
+    uint2 q[2];
+    float am[2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int u = 0; u < 2; ++u) {
+      const int64_t tile = tile0 + u * (int64_t)gridDim.x;
+      if (tile < n_tiles) {
+        const int64_t n0 = (tile / tiles_k) * 64, k0 = (tile % tiles_k) * 64;
+        const int64_t elem = (n0 + r) * K + k0 + 16 * part;
+        q[u] = __ldg(reinterpret_cast<const uint2*>(w.packed + (elem >> 1)));
+        am[u] = absmax_of_block(w, elem >> 6, s_nqm);
+      }
+    }
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        uint32_t byte = (words[j] >> (8 * b)) & 0xFFu;
-        uint32_t p = pack2<OutT>(__fmul_rn(s_qm[byte >> 4], am), __fmul_rn(s_qm[byte & 0xF], am));
-        // column rotated by 16*part: spreads the four parts over distinct banks
-        int kk = 16 * part + 8 * j + 2 * b;
-        int col = (r + 16 * part) & 63;
-        s_t[kk][col] = static_cast<uint16_t>(p & 0xFFFFu);
-        s_t[kk + 1][col] = static_cast<uint16_t>(p >> 16);
+    for (int u = 0; u < 2; ++u) {
+      if (tile0 + u * (int64_t)gridDim.x >= n_tiles) break;  // block-uniform
+      const uint32_t words[2] = {q[u].x, q[u].y};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          uint32_t byte = (words[j] >> (8 * b)) & 0xFFu;
+          uint32_t p = pack2<OutT>(__fmul_rn(s_qm[byte >> 4], am[u]), __fmul_rn(s_qm[byte & 0xF], am[u]));
+          // column rotated by 16*part: spreads the four parts over distinct banks
+          int kk = 16 * part + 8 * j + 2 * b;
+          int col = (r + 16 * part) & 63;
+          s_t[u][kk][col] = static_cast<uint16_t>(p & 0xFFFFu);
+          s_t[u][kk + 1][col] = static_cast<uint16_t>(p >> 16);
+        }
       }
     }
     __syncthreads();
-    // 64 rows (k) x 128 bytes: 8 threads per row, 16 bytes each.
+    // per tile: 64 rows (k) x 128 bytes: 8 threads per row, 16 bytes each.
 #pragma unroll
-    for (int pass = 0; pass < 2; ++pass) {
-      const int kr = (threadIdx.x >> 3) + 32 * pass;
-      const int c8 = threadIdx.x & 7;
-      const uint4 v = *reinterpret_cast<const uint4*>(&s_t[kr][(c8 * 8 + 16 * (kr >> 4)) & 63]);
-      *reinterpret_cast<uint4*>(out + (k0 + kr) * N + n0 + c8 * 8) = v;
+    for (int u = 0; u < 2; ++u) {
+      const int64_t tile = tile0 + u * (int64_t)gridDim.x;
+      if (tile >= n_tiles) break;  // block-uniform
+      const int64_t n0 = (tile / tiles_k) * 64, k0 = (tile % tiles_k) * 64;
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int kr = (threadIdx.x >> 3) + 32 * pass;
+        const int c8 = threadIdx.x & 7;
+        const uint4 v = *reinterpret_cast<const uint4*>(&s_t[u][kr][(c8 * 8 + 16 * (kr >> 4)) & 63]);
+        *reinterpret_cast<uint4*>(out + (k0 + kr) * N + n0 + c8 * 8) = v;
+      }
     }
     __syncthreads();
   }
