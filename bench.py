@@ -230,6 +230,58 @@ def gemv_sweep(dev, peak_gbs, reps=20, cpu=True):
                 "value": round(c["GB/s"], 3), "unit": "GB/s", "cores": c["threads"], "kind": "port",
                 "sample": f"one M=1 call on the host cores: torch dequant in the oracle's op order + "
                           f"fp32 product ({c['us'] / 1000:.1f} ms)"}
+    # The projections a decode layer issues together: q/k/v of one x as one
+    # grouped call (LoRA on q and v) and gate/up with the SwiGLU applied
+    # (fitq_nf4_gemv_grouped / fitq_nf4_gemv_swiglu): one GEMV launch and one
+    # finishing launch each for M <= 8 (tcgen05 for larger M).
+    for name, parts, swiglu in (("qkv_grouped", [(5120, 16), (1024, 0), (1024, 16)], False),
+                                ("gate_up_swiglu", [(27648, 0), (27648, 0)], True)):
+        k = 5120
+        wbytes = sum(n * k // 2 + n * k // 64 + ((n * k // 64 + 255) // 256) * 4 for n, _ in parts)
+        nsets = max(2, int(2 * l2 // wbytes) + 1)
+        sets = []
+        for _ in range(nsets):
+            jobs = []
+            for n, r in parts:
+                w = torch.randn(n, k, generator=g, device=dev) * 0.02
+                wr = Nf4WeightCRef(*quantize_nf4(w))
+                del w
+                A = (torch.rand(r, k, generator=g, device=dev) - 0.5) * 0.02 if r else None
+                B = torch.randn(n, r, generator=g, device=dev) * 0.01 if r else None
+                jobs.append((wr, A, B, 2.0, None, None))
+            sets.append(jobs)
+        for m in (1, 4, 16, 64):
+            x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+
+            def call(jobs):
+                if swiglu:
+                    ops.nf4_gemv_swiglu(x, jobs[0], jobs[1])
+                else:
+                    ops.nf4_gemv_grouped(x, jobs)
+
+            for jobs in sets[:2]:
+                call(jobs)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for jobs in sets:
+                    call(jobs)
+            graph.replay()
+            torch.cuda.synchronize()
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            for _ in range(reps):
+                graph.replay()
+            e_ev.record()
+            torch.cuda.synchronize()
+            us = s_ev.elapsed_time(e_ev) * 1000.0 / (reps * nsets)
+            gbs = wbytes / (us * 1e-6) / 1e9
+            out[f"{name}_m{m}"] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                                   "frac_of_hbm": round(gbs / peak_gbs, 3),
+                                   "weights": [f"{n}x{k}" + ("+lora" if r else "") for n, r in parts]}
+            del graph
+        del sets
+        torch.cuda.empty_cache()
     return out
 
 
