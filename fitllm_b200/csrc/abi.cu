@@ -193,9 +193,17 @@ int launch_status(int rc, const char* what) {
 // materialised dequant + bf16 GEMM, by measured throughput per shape;
 // FITQ_NF4_FUSED=1 / 0 in the environment forces one (shapes the fused
 // kernels do not take always use the dequant path).
+//
+// Measured on one B200 (whole call, CUDA-graph replay, L2 flushed): the fused
+// kernel wins only where the GEMM's output side is the long one (four times
+// the reduction) and the rows are few, so the dequant pass of the 283 MB
+// bf16 weight weighs most against the GEMM: at M = 2,048 gate/up forward
+// (N 27,648, K 5,120) 448.5 vs 458.8 µs and down_proj dX (output 27,648,
+// reduction 5,120) 456.8 vs 471.0 µs; at M = 4,096 and on every other
+// Qwen2.5-32B shape the dequant path is faster (up to 1.45x).
 bool fused_faster(int64_t m, int64_t n_out, int64_t k_in, int trans) {
-  (void)m; (void)n_out; (void)k_in; (void)trans;
-  return false;
+  if (m > 2048) return false;
+  return trans == 0 ? n_out >= 4 * k_in : k_in >= 4 * n_out;
 }
 
 bool use_fused_gemm(int64_t m, int64_t n_out, int64_t k_in, int trans) {

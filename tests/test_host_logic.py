@@ -58,6 +58,13 @@ def test_abi_rejects_bad_arguments_without_a_device():
         os.environ.pop("FITQ_NF4_FUSED", None)
     # shapes the fused GEMM does not take (N % 128 != 0) keep the dequant path
     assert L.fitq_qlora_fwd_workspace(512, 320, 256, 16) > 320 * 256 * 2
+    # by default the fused GEMM takes few-row GEMMs whose output side is 4x the
+    # reduction (gate/up forward, down_proj dX at M <= 2048), dequant otherwise
+    assert L.fitq_qlora_fwd_workspace(2048, 27648, 5120, 0) < 27648 * 5120 // 2
+    assert L.fitq_qlora_bwd_workspace(2048, 5120, 27648, 0) < 27648 * 5120 // 2
+    assert L.fitq_qlora_fwd_workspace(4096, 27648, 5120, 0) >= 27648 * 5120 * 2
+    assert L.fitq_qlora_fwd_workspace(2048, 5120, 27648, 0) >= 27648 * 5120 * 2
+    assert L.fitq_qlora_bwd_workspace(2048, 27648, 5120, 0) >= 27648 * 5120 * 2
 
 
 # ---------------------------------------------------------------- reference API
