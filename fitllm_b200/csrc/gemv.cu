@@ -1011,12 +1011,19 @@ static int launch_dec(const DecJobs& jb, const void* x, int64_t m, const GemvEpi
   return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
+// Blocks per token row of the finishing kernels: 128 outputs each (their
+// loads of the slice partials and of lora_b are latency-bound, so more blocks
+// in flight finish sooner), at most 128.
+static int64_t finish_blocks(int64_t n) {
+  const int64_t nb = (n + 127) / 128;
+  return nb > 128 ? 128 : nb;
+}
+
 int launch_nf4_gemv_dec_finish(int64_t m, int64_t n_out, int slices, const GemvEpilogue& out,
                                cudaStream_t st, int num_sms) {
   (void)num_sms;
   if (out.rank > 64) return FITQ_ERR_UNSUPPORTED;
-  int64_t nb = (n_out + 511) / 512;
-  if (nb > 64) nb = 64;
+  int64_t nb = finish_blocks(n_out);
   const size_t smem = out.rank > 0 ? kFinStage * sizeof(float) : 0;
   const cudaError_t e = launch_pdl(gemv_dec_finish_kernel,
                                    dim3(static_cast<unsigned>(nb), static_cast<unsigned>(m)), dim3(256),
@@ -1037,8 +1044,7 @@ int launch_nf4_gemv_group_finish(int64_t m, const int64_t* n_out, int jobs, int 
     gf.n[j] = static_cast<int>(n_out[jj]);
     if (eps[jj].rank > 64 || (swiglu_act && eps[jj].rank > 0)) return FITQ_ERR_UNSUPPORTED;
     if (j < used) {
-      int64_t nb = (n_out[j] + 511) / 512;
-      if (nb > 64) nb = 64;
+      int64_t nb = finish_blocks(n_out[j]);
       end += static_cast<int>(nb);
       rank_any |= eps[j].rank;
     }
