@@ -685,14 +685,24 @@ static int grouped_impl(const fitq_gemv_job* jobs, int count, const void* x, int
   if (rc) return launch_status(rc, tc ? "nf4_gemv_grouped tcgen05" : "nf4_gemv_grouped decode");
   fitq::GemvEpilogue ep[3];
   int64_t n_out[3];
+  const float* t_a[3];
+  int t_r[3];
+  float* t_out[3];
+  int t_jobs = 0;
   for (int g = 0; g < count; ++g) {
     const fitq_gemv_job& j = jobs[g];
-    if (j.rank > 0 && (rc = fitq::launch_lora_t(x, m, K, j.lora_a, j.rank, t_part[g], st)))
-      return launch_status(rc, "lora T = x.A^T");
+    if (j.rank > 0) {  // every job's T partials in one launch
+      t_a[t_jobs] = j.lora_a;
+      t_r[t_jobs] = j.rank;
+      t_out[t_jobs] = t_part[g];
+      ++t_jobs;
+    }
     ep[g] = fitq::GemvEpilogue{j.y, j.y_add, j.bias, j.lora_b, t_part[g], fitq::lora_t_groups(K), nullptr,
                                j.rank, j.scale, partial[g]};
     n_out[g] = a[g].n_out;
   }
+  if (t_jobs > 0 && (rc = fitq::launch_lora_t_multi(x, m, K, t_a, t_r, t_out, t_jobs, st)))
+    return launch_status(rc, "lora T = x.A^T");
   return launch_status(fitq::launch_nf4_gemv_group_finish(m, n_out, count, slices, ep, act, st),
                        "nf4_gemv_grouped finish");
 }

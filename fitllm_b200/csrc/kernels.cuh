@@ -134,6 +134,9 @@ size_t lora_t_workspace(int64_t M, int64_t K, int r);
 int lora_t_groups(int64_t K);
 int launch_lora_t(const void* x, int64_t M, int64_t K, const float* a, int r, float* part_ws,
                   cudaStream_t st);
+// The same for 1-3 (A, rank, partials) jobs on one x in one launch.
+int launch_lora_t_multi(const void* x, int64_t M, int64_t K, const float* const* a, const int* r,
+                        float* const* part_ws, int jobs, cudaStream_t st);
 
 int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, const void* wt_bf16,
                         int r, void* out_pad, void* out_dense, cudaStream_t st, int num_sms);

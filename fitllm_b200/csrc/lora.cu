@@ -334,11 +334,24 @@ void colproj_geometry(int64_t M, int64_t D, int num_sms, int64_t* rows_per_chunk
 // GEMV's partial sums too.
 constexpr int kTCols = 64;
 
+// blockIdx.y picks one of up to three (A, rank, partials) jobs on the same x
+// (the LoRA projections of a grouped q/k/v call share one launch).
+struct LoraTJobs {
+  const float* a[3];
+  float* part[3];
+  int r[3];
+  int tp[3];
+};
+
 __global__ void __launch_bounds__(256)
-    lora_t_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, const float* __restrict__ a,
-                  int r, int tp, float* __restrict__ part) {
+    lora_t_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, LoraTJobs tj) {
   extern __shared__ float s_lt[];
   pdl_launch_dependents();
+  const int jy = blockIdx.y;
+  const float* __restrict__ a = jy == 0 ? tj.a[0] : jy == 1 ? tj.a[1] : tj.a[2];
+  float* __restrict__ part = jy == 0 ? tj.part[0] : jy == 1 ? tj.part[1] : tj.part[2];
+  const int r = jy == 0 ? tj.r[0] : jy == 1 ? tj.r[1] : tj.r[2];
+  const int tp = jy == 0 ? tj.tp[0] : jy == 1 ? tj.tp[1] : tj.tp[2];
   constexpr int pitch = kTCols + 1;
   const int c0 = blockIdx.x * kTCols;
   float* as = s_lt;
@@ -453,19 +466,35 @@ size_t lora_t_workspace(int64_t M, int64_t K, int r) {
 
 int lora_t_groups(int64_t K) { return static_cast<int>(K / kTCols); }
 
-int launch_lora_t(const void* x, int64_t M, int64_t K, const float* a, int r, float* part_ws,
-                  cudaStream_t st) {
-  if (K % kTCols != 0 || M < 1 || M > 64 || r < 1 || r > 64 || r % 4 != 0) return FITQ_ERR_UNSUPPORTED;
-  const size_t smem = static_cast<size_t>(r + M) * (kTCols + 1) * sizeof(float);
+int launch_lora_t_multi(const void* x, int64_t M, int64_t K, const float* const* a, const int* r,
+                        float* const* part_ws, int jobs, cudaStream_t st) {
+  if (K % kTCols != 0 || M < 1 || M > 64 || jobs < 1 || jobs > 3) return FITQ_ERR_UNSUPPORTED;
+  LoraTJobs tj{};
+  int r_max = 0;
+  for (int j = 0; j < 3; ++j) {
+    const int jj = j < jobs ? j : jobs - 1;
+    if (r[jj] < 1 || r[jj] > 64 || r[jj] % 4 != 0) return FITQ_ERR_UNSUPPORTED;
+    tj.a[j] = a[jj];
+    tj.part[j] = part_ws[jj];
+    tj.r[j] = r[jj];
+    int tp = 32;  // lanes per (m, j) dot product: fill the 256 threads
+    while (tp > 1 && static_cast<int64_t>(256 / tp) < M * r[jj]) tp >>= 1;
+    tj.tp[j] = tp;
+    r_max = r[jj] > r_max ? r[jj] : r_max;
+  }
+  const size_t smem = static_cast<size_t>(r_max + M) * (kTCols + 1) * sizeof(float);
   if (!set_smem_limit(lora_t_kernel, (64 + 64) * (kTCols + 1) * static_cast<int>(sizeof(float))))
     return FITQ_ERR_CUDA;
-  int tp = 32;  // lanes per (m, j) dot product: fill the 256 threads
-  while (tp > 1 && static_cast<int64_t>(256 / tp) < M * r) tp >>= 1;
-  const cudaError_t e = launch_pdl(lora_t_kernel, dim3(static_cast<unsigned>(K / kTCols)), dim3(256),
+  const cudaError_t e = launch_pdl(lora_t_kernel, dim3(static_cast<unsigned>(K / kTCols), jobs), dim3(256),
                                    smem, st, static_cast<const __nv_bfloat16*>(x), static_cast<int>(M),
-                                   static_cast<int>(K), a, r, tp, part_ws);
+                                   static_cast<int>(K), tj);
   note_launch();
   return e == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+}
+
+int launch_lora_t(const void* x, int64_t M, int64_t K, const float* a, int r, float* part_ws,
+                  cudaStream_t st) {
+  return launch_lora_t_multi(x, M, K, &a, &r, &part_ws, 1, st);
 }
 
 size_t lora_colproj_workspace(int64_t M, int64_t D, int r, int num_sms) {
