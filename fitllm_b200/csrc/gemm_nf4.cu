@@ -182,6 +182,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();  // the set-up above overlaps the previous kernel; A, B and C are touched after it
 
   const int num_tiles = p.num_m * p.num_n;
   const int num_kb = p.k / BK;
@@ -527,7 +529,7 @@ int launch_gemm_nf4(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(n) *
                        static_cast<double>(k + g.lora_k);
   const int slot = timing_begin(st, flops);
-  gemm_nf4_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tp, tpa, tpb, p);
+  launch_pdl(gemm_nf4_kernel, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, st, ta, tp, tpa, tpb, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

@@ -201,6 +201,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();  // barrier inits, the nested map and TMEM allocation visible to the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();  // the set-up above overlaps the previous kernel; A, B and C are touched after it
 
   const int num_tiles = p.num_m * p.num_n;
   const int cluster_id = blockIdx.x >> 1;
@@ -561,9 +563,11 @@ int launch_gemm_nf4_2cta(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
                        static_cast<double>(k + g.lora_k);
   const int slot = timing_begin(st, flops);
   if (msub == 1)
-    gemm_nf4_2cta_kernel<1><<<2 * clusters, NUM_THREADS, Cfg<1>::SMEM, st>>>(ta, tp, tpa, tpb, p);
+    launch_pdl(gemm_nf4_2cta_kernel<1>, dim3(2 * clusters), dim3(NUM_THREADS), Cfg<1>::SMEM, st, ta, tp, tpa,
+               tpb, p);
   else
-    gemm_nf4_2cta_kernel<2><<<2 * clusters, NUM_THREADS, Cfg<2>::SMEM, st>>>(ta, tp, tpa, tpb, p);
+    launch_pdl(gemm_nf4_2cta_kernel<2>, dim3(2 * clusters), dim3(NUM_THREADS), Cfg<2>::SMEM, st, ta, tp, tpa,
+               tpb, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

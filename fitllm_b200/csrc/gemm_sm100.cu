@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const __grid_constant__ CUtensorMap tm_pa,
                         const __grid_constant__ CUtensorMap tm_pb, const Params p) {
   static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "UMMA N for M = 128");
+  pdl_launch_dependents();
   constexpr int B_BYTES = b_bytes<BN>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -116,6 +117,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the set-up above overlaps the previous kernel; A, B and C are touched after it
 
   const int num_tiles = p.num_m * p.num_n;
   const int num_kb = p.k / BK;
@@ -390,7 +392,7 @@ int launch_gemm_bf16_tn_bn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *
                        static_cast<double>(g.k + g.lora_k);
   const int slot = timing_begin(st, flops);
-  gemm_bf16_tn_kernel<BN><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, p);
+  launch_pdl(gemm_bf16_tn_kernel<BN>, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, st, ta, tb, tpa, tpb, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

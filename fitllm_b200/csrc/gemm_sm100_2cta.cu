@@ -143,6 +143,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();  // barrier inits and TMEM allocation visible to the peer
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();  // the set-up above overlaps the previous kernel; A, B and C are touched after it
 
   const int num_tiles = p.num_m * p.num_n;
   const int cluster_id = blockIdx.x >> 1;
@@ -488,7 +490,8 @@ int launch_gemm_bf16_tn_2cta_bn(const GemmArgs& g, cudaStream_t st, int num_sms)
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(g.n) *
                        static_cast<double>(g.k + g.lora_k) * (two_b ? 2.0 : 1.0);
   const int slot = timing_begin(st, flops);
-  gemm_bf16_tn_2cta_kernel<BN><<<2 * clusters, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, tpa, tpb, tb2, p);
+  launch_pdl(gemm_bf16_tn_2cta_kernel<BN>, dim3(2 * clusters), dim3(NUM_THREADS), SMEM_BYTES, st, ta, tb, tpa, tpb,
+             tb2, p);
   note_launch();
   timing_end(slot, st);
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;

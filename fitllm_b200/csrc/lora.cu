@@ -30,6 +30,8 @@ __global__ void __launch_bounds__(128) lora_rowproj_kernel(const __nv_bfloat16* 
                                                            const __nv_bfloat16* __restrict__ wt,
                                                            __nv_bfloat16* __restrict__ out_pad,
                                                            __nv_bfloat16* __restrict__ out_dense) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   constexpr int NT = R / 8;
   __shared__ float red[4][16][R];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -88,6 +90,8 @@ template <int R>
 __global__ void __launch_bounds__(128) lora_rowproj_split_kernel(
     const __nv_bfloat16* __restrict__ in, int64_t ld, int64_t M, int64_t D,
     const __nv_bfloat16* __restrict__ wt, float* __restrict__ partial) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   constexpr int NT = R / 8;
   __shared__ float red[4][16][R];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -133,6 +137,8 @@ __global__ void __launch_bounds__(128) lora_rowproj_split_kernel(
 __global__ void lora_rowproj_finish_kernel(const float* __restrict__ partial, int slices,
                                            int64_t M, int R, __nv_bfloat16* __restrict__ out_pad,
                                            __nv_bfloat16* __restrict__ out_dense) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   const int64_t total = M * R;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -173,6 +179,8 @@ constexpr int kCpRows = 32;  // rows per staged tile
 __global__ void __launch_bounds__(256) lora_colproj_mma_kernel(
     const __nv_bfloat16* __restrict__ p_pad, int64_t ld_p, const __nv_bfloat16* __restrict__ in,
     int64_t ld, int64_t M, int64_t D, int64_t rows_per_chunk, int R, float* __restrict__ partial) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   __shared__ __align__(128) uint8_t xs[2][kCpRows * 512];
   __shared__ __align__(128) uint8_t ps[2][kCpRows * 32];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -253,6 +261,8 @@ __global__ void __launch_bounds__(256) lora_colproj_mma_kernel(
 __global__ void lora_colproj_finish_kernel(const float* __restrict__ partial, int64_t nchunks,
                                            int R, int64_t D, float scale, float* __restrict__ res,
                                            int layout, int accumulate) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   const int64_t total = static_cast<int64_t>(R) * D;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -270,6 +280,8 @@ __global__ void lora_colproj_finish_kernel(const float* __restrict__ partial, in
 __global__ void pad_lora_weight_kernel(const float* __restrict__ in, int64_t rows, int r,
                                        float scale, int transpose_in,
                                        __nv_bfloat16* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   const int64_t total = rows * 64;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -283,6 +295,8 @@ __global__ void pad_lora_weight_kernel(const float* __restrict__ in, int64_t row
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, int64_t n,
                                    __nv_bfloat16* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x)
     out[e] = __float2bfloat16_rn(in[e]);
@@ -291,6 +305,8 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ in, int64_t n,
 // out[j][i] = bf16(in[i][j]) for in fp32 [rows, cols].
 __global__ void f32_to_bf16_t_kernel(const float* __restrict__ in, int64_t rows, int cols,
                                      __nv_bfloat16* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();  // inputs are the previous kernels' outputs
   const int64_t total = rows * cols;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -424,10 +440,10 @@ int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, con
   auto op = static_cast<__nv_bfloat16*>(out_pad);
   auto od = static_cast<__nv_bfloat16*>(out_dense);
   switch (r) {
-    case 16: lora_rowproj_kernel<16><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
-    case 32: lora_rowproj_kernel<32><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
-    case 48: lora_rowproj_kernel<48><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
-    case 64: lora_rowproj_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 16: launch_pdl(lora_rowproj_kernel<16>, dim3(grid), dim3(128), 0, st, i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 32: launch_pdl(lora_rowproj_kernel<32>, dim3(grid), dim3(128), 0, st, i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 48: launch_pdl(lora_rowproj_kernel<48>, dim3(grid), dim3(128), 0, st, i, ld_in, M, D, w, op, od); note_launch(); break;
+    case 64: launch_pdl(lora_rowproj_kernel<64>, dim3(grid), dim3(128), 0, st, i, ld_in, M, D, w, op, od); note_launch(); break;
     default: return FITQ_ERR_UNSUPPORTED;
   }
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
@@ -446,16 +462,16 @@ int launch_lora_rowproj_small(const void* in, int64_t ld_in, int64_t M, int64_t 
   auto i = static_cast<const __nv_bfloat16*>(in);
   auto w = static_cast<const __nv_bfloat16*>(wt_bf16);
   switch (r) {
-    case 16: lora_rowproj_split_kernel<16><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
-    case 32: lora_rowproj_split_kernel<32><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
-    case 48: lora_rowproj_split_kernel<48><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
-    case 64: lora_rowproj_split_kernel<64><<<grid, 128, 0, st>>>(i, ld_in, M, D, w, partial_ws); break;
+    case 16: launch_pdl(lora_rowproj_split_kernel<16>, grid, dim3(128), 0, st, i, ld_in, M, D, w, partial_ws); break;
+    case 32: launch_pdl(lora_rowproj_split_kernel<32>, grid, dim3(128), 0, st, i, ld_in, M, D, w, partial_ws); break;
+    case 48: launch_pdl(lora_rowproj_split_kernel<48>, grid, dim3(128), 0, st, i, ld_in, M, D, w, partial_ws); break;
+    case 64: launch_pdl(lora_rowproj_split_kernel<64>, grid, dim3(128), 0, st, i, ld_in, M, D, w, partial_ws); break;
     default: return FITQ_ERR_UNSUPPORTED;
   }
   note_launch();
-  lora_rowproj_finish_kernel<<<grid_for(M * r, 256, 148), 256, 0, st>>>(
-      partial_ws, static_cast<int>(slices), M, r, static_cast<__nv_bfloat16*>(out_pad),
-      static_cast<__nv_bfloat16*>(out_dense));
+  launch_pdl(lora_rowproj_finish_kernel, dim3(grid_for(M * r, 256, 148)), dim3(256), 0, st,
+             static_cast<const float*>(partial_ws), static_cast<int>(slices), M, r,
+             static_cast<__nv_bfloat16*>(out_pad), static_cast<__nv_bfloat16*>(out_dense));
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
@@ -510,34 +526,35 @@ int launch_lora_colproj(const void* p_pad, int64_t ld_p, const void* in, int64_t
   colproj_geometry(M, D, num_sms, &rpc, &nch);
   dim3 grid(static_cast<unsigned>((D + 255) / 256), static_cast<unsigned>(nch),
             static_cast<unsigned>(r / 16));
-  lora_colproj_mma_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(p_pad), ld_p,
-                                                static_cast<const __nv_bfloat16*>(in), ld_in, M, D,
-                                                rpc, r, partial_ws);
+  launch_pdl(lora_colproj_mma_kernel, dim3(grid), dim3(256), 0, st,
+             static_cast<const __nv_bfloat16*>(p_pad), ld_p, static_cast<const __nv_bfloat16*>(in),
+             ld_in, M, D, rpc, r, partial_ws);
   note_launch();
-  lora_colproj_finish_kernel<<<grid_for(static_cast<int64_t>(r) * D, 256, num_sms), 256, 0, st>>>(
-      partial_ws, nch, r, D, scale, res, layout, accumulate);
+  launch_pdl(lora_colproj_finish_kernel, dim3(grid_for(static_cast<int64_t>(r) * D, 256, num_sms)),
+             dim3(256), 0, st, static_cast<const float*>(partial_ws), nch, r, D, scale, res, layout,
+             accumulate);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, int transpose_in,
                            void* out_pad, cudaStream_t st) {
-  pad_lora_weight_kernel<<<grid_for(rows * 64, 256, 148), 256, 0, st>>>(
-      in, rows, r, scale, transpose_in, static_cast<__nv_bfloat16*>(out_pad));
+  launch_pdl(pad_lora_weight_kernel, dim3(grid_for(rows * 64, 256, 148)), dim3(256), 0, st, in, rows, r,
+             scale, transpose_in, static_cast<__nv_bfloat16*>(out_pad));
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 int launch_f32_to_bf16_t(const float* in, int64_t rows, int cols, void* out, cudaStream_t st) {
-  f32_to_bf16_t_kernel<<<grid_for(rows * cols, 256, 148), 256, 0, st>>>(
-      in, rows, cols, static_cast<__nv_bfloat16*>(out));
+  launch_pdl(f32_to_bf16_t_kernel, dim3(grid_for(rows * cols, 256, 148)), dim3(256), 0, st, in, rows,
+             cols, static_cast<__nv_bfloat16*>(out));
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }
 
 int launch_f32_to_bf16(const float* in, int64_t n, void* out, cudaStream_t st) {
-  f32_to_bf16_kernel<<<grid_for(n, 256, 148), 256, 0, st>>>(in, n,
-                                                             static_cast<__nv_bfloat16*>(out));
+  launch_pdl(f32_to_bf16_kernel, dim3(grid_for(n, 256, 148)), dim3(256), 0, st, in, n,
+             static_cast<__nv_bfloat16*>(out));
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
 }

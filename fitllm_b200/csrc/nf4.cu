@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args w, OutT* __res
                                                           int64_t n_items) {
   __shared__ float s_qm[16];
   __shared__ float s_nqm[256];
+  pdl_launch_dependents();
+  pdl_wait();  // out may still be read by the previous kernel
   if (threadIdx.x < 16) s_qm[threadIdx.x] = w.quant_map[threadIdx.x];
   if (w.nested_quant_map != nullptr) s_nqm[threadIdx.x] = w.nested_quant_map[threadIdx.x];
   __syncthreads();
@@ -88,6 +90,8 @@ template <typename OutT>
 __global__ void __launch_bounds__(256) nf4_dequant_t_kernel(Nf4Args w, OutT* __restrict__ out) {
   __shared__ float s_qm[16];
   __shared__ float s_nqm[256];
+  pdl_launch_dependents();
+  pdl_wait();  // out may still be read by the previous kernel
   // [tile of the pass][k][n], padded rows; two tiles per pass, their loads
   // issued together (one 8-byte load in flight per thread left HBM idle)
   __shared__ uint16_t s_t[2][64][64 + 8];
@@ -240,17 +244,17 @@ int launch_nf4_dequant(const Nf4Args& w, void* out, int out_dtype, int transpose
     const int64_t want = (items + 255) / 256;
     const int grid = (int)(want < (int64_t)num_sms * 8 ? want : (int64_t)num_sms * 8);
     if (out_dtype == FITQ_DTYPE_BF16)
-      nf4_dequant_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(w, (__nv_bfloat16*)out, items);
+      launch_pdl(nf4_dequant_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, w, (__nv_bfloat16*)out, items);
     else
-      nf4_dequant_kernel<__half><<<grid, 256, 0, st>>>(w, (__half*)out, items);
+      launch_pdl(nf4_dequant_kernel<__half>, dim3(grid), dim3(256), 0, st, w, (__half*)out, items);
     note_launch();
   } else {
     const int64_t tiles = (w.n_out / 64) * (w.k_in / 64);
     const int grid = (int)(tiles < (int64_t)num_sms * 8 ? tiles : (int64_t)num_sms * 8);
     if (out_dtype == FITQ_DTYPE_BF16)
-      nf4_dequant_t_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(w, (__nv_bfloat16*)out);
+      launch_pdl(nf4_dequant_t_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, w, (__nv_bfloat16*)out);
     else
-      nf4_dequant_t_kernel<__half><<<grid, 256, 0, st>>>(w, (__half*)out);
+      launch_pdl(nf4_dequant_t_kernel<__half>, dim3(grid), dim3(256), 0, st, w, (__half*)out);
     note_launch();
   }
   return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
