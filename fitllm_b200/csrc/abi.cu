@@ -439,6 +439,8 @@ static int qlora_fwd_impl(const fitq_nf4_weight* w, const void* x, int64_t m, co
     return fail(FITQ_ERR_WORKSPACE, "qlora_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
   Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
   plan_fwd(c, m, N, K, rank, sms, &p);
+  if (!c.ok())  // the size query and the call carve the same plan: never past the end
+    return fail(FITQ_ERR_WORKSPACE, "qlora_fwd: plan of %zu bytes exceeds the workspace", c.used);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   if (p.dec || p.tc) {
@@ -679,6 +681,7 @@ static int grouped_impl(const fitq_gemv_job* jobs, int count, const void* x, int
     if (jobs[g].rank > 0)
       t_part[g] = static_cast<float*>(c.take(fitq::lora_t_workspace(m, a[g].k_in, jobs[g].rank)));
   }
+  if (!c.ok()) return fail(FITQ_ERR_WORKSPACE, "%s: plan of %zu bytes exceeds the workspace", what, c.used);
   const int64_t K = a[0].k_in;
   rc = tc ? fitq::launch_nf4_gemv_tc_grouped(a, count, x, m, partial, status_ptr(), st, sms)
           : fitq::launch_nf4_gemv_dec_grouped(a, count, x, m, partial, status_ptr(), st, sms);
@@ -766,6 +769,8 @@ int fitq_qlora_bwd(const fitq_nf4_weight* w, const void* x, const void* dy, int6
     return fail(FITQ_ERR_WORKSPACE, "qlora_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
   Carve c{static_cast<uint8_t*>(workspace), workspace_bytes};
   plan_bwd(c, m, N, K, rank, need_dx, need_t, sms, &p);
+  if (!c.ok())
+    return fail(FITQ_ERR_WORKSPACE, "qlora_bwd: plan of %zu bytes exceeds the workspace", c.used);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   // The weight side of dX (s.A^T padding, transposed NF4 dequant) on the side
