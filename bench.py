@@ -50,6 +50,8 @@ def parse():
                     help="N,K,M[,R]: run one NF4 GEMV shape and exit (a profiling target)")
     ap.add_argument("--attn-case", default=None,
                     help="B,H,KVH,T,prefix: run the verify attention on one shape and exit")
+    ap.add_argument("--train-attn-case", default=None,
+                    help="B,S,H,KVH: time the causal training attention (fwd, bwd) against SDPA and exit")
     ap.add_argument("--ce-case", default=None,
                     help="rows,vocab: run the cross-entropy kernel on one shape and exit")
     ap.add_argument("--qproj-case", action="store_true",
@@ -575,6 +577,52 @@ def attn_case(dev, spec):
             "kv_GB/s": round(kv / us / 1e3, 1)}
 
 
+def train_attn_case(dev, spec):
+    """Causal GQA training attention on one shape ("B,S,H,KVH", head_dim 128):
+    fitq_attention_fwd / _bwd against torch SDPA (cuDNN) on the same bf16
+    tensors, three warm calls then 10 timed of each (CUDA events).  FLOPs in
+    the flash-attention convention: causal forward 2*B*H*S*S*D (two GEMMs over
+    half the score matrix), backward 2.5x that."""
+    import torch
+    import torch.nn.functional as F
+    from fitllm_b200.layer_ops import attention_backward, attention_forward
+    b, s, h, kvh = map(int, spec.split(","))
+    g = torch.Generator(device=dev).manual_seed(15)
+    q = torch.randn(b, s, h, 128, generator=g, device=dev).bfloat16()
+    k = torch.randn(b, s, kvh, 128, generator=g, device=dev).bfloat16()
+    v = torch.randn(b, s, kvh, 128, generator=g, device=dev).bfloat16()
+    do = torch.randn(b, s, h, 128, generator=g, device=dev).bfloat16()
+    fwd_flop = 2.0 * b * h * s * s * 128
+    res = {"train_attn_case": spec, "fwd_gflop": round(fwd_flop / 1e9, 1)}
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(10):
+            fn()
+        e_ev.record()
+        torch.cuda.synchronize()
+        return s_ev.elapsed_time(e_ev) / 10
+
+    o, lse = attention_forward(q, k, v)
+    res["fitq_fwd_ms"] = round(timed(lambda: attention_forward(q, k, v)), 4)
+    res["fitq_bwd_ms"] = round(timed(lambda: attention_backward(q, k, v, o, lse, do)), 4)
+    qt, kt, vt = (t.transpose(1, 2).detach().requires_grad_(True) for t in (q, k, v))
+    dot = do.transpose(1, 2)
+    ot = F.scaled_dot_product_attention(qt, kt, vt, is_causal=True, enable_gqa=True)
+    res["sdpa_fwd_ms"] = round(timed(lambda: F.scaled_dot_product_attention(
+        qt, kt, vt, is_causal=True, enable_gqa=True)), 4)
+    res["sdpa_bwd_ms"] = round(timed(lambda: torch.autograd.grad(ot, (qt, kt, vt), dot,
+                                                                 retain_graph=True)), 4)
+    for key in ("fitq", "sdpa"):
+        res[key + "_fwd_tflops"] = round(fwd_flop / res[key + "_fwd_ms"] / 1e9, 1)
+        res[key + "_bwd_tflops"] = round(2.5 * fwd_flop / res[key + "_bwd_ms"] / 1e9, 1)
+    return res
+
+
 def ce_case(dev, spec):
     """fitq_cross_entropy on its own ("rows,vocab"): bf16 logits, three warm
     calls then 20 timed on fresh copies (a profiling target)."""
@@ -657,7 +705,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     L = _lib.load()
-    for case, fn in ((a.gemv_case, gemv_case), (a.attn_case, attn_case), (a.ce_case, ce_case)):
+    for case, fn in ((a.gemv_case, gemv_case), (a.attn_case, attn_case), (a.ce_case, ce_case),
+                     (a.train_attn_case, train_attn_case)):
         if case:
             if rank == 0:
                 print(json.dumps(fn(dev, case)), flush=True)

@@ -86,6 +86,9 @@ SIGNATURES = {
     "fitq_cross_entropy": (I32, [P, P, I64, I64, I64, F32, P, P, SZ, P]),
     "fitq_verify_attention_workspace": (SZ, [I64, I32, I32, I32, I32]),
     "fitq_verify_attention": (I32, [P, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, SZ, P]),
+    "fitq_attention_fwd": (I32, [P, P, P, P, P, I64, I64, I32, I32, I32, P]),
+    "fitq_attention_bwd_workspace": (SZ, [I64, I64, I32]),
+    "fitq_attention_bwd": (I32, [P, P, P, P, P, P, P, P, P, I64, I64, I32, I32, I32, P, SZ, P]),
 }
 
 

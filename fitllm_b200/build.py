@@ -24,7 +24,7 @@ INCLUDE = PKG.parent / "include"
 
 SOURCES = ["nf4.cu", "gemm_sm100.cu", "lora.cu", "gemv.cu", "optim.cu", "abi.cu",
            "gemv_noalloc.cu", "layer_ops.cu", "gemm_sm100_2cta.cu", "gemv_tc.cu", "attn.cu", "ce.cu",
-           "selftest.cu", "gemm_nf4.cu", "gemm_nf4_2cta.cu", "merge.cu"]
+           "selftest.cu", "gemm_nf4.cu", "gemm_nf4_2cta.cu", "merge.cu", "train_attn.cu"]
 HEADERS = ["common.cuh", "kernels.cuh", "pair.cuh", "nf4_decode.cuh"]
 
 NVCC_FLAGS = [

@@ -1221,6 +1221,57 @@ int fitq_verify_attention(const void* q, const void* k_cache, const void* v_cach
                        "verify_attention");
 }
 
+// Shape checks shared by the training attention forward and backward.
+static int attention_shape(const char* what, int64_t batch, int64_t seq, int heads, int kv_heads,
+                           int head_dim) {
+  if (batch <= 0 || batch > 65535 || seq <= 0 || seq % 64 != 0 || seq > (1ll << 30) || heads <= 0 ||
+      heads > 65535 || kv_heads <= 0 || heads % kv_heads != 0)
+    return fail(FITQ_ERR_SHAPE, "%s: bad shape (B=%lld S=%lld H=%d KVH=%d; S %% 64 == 0, H %% KVH == 0)",
+                what, (long long)batch, (long long)seq, heads, kv_heads);
+  if (head_dim != 128) return fail(FITQ_ERR_UNSUPPORTED, "%s: needs head_dim 128 (got %d)", what, head_dim);
+  return FITQ_OK;
+}
+
+int fitq_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                       int64_t batch, int64_t seq, int heads, int kv_heads, int head_dim,
+                       fitq_stream_t stream) {
+  if (!q || !k || !v || !o || !lse) return fail(FITQ_ERR_ARG, "attention_fwd: NULL tensor");
+  int rc = attention_shape("attention_fwd", batch, seq, heads, kv_heads, head_dim);
+  if (rc) return rc;
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(o) || !al16(lse))
+    return fail(FITQ_ERR_ALIGN, "attention_fwd: 16-byte alignment");
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_train_attn_fwd(q, k, v, o, lse, batch, seq, heads, kv_heads,
+                                                   static_cast<cudaStream_t>(stream)),
+                       "attention_fwd");
+}
+
+size_t fitq_attention_bwd_workspace(int64_t batch, int64_t seq, int heads) {
+  if (batch <= 0 || seq <= 0 || heads <= 0) return 0;
+  return static_cast<size_t>(batch) * static_cast<size_t>(seq) * static_cast<size_t>(heads) * sizeof(float);
+}
+
+int fitq_attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                       const float* lse, void* dq, void* dk, void* dv, int64_t batch, int64_t seq,
+                       int heads, int kv_heads, int head_dim, void* workspace, size_t workspace_bytes,
+                       fitq_stream_t stream) {
+  if (!q || !k || !v || !o || !d_o || !lse || !dq || !dk || !dv || !workspace)
+    return fail(FITQ_ERR_ARG, "attention_bwd: NULL tensor or workspace");
+  int rc = attention_shape("attention_bwd", batch, seq, heads, kv_heads, head_dim);
+  if (rc) return rc;
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(o) || !al16(d_o) || !al16(lse) || !al16(dq) ||
+      !al16(dk) || !al16(dv) || !al16(workspace))
+    return fail(FITQ_ERR_ALIGN, "attention_bwd: 16-byte alignment");
+  const size_t need = fitq_attention_bwd_workspace(batch, seq, heads);
+  if (workspace_bytes < need)
+    return fail(FITQ_ERR_WORKSPACE, "attention_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (!current_sms(&rc)) return rc;
+  return launch_status(fitq::launch_train_attn_bwd(q, k, v, o, d_o, lse, dq, dk, dv,
+                                                   static_cast<float*>(workspace), batch, seq, heads,
+                                                   kv_heads, static_cast<cudaStream_t>(stream)),
+                       "attention_bwd");
+}
+
 int fitq_rope_append(const void* q, const void* k, const void* v, void* q_out, void* k_cache,
                      void* v_cache, const float* cos_half, const float* sin_half, int64_t batch,
                      int t_new, int heads, int kv_heads, int head_dim, int prefix, int capacity,

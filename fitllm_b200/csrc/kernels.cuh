@@ -241,6 +241,14 @@ int launch_cross_entropy(void* logits, const int64_t* labels, int64_t T, int64_t
 
 // Speculative-verify attention over a KV cache (attn.cu): q, out [B, T, H, 128],
 // caches [B, KVH, cap, 128] bf16, (H / KVH) * T <= 32, prefix + T <= cap.
+// Causal GQA attention of the training layer (train_attn.cu); shapes checked
+// by the caller: head_dim 128, seq % 64 == 0, heads % kv_heads == 0.
+int launch_train_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+                          int64_t batch, int64_t seq, int heads, int kv_heads, cudaStream_t st);
+int launch_train_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                          const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                          float* delta, int64_t batch, int64_t seq, int heads, int kv_heads,
+                          cudaStream_t st);
 size_t verify_attention_workspace(int64_t batch, int kv_heads, int len, int num_sms);
 int launch_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
                             int64_t batch, int heads, int kv_heads, int t_new, int prefix, int cap,

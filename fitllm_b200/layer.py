@@ -26,7 +26,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .layer_ops import rms_norm, rope, swiglu
+from .layer_ops import attention, rms_norm, rope, swiglu
 from .qlora import Linear4bit, QLoRALinear4bit
 
 
@@ -122,10 +122,20 @@ class Attention(nn.Module):
         self.k_proj = Linear4bit(h, kvd, bias=True, device=device)
         self.v_proj = Linear4bit(h, kvd, bias=True, device=device)
         self.o_proj = Linear4bit(qd, h, bias=False, device=device)
+        # FITQ_ATTN=1: this library's causal GQA attention kernels (fwd + bwd,
+        # [B, S, heads, 128] in place, no transposes) instead of torch SDPA.
+        self.own_kernel = os.environ.get("FITQ_ATTN", "0") == "1"
 
     def forward(self, x, residual, cos, sin, attn_mask: Optional[torch.Tensor] = None):
         cfg = self.cfg
         b, s, _ = x.shape
+        if (self.own_kernel and attn_mask is None and x.is_cuda and cfg.head_dim == 128
+                and s % 64 == 0):
+            q = rope(self.q_proj(x), cos, sin, cfg.heads).view(b, s, cfg.heads, cfg.head_dim)
+            k = rope(self.k_proj(x), cos, sin, cfg.kv_heads).view(b, s, cfg.kv_heads, cfg.head_dim)
+            v = self.v_proj(x).view(b, s, cfg.kv_heads, cfg.head_dim)
+            o = attention(q, k, v).view(b, s, cfg.heads * cfg.head_dim)
+            return self.o_proj(o, residual=residual)
         q = rope(self.q_proj(x), cos, sin, cfg.heads).view(b, s, cfg.heads, cfg.head_dim).transpose(1, 2)
         k = rope(self.k_proj(x), cos, sin, cfg.kv_heads).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
         v = self.v_proj(x).view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)

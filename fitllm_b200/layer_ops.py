@@ -146,3 +146,56 @@ def swiglu_backward(d, gate, up):
 
 def swiglu(gate, up):
     return SwiGLUFn.apply(gate, up)
+
+
+def attention_forward(q, k, v):
+    """Causal GQA attention (fitq_attention_fwd).  q [B, S, H, 128], k/v
+    [B, S, KVH, 128] bf16 contiguous; returns (o [B, S, H, 128] bf16, lse
+    [B, H, S] fp32, base 2)."""
+    b, s, h, d = q.shape
+    kvh = k.shape[2]
+    o = torch.empty_like(q)
+    lse = torch.empty(b, h, s, dtype=torch.float32, device=q.device)
+    L = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(L.fitq_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                        lse.data_ptr(), b, s, h, kvh, d, _st(q)), "fitq_attention_fwd")
+    return o, lse
+
+
+def attention_backward(q, k, v, o, lse, d_o):
+    """(dq, dk, dv) of attention_forward for upstream d_o [B, S, H, 128] (fitq_attention_bwd)."""
+    b, s, h, d = q.shape
+    kvh = k.shape[2]
+    d_o = _c(d_o.to(q.dtype))
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    L = _lib.load()
+    with torch.cuda.device(q.device):
+        nbytes = L.fitq_attention_bwd_workspace(b, s, h)
+        ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=q.device)
+        _lib.check(L.fitq_attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                        d_o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                        dv.data_ptr(), b, s, h, kvh, d, ws.data_ptr(), nbytes, _st(q)),
+                   "fitq_attention_bwd")
+    return dq, dk, dv
+
+
+class AttentionFn(torch.autograd.Function):
+    """softmax(q k^T / sqrt(128) + causal mask) v over [B, S, heads, 128]
+    tensors, the KV heads shared by heads / kv_heads query heads each."""
+
+    @staticmethod
+    def forward(ctx, q, k, v):
+        q, k, v = _c(q), _c(k), _c(v)
+        o, lse = attention_forward(q, k, v)
+        ctx.save_for_backward(q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, d_o):
+        q, k, v, o, lse = ctx.saved_tensors
+        return attention_backward(q, k, v, o, lse, d_o)
+
+
+def attention(q, k, v):
+    return AttentionFn.apply(q, k, v)

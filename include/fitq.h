@@ -296,6 +296,33 @@ FITQ_API int fitq_verify_attention(const void* q, const void* k_cache, const voi
                                    void* out, int64_t batch, int heads, int kv_heads, int t_new,
                                    int prefix, int capacity, int head_dim, void* workspace,
                                    size_t workspace_bytes, fitq_stream_t stream);
+
+/* Causal grouped-query attention of the training layer, forward and
+ * backward.  Replaces the attention of the Qwen2 decoder layer FitLLM runs in
+ * the shard-stationary forward and in the backward's recompute (HF layer via
+ * fitllm/forward.py:657-701, fitllm/backward.py:222-231):
+ * O = softmax(Q K^T / sqrt(head_dim) + causal mask) V, query head h reading
+ * KV head h / (heads / kv_heads).
+ *   q, o, d_o, dq: [batch, seq, heads, head_dim] bf16 (the q_proj output /
+ *                  o_proj input, row-major, no transposes);
+ *   k, v, dk, dv:  [batch, seq, kv_heads, head_dim] bf16;
+ *   lse:           [batch, heads, seq] fp32, written by the forward and read
+ *                  by the backward (the row's log-sum-exp of the scaled
+ *                  scores, in base-2 units);
+ *   workspace:     fitq_attention_bwd_workspace bytes (fp32 row sums of
+ *                  dO . O).
+ * fp32 softmax and accumulation; P and dS enter the tensor cores as bf16.
+ * The backward is deterministic (no atomics).  Needs head_dim == 128
+ * (FITQ_ERR_UNSUPPORTED otherwise), seq % 64 == 0 and heads % kv_heads == 0
+ * (FITQ_ERR_SHAPE), 16-byte aligned pointers (FITQ_ERR_ALIGN). */
+FITQ_API int fitq_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                                int64_t batch, int64_t seq, int heads, int kv_heads, int head_dim,
+                                fitq_stream_t stream);
+FITQ_API size_t fitq_attention_bwd_workspace(int64_t batch, int64_t seq, int heads);
+FITQ_API int fitq_attention_bwd(const void* q, const void* k, const void* v, const void* o,
+                                const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                                int64_t batch, int64_t seq, int heads, int kv_heads, int head_dim,
+                                void* workspace, size_t workspace_bytes, fitq_stream_t stream);
 FITQ_API int fitq_swiglu_bwd(const void* d_act, const void* gate, const void* up, void* d_gate,
                              void* d_up, int64_t n, fitq_stream_t stream);
 
