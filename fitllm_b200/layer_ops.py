@@ -148,10 +148,25 @@ def swiglu(gate, up):
     return SwiGLUFn.apply(gate, up)
 
 
+def _check_attention_inputs(q, k, v):
+    # the C ABI sees plain pointers: dtype, layout and device are checked here
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("attention: q, k, v must be [B, S, heads, head_dim]")
+    if k.shape != v.shape or k.shape[:2] != q.shape[:2] or k.shape[3] != q.shape[3]:
+        raise ValueError(f"attention: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} "
+                         "do not match")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"attention: {name} must be a contiguous bf16 CUDA tensor")
+        if t.device != q.device:
+            raise ValueError("attention: q, k, v must be on one device")
+
+
 def attention_forward(q, k, v):
     """Causal GQA attention (fitq_attention_fwd).  q [B, S, H, 128], k/v
     [B, S, KVH, 128] bf16 contiguous; returns (o [B, S, H, 128] bf16, lse
     [B, H, S] fp32, base 2)."""
+    _check_attention_inputs(q, k, v)
     b, s, h, d = q.shape
     kvh = k.shape[2]
     o = torch.empty_like(q)
@@ -165,9 +180,13 @@ def attention_forward(q, k, v):
 
 def attention_backward(q, k, v, o, lse, d_o):
     """(dq, dk, dv) of attention_forward for upstream d_o [B, S, H, 128] (fitq_attention_bwd)."""
+    _check_attention_inputs(q, k, v)
+    if o.shape != q.shape or d_o.shape != q.shape or lse.shape != (q.shape[0], q.shape[2], q.shape[1]):
+        raise ValueError("attention_backward: o / d_o must be shaped like q and lse [B, H, S]")
     b, s, h, d = q.shape
     kvh = k.shape[2]
     d_o = _c(d_o.to(q.dtype))
+    o, lse = _c(o), _c(lse.float())
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     L = _lib.load()
     with torch.cuda.device(q.device):

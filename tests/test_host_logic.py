@@ -388,3 +388,22 @@ def test_failed_rank_ends_collectives_with_an_error(mode):
     assert res[0][1] < 60.0, res
     if mode == "raise":
         assert res[1][0] == "RuntimeError"
+
+
+def test_attention_wrapper_rejects_bad_tensors_before_the_library():
+    """The training attention's Python wrappers check dtype, layout and shapes
+    themselves (the C ABI only sees pointers); every case raises before any
+    device work, so this runs without a GPU."""
+    import pytest
+    import torch
+    from fitllm_b200.layer_ops import attention_backward, attention_forward
+    q = torch.zeros(1, 64, 4, 128, dtype=torch.bfloat16)
+    k = torch.zeros(1, 64, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        attention_forward(q, k, k)                      # CPU tensors
+    with pytest.raises(ValueError, match="match"):
+        attention_forward(q, k[:, :32], k)              # S mismatch
+    with pytest.raises(ValueError, match="head_dim"):
+        attention_forward(q[0], k, k)                   # not 4-D
+    with pytest.raises(ValueError, match="CUDA"):
+        attention_backward(q.float(), k, k, q, torch.zeros(1, 4, 64), q)
