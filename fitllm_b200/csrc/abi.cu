@@ -183,9 +183,16 @@ inline size_t bf16_bytes(int64_t n) { return static_cast<size_t>(n) * 2; }
 
 bool valid_rank(int r) { return r == 0 || r == 16 || r == 32 || r == 48 || r == 64; }
 
+thread_local cudaError_t g_launch_error = cudaSuccess;
+
 int launch_status(int rc, const char* what) {
-  if (rc == FITQ_OK) return FITQ_OK;
+  if (rc == FITQ_OK) {
+    g_launch_error = cudaSuccess;
+    return FITQ_OK;
+  }
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = g_launch_error;  // a launcher's launch_result() read it already
+  g_launch_error = cudaSuccess;
   return fail(rc, "%s: launch failed (%s)", what, cudaGetErrorString(e));
 }
 
@@ -1115,6 +1122,12 @@ extern "C" long long fitq_launch_count(void) { return g_launches.load(); }
 namespace fitq {
 // Lets entry points defined in other files report through fitq_last_error().
 void set_last_error(const char* msg) { g_last_error = msg; }
+int launch_result() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return FITQ_OK;
+  g_launch_error = e;
+  return FITQ_ERR_CUDA;
+}
 }  // namespace fitq
 
 // ---------------------------------------------------------------- layer kernels

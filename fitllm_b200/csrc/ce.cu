@@ -172,7 +172,7 @@ int launch_cross_entropy(void* logits, const int64_t* labels, int64_t T, int64_t
   note_launch();
   ce_finish_kernel<<<1, 1024, 0, st>>>(loss_rows, T, n_valid, loss_out);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

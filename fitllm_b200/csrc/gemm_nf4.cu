@@ -532,7 +532,7 @@ int launch_gemm_nf4(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
   launch_pdl(gemm_nf4_kernel, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, st, ta, tp, tpa, tpb, p);
   note_launch();
   timing_end(slot, st);
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

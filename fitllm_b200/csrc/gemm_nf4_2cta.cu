@@ -570,7 +570,7 @@ int launch_gemm_nf4_2cta(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
                tpb, p);
   note_launch();
   timing_end(slot, st);
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

@@ -395,7 +395,7 @@ int launch_gemm_bf16_tn_bn(const GemmArgs& g, cudaStream_t st, int num_sms) {
   launch_pdl(gemm_bf16_tn_kernel<BN>, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, st, ta, tb, tpa, tpb, p);
   note_launch();
   timing_end(slot, st);
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_gemm(const GemmArgs& g, cudaStream_t st, int num_sms) {

@@ -494,7 +494,7 @@ int launch_gemm_bf16_tn_2cta_bn(const GemmArgs& g, cudaStream_t st, int num_sms)
              tb2, p);
   note_launch();
   timing_end(slot, st);
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

@@ -1107,7 +1107,7 @@ int launch_nf4_gemv_core(const Nf4Args& w, const void* x, int64_t m, float* part
 #undef FITQ_GEMV_CASE
   if (e != cudaSuccess) return FITQ_ERR_CUDA;
   *splits_out = static_cast<int>(p.slices);
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, const void* t_pad,
@@ -1122,7 +1122,7 @@ int launch_gemv_finish(const float* partial, int splits, int64_t m, int64_t n, c
       rank, scale, static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(y_add),
       static_cast<__nv_bfloat16*>(y));
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

@@ -288,6 +288,10 @@ int launch_selftest_wait(uint64_t limit_ns, unsigned long long* elapsed_ns, int*
                          cudaStream_t st);
 // Sets the text returned by fitq_last_error() for the calling thread.
 void set_last_error(const char* msg);
+// Status of the launches just issued: FITQ_OK, or FITQ_ERR_CUDA with the CUDA
+// error kept for the calling thread, so that the message the entry point
+// writes names it (reading cudaGetLastError() clears it).
+int launch_result();
 // fitq_nf4_gemv with the given scratch in place of a caller workspace (abi.cu).
 int nf4_gemv_on_scratch(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
                         const float* lora_b, int rank, float scale, const void* bias, void* y,

@@ -280,7 +280,7 @@ int launch_rmsnorm_bwd(const void* dy, const void* x, const void* w, void* dx, i
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
       static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(dx), cols, eps);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_rope(const void* t, void* out, const float* cs, const float* sn, int64_t rows,
@@ -295,7 +295,7 @@ int launch_rope(const void* t, void* out, const float* cs, const float* sn, int6
         static_cast<const __nv_bfloat16*>(t), static_cast<__nv_bfloat16*>(out), cs, sn, rows,
         heads, dim, seq);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_rope_append(const void* q, const void* k, const void* v, void* q_out, void* k_cache,
@@ -311,7 +311,7 @@ int launch_rope_append(const void* q, const void* k, const void* v, void* q_out,
       static_cast<__nv_bfloat16*>(v_cache), cs, sn, rows, t_new, heads, kv_heads, dim, prefix, cap);
   note_launch();
   if (e != cudaSuccess) return FITQ_ERR_CUDA;
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_swiglu_fwd(const void* g, const void* u, void* act, int64_t n, cudaStream_t st,
@@ -320,7 +320,7 @@ int launch_swiglu_fwd(const void* g, const void* u, void* act, int64_t n, cudaSt
       static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(u),
       static_cast<__nv_bfloat16*>(act), n / 8);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_swiglu_bwd(const void* d, const void* g, const void* u, void* dg, void* du, int64_t n,
@@ -330,7 +330,7 @@ int launch_swiglu_bwd(const void* d, const void* g, const void* u, void* dg, voi
       static_cast<const __nv_bfloat16*>(u), static_cast<__nv_bfloat16*>(dg),
       static_cast<__nv_bfloat16*>(du), n / 8);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

@@ -446,7 +446,7 @@ int launch_lora_rowproj(const void* in, int64_t ld_in, int64_t M, int64_t D, con
     case 64: launch_pdl(lora_rowproj_kernel<64>, dim3(grid), dim3(128), 0, st, i, ld_in, M, D, w, op, od); note_launch(); break;
     default: return FITQ_ERR_UNSUPPORTED;
   }
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 size_t lora_rowproj_small_workspace(int64_t M, int64_t D, int r) {
@@ -473,7 +473,7 @@ int launch_lora_rowproj_small(const void* in, int64_t ld_in, int64_t M, int64_t 
              static_cast<const float*>(partial_ws), static_cast<int>(slices), M, r,
              static_cast<__nv_bfloat16*>(out_pad), static_cast<__nv_bfloat16*>(out_dense));
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 size_t lora_t_workspace(int64_t M, int64_t K, int r) {
@@ -534,7 +534,7 @@ int launch_lora_colproj(const void* p_pad, int64_t ld_p, const void* in, int64_t
              dim3(256), 0, st, static_cast<const float*>(partial_ws), nch, r, D, scale, res, layout,
              accumulate);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, int transpose_in,
@@ -542,21 +542,21 @@ int launch_pad_lora_weight(const float* in, int64_t rows, int r, float scale, in
   launch_pdl(pad_lora_weight_kernel, dim3(grid_for(rows * 64, 256, 148)), dim3(256), 0, st, in, rows, r,
              scale, transpose_in, static_cast<__nv_bfloat16*>(out_pad));
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_f32_to_bf16_t(const float* in, int64_t rows, int cols, void* out, cudaStream_t st) {
   launch_pdl(f32_to_bf16_t_kernel, dim3(grid_for(rows * cols, 256, 148)), dim3(256), 0, st, in, rows,
              cols, static_cast<__nv_bfloat16*>(out));
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_f32_to_bf16(const float* in, int64_t n, void* out, cudaStream_t st) {
   launch_pdl(f32_to_bf16_kernel, dim3(grid_for(n, 256, 148)), dim3(256), 0, st, in, n,
              static_cast<__nv_bfloat16*>(out));
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

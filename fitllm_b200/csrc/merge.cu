@@ -116,7 +116,7 @@ int launch_lora_merge(void* w, int out_dtype, int64_t n, int64_t k, const float*
     lora_merge_kernel<float><<<grid, kMergeThreads, smem, st>>>(static_cast<float*>(w), N, K, a, b,
                                                                  rank, scale);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

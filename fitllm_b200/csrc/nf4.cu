@@ -257,7 +257,7 @@ int launch_nf4_dequant(const Nf4Args& w, void* out, int out_dtype, int transpose
       launch_pdl(nf4_dequant_t_kernel<__half>, dim3(grid), dim3(256), 0, st, w, (__half*)out);
     note_launch();
   }
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 int launch_nf4_quantize(const float* wt, int64_t n, const float* qmap, const float* nqmap,
@@ -278,7 +278,7 @@ int launch_nf4_quantize(const float* wt, int64_t n, const float* qmap, const flo
   const int64_t nn = (nb + 255) / 256;
   dq_quant_kernel<<<(int)nn, 256, 0, st>>>(absmax_ws, nb, nqmap, offset_out, codes, nested_absmax);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

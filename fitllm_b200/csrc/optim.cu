@@ -81,7 +81,7 @@ int launch_adamw(float* p, const float* g, float* m, float* v, int64_t n, float 
                                                          eps, wd, static_cast<float>(bc1),
                                                          static_cast<float>(bc2), clip);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 size_t grad_norm_workspace(int64_t n) {
@@ -99,7 +99,7 @@ int launch_grad_clip(const float* g, int64_t n, float max_norm, float* norm_out,
   }
   clip_finish_kernel<<<1, 32, 0, st>>>(partial, parts, max_norm, norm_out);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq

@@ -33,7 +33,7 @@ int launch_selftest_wait(uint64_t limit_ns, unsigned long long* elapsed_ns, int*
                          cudaStream_t st) {
   selftest_wait_kernel<<<1, 32, 0, st>>>(status, limit_ns, elapsed_ns);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? FITQ_OK : FITQ_ERR_CUDA;
+  return launch_result();
 }
 
 }  // namespace fitq
