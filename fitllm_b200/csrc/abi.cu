@@ -184,16 +184,21 @@ inline size_t bf16_bytes(int64_t n) { return static_cast<size_t>(n) * 2; }
 bool valid_rank(int r) { return r == 0 || r == 16 || r == 32 || r == 48 || r == 64; }
 
 thread_local cudaError_t g_launch_error = cudaSuccess;
+thread_local std::string g_launch_detail;
 
 int launch_status(int rc, const char* what) {
   if (rc == FITQ_OK) {
     g_launch_error = cudaSuccess;
+    g_launch_detail.clear();
     return FITQ_OK;
   }
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = g_launch_error;  // a launcher's launch_result() read it already
   g_launch_error = cudaSuccess;
-  return fail(rc, "%s: launch failed (%s)", what, cudaGetErrorString(e));
+  const std::string detail = g_launch_detail;
+  g_launch_detail.clear();
+  return fail(rc, "%s: launch failed (%s)%s%s", what, cudaGetErrorString(e), detail.empty() ? "" : "; ",
+              detail.c_str());
 }
 
 // NF4 dequant fused into the GEMM (gemm_nf4.cu, gemm_nf4_2cta.cu) or the
@@ -1122,6 +1127,7 @@ extern "C" long long fitq_launch_count(void) { return g_launches.load(); }
 namespace fitq {
 // Lets entry points defined in other files report through fitq_last_error().
 void set_last_error(const char* msg) { g_last_error = msg; }
+void note_launch_detail(const char* msg) { g_launch_detail = msg; }
 int launch_result() {
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return FITQ_OK;

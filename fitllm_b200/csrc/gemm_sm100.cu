@@ -14,6 +14,8 @@
 // Every mbarrier wait is bounded (common.cuh); no TMA multicast is used.
 #include <cstdlib>
 
+#include <cstdio>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -298,6 +300,10 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_ERROR_INVALID_CONTEXT && bind_primary_context())
+    r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -312,9 +318,22 @@ bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base,
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1u, 1u};
-  return fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
+  CUresult r = fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_ERROR_INVALID_CONTEXT && bind_primary_context())
+    r = fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "cuTensorMapEncodeTiled = %d (dtype %d, base %p, dims %llu x %llu, row %llu B, box %u x %u, "
+             "swizzle %d, l2 %d)",
+             static_cast<int>(r), static_cast<int>(dtype), base, static_cast<unsigned long long>(inner),
+             static_cast<unsigned long long>(outer), static_cast<unsigned long long>(row_bytes), box_inner,
+             box_outer, static_cast<int>(swizzle), static_cast<int>(l2));
+    note_launch_detail(msg);
+  }
+  return r == CUDA_SUCCESS;
 }
 
 // Tile width: 256 unless a narrower one finishes the grid in less tile time

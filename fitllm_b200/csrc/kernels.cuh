@@ -292,6 +292,20 @@ void set_last_error(const char* msg);
 // error kept for the calling thread, so that the message the entry point
 // writes names it (reading cudaGetLastError() clears it).
 int launch_result();
+// Makes the primary context of the runtime's current device current on the
+// calling host thread.  A thread that has not yet made a CUDA runtime call
+// that binds one (PyTorch's autograd worker for device 0, a foreign caller's
+// own thread) has no current context; launches through the runtime bind it
+// themselves, but driver calls such as cuTensorMapEncodeTiled then fail with
+// CUDA_ERROR_INVALID_CONTEXT.  The tensor-map encoders call this on that error
+// and retry once.
+inline bool bind_primary_context() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess;
+}
+// Extra text for the next failure message of the calling thread (what a
+// launcher's host-side set-up rejected, e.g. a tensor map the driver refused).
+void note_launch_detail(const char* msg);
 // fitq_nf4_gemv with the given scratch in place of a caller workspace (abi.cu).
 int nf4_gemv_on_scratch(const fitq_nf4_weight* w, const void* x, int64_t m, const float* lora_a,
                         const float* lora_b, int rank, float scale, const void* bias, void* y,
