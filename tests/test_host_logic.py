@@ -34,6 +34,27 @@ def test_library_loads_and_exports_header_symbols():
     assert _lib.version().startswith("fitq")
 
 
+def test_attention_abi_checks_arguments_before_the_device():
+    """The training attention's shape, head_dim and alignment checks run on
+    the host before any CUDA call (pointers are never dereferenced there), so
+    they answer without a GPU.  Every call here is refused before launch, so
+    the stand-in pointers are safe on a machine with a GPU too."""
+    from fitllm_b200 import _lib
+    L = _lib.load()
+    p = 1 << 20  # a 16-byte-aligned stand-in address, never touched
+    assert L.fitq_attention_fwd(None, p, p, p, p, 1, 128, 4, 2, 128, None) == 1      # NULL
+    assert L.fitq_attention_fwd(p, p, p, p, p, 1, 100, 4, 2, 128, None) == 2         # S % 64
+    assert L.fitq_attention_fwd(p, p, p, p, p, 1, 128, 6, 4, 128, None) == 2         # H % KVH
+    assert L.fitq_attention_fwd(p, p, p, p, p, 0, 128, 4, 2, 128, None) == 2         # batch
+    assert L.fitq_attention_fwd(p, p, p, p, p, 1, 128, 4, 2, 96, None) == 4          # head_dim
+    assert L.fitq_attention_fwd(p + 8, p, p, p, p, 1, 128, 4, 2, 128, None) == 3     # alignment
+    assert b"16-byte" in L.fitq_last_error()
+    ws = L.fitq_attention_bwd_workspace(2, 256, 40)
+    assert ws == 2 * 256 * 40 * 4 and L.fitq_attention_bwd_workspace(0, 256, 40) == 0
+    assert L.fitq_attention_bwd(p, p, p, p, p, p, p, p, p, 2, 256, 40, 8, 128, p, ws - 1, None) == 5
+    assert b"workspace" in L.fitq_last_error()
+
+
 def test_abi_rejects_bad_arguments_without_a_device():
     from fitllm_b200 import _lib
     L = _lib.load()
