@@ -454,7 +454,6 @@ bool make_tmap_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
-constexpr int kMaxDev = 64;
 
 }  // namespace
 
@@ -514,16 +513,7 @@ int launch_gemm_nf4(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
     p.group_m = gm ? atoi(gm) : GROUP_M;
     if (p.group_m < 1) p.group_m = GROUP_M;
   }
-  static bool attr_set[kMaxDev] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDev) return FITQ_ERR_NO_DEVICE;
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_nf4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMEM_BYTES)) != cudaSuccess)
-      return FITQ_ERR_CUDA;
-    attr_set[dev] = true;
-  }
+  if (!set_smem_limit(gemm_nf4_kernel, static_cast<int>(SMEM_BYTES))) return FITQ_ERR_CUDA;
   const int tiles = p.num_m * p.num_n;
   const int grid = tiles < num_sms ? tiles : num_sms;
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(n) *

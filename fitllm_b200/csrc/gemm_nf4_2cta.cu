@@ -477,7 +477,6 @@ bool make_tmap_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
-constexpr int kMaxDev = 64;
 
 // 512-row tiles when there are enough of them to occupy the pairs (half the
 // decode work per FLOP, epilogue not overlapped); FITQ_NF4_MSUB=1|2 forces one.
@@ -544,19 +543,10 @@ int launch_gemm_nf4_2cta(const Nf4GemmArgs& g, cudaStream_t st, int num_sms) {
     p.group_m = gm ? atoi(gm) : (p.num_n >= 16 ? 2 * GROUP_M : GROUP_M);
     if (p.group_m < 1) p.group_m = GROUP_M;
   }
-  static bool attr_set[kMaxDev][2] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDev) return FITQ_ERR_NO_DEVICE;
-  if (!attr_set[dev][msub - 1]) {
-    const cudaError_t e =
-        msub == 1 ? cudaFuncSetAttribute(gemm_nf4_2cta_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(Cfg<1>::SMEM))
-                  : cudaFuncSetAttribute(gemm_nf4_2cta_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(Cfg<2>::SMEM));
-    if (e != cudaSuccess) return FITQ_ERR_CUDA;
-    attr_set[dev][msub - 1] = true;
-  }
+  // once per (device, kernel), under the helper's lock
+  if (!(msub == 1 ? set_smem_limit(gemm_nf4_2cta_kernel<1>, static_cast<int>(Cfg<1>::SMEM))
+                  : set_smem_limit(gemm_nf4_2cta_kernel<2>, static_cast<int>(Cfg<2>::SMEM))))
+    return FITQ_ERR_CUDA;
   const int tiles = p.num_m * p.num_n;
   const int clusters = tiles < num_sms / 2 ? tiles : num_sms / 2;
   const double flops = 2.0 * static_cast<double>(g.m) * static_cast<double>(n) *
